@@ -1,0 +1,394 @@
+#!/usr/bin/env python3
+"""Tree-verification hot-path benchmark (tree tokens/s and effective KV GB/s).
+
+One step = one verify pass of the serving-mix configuration over HBM-resident inputs:
+tree-node K/V scatter into scratch slots, packed GQA tree attention, accepted-only KV
+commit.  At N GPUs the global batch has N x 64 requests and every GPU owns 8/N of the
+8 KV heads of every request (KV-head sharding: per-GPU work is fixed, scaling "weak";
+there is no collective on the data path, only the timing max-reduction).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+Rank 0 prints one JSON line.  ``--impl reference`` times the reference's CPU path (the
+oracle port of its masked-SDPA attention) on the host cores for the same workload.
+"""
+from __future__ import annotations
+
+import argparse
+from datetime import timedelta
+import json
+import os
+from pathlib import Path
+import statistics
+import sys
+import threading
+import time
+
+import numpy as np
+import torch
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+import __graft_entry__  # noqa: E402
+
+jb = __graft_entry__.load_package()
+from jetspec_b200 import workloads  # noqa: E402
+from jetspec_b200.sharding import shard_for_rank  # noqa: E402
+
+METRIC = "tree tokens/s (serving-mix tree verification: KV store + GQA tree attention + commit)"
+UNIT = "tree tokens/s"
+KV_HEADS, GROUPS, HEAD_DIM, BLOCK = 8, 4, 128, 256
+PEAKS_FALLBACK = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0}
+
+
+def parse():
+    parser = argparse.ArgumentParser(description=__doc__)
+    parser.add_argument("--gpus", type=int, default=1)
+    parser.add_argument("--steps", type=int, default=200)
+    parser.add_argument("--warmup", type=int, default=10)
+    parser.add_argument("--impl", choices=("ours", "reference"), default="ours")
+    parser.add_argument("--requests-per-gpu", type=int, default=64)
+    parser.add_argument("--no-cpu-baseline", action="store_true")
+    parser.add_argument("--cpu-seconds", type=float, default=12.0,
+                        help="CPU-baseline sample budget (seconds of oracle work)")
+    return parser.parse_args()
+
+
+def peaks():
+    path = ROOT / "MEASURED_PEAKS.json"
+    if path.exists():
+        data = json.loads(path.read_text())
+        return {"hbm_gbs": float(data["hbm_gbs"]), "bf16_tflops": float(data["bf16_tflops"]),
+                "source": "measured"}
+    return dict(PEAKS_FALLBACK, source="fallback")
+
+
+def global_batch(world: int, requests_per_gpu: int):
+    """config3 statistics with world x requests_per_gpu requests (one seed per rank block)."""
+    return workloads.config3(seed=1003, num_requests=requests_per_gpu * world)
+
+
+# ---- clocks ---------------------------------------------------------------------------
+class ClockSampler:
+    """NVML sampling of SM clock and throttle reasons on a background thread (read-only)."""
+
+    REASONS = {0x1: "gpu_idle", 0x2: "applications_clocks_setting", 0x4: "sw_power_cap",
+               0x8: "hw_slowdown", 0x10: "sync_boost", 0x20: "sw_thermal_slowdown",
+               0x40: "hw_thermal_slowdown", 0x80: "hw_power_brake_slowdown",
+               0x100: "display_clock_setting"}
+
+    def __init__(self, index: int, period: float = 0.01):
+        self.samples, self.reasons, self.ok = [], 0, False
+        self.max_mhz = None
+        self._stop = threading.Event()
+        try:
+            import pynvml
+            pynvml.nvmlInit()
+            self._nvml = pynvml
+            self._handle = pynvml.nvmlDeviceGetHandleByIndex(index)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self._handle, pynvml.NVML_CLOCK_SM)
+            self.ok = True
+        except Exception:  # noqa: BLE001 - clocks are best effort; reported as missing
+            self.ok = False
+        self._period = period
+        self._thread = threading.Thread(target=self._run, daemon=True)
+
+    def _run(self):
+        nv = self._nvml
+        while not self._stop.is_set():
+            try:
+                self.samples.append(nv.nvmlDeviceGetClockInfo(self._handle, nv.NVML_CLOCK_SM))
+                self.reasons |= int(nv.nvmlDeviceGetCurrentClocksEventReasons(self._handle))
+            except Exception:  # noqa: BLE001
+                pass
+            time.sleep(self._period)
+
+    def __enter__(self):
+        if self.ok:
+            self._thread.start()
+        return self
+
+    def __exit__(self, *exc):
+        self._stop.set()
+        if self.ok:
+            self._thread.join()
+
+    def report(self):
+        if not self.ok or not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": self.max_mhz, "reasons": ["unavailable"]}
+        names = [name for bit, name in self.REASONS.items() if self.reasons & bit]
+        return {"sm_mhz": statistics.median(self.samples), "sm_max_mhz": self.max_mhz,
+                "reasons": names, "samples": len(self.samples)}
+
+
+# ---- CPU side -------------------------------------------------------------------------
+def cpu_oracle_rate(batch, budget_s: float, seed: int = 5):
+    """Reference CPU path (fp32 masked SDPA, all host threads) on a strided request sample.
+
+    Returns (tree tokens/s, sample description, threads).  Inputs are generated on the
+    host with the workload's shapes; only the sampled requests' rows are materialised.
+    """
+    from oracle import tree_attention as attn_oracle
+
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    gen = torch.Generator().manual_seed(seed)
+    std = batch.head_dim ** -0.5
+    order = list(range(0, batch.num_requests, 8)) + [r for r in range(batch.num_requests) if r % 8]
+    done, tokens, keys, elapsed = [], 0, 0, 0.0
+    for r in order:
+        prefix, nodes = batch.prefix_lens[r], len(batch.parents[r])
+        q = (torch.randn((nodes, batch.num_query_heads, batch.head_dim), generator=gen) * std).bfloat16()
+        rows = prefix + nodes
+        k = (torch.randn((1, rows, batch.num_kv_heads, batch.head_dim), generator=gen) * std).bfloat16()
+        v = (torch.randn((1, rows, batch.num_kv_heads, batch.head_dim), generator=gen) * std).bfloat16()
+        # A request-local pool: prefix at positions 0..P-1 of one page-table-free page.
+        t0 = time.perf_counter()
+        attn_oracle.masked_sdpa(q, k, v, [prefix], [[0] if prefix else []],
+                                [list(range(prefix, rows))], [batch.parents[r]],
+                                batch.head_dim ** -0.5, batch.groups)
+        elapsed += time.perf_counter() - t0
+        done.append(r)
+        tokens += nodes
+        keys += rows
+        if elapsed >= budget_s:
+            break
+    sample = (f"{len(done)} of {batch.num_requests} requests (every 8th first), "
+              f"{tokens} tree tokens, {keys} keys x {batch.num_kv_heads} KV heads, fp32 masked SDPA")
+    return tokens / elapsed, sample, threads
+
+
+def run_reference(args, rank: int, world: int):
+    if rank != 0:
+        return
+    batch = global_batch(world, args.requests_per_gpu)
+    steps, warmup = max(args.steps, 1), max(args.warmup, 0)
+    budget = max(0.5, min(20.0, 150.0 / (steps + warmup)))
+    rates = []
+    sample = threads = None
+    for i in range(warmup + steps):
+        rate, sample, threads = cpu_oracle_rate(batch, budget, seed=7 + i)
+        if i >= warmup:
+            rates.append(rate)
+    value = statistics.median(rates)
+    line = {"metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": steps,
+            "warmup": warmup, "ms_per_step": None, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "f32 (bf16 operands)", "data": "synthetic",
+            "impl": "reference",
+            "config": {"workload": f"config3 serving mix, {batch.num_requests} requests",
+                       "kv_heads_per_gpu": KV_HEADS // world},
+            "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": "port",
+                             "sample": f"per step: {sample}"},
+            "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+# ---- GPU side -------------------------------------------------------------------------
+class Step:
+    """Device-resident inputs of one verify step on this rank's KV-head shard."""
+
+    def __init__(self, batch, shard, device):
+        self.batch, self.shard, self.device = batch, shard, device
+        heads = shard.local_kv_heads
+        self.heads = heads
+        self.meta = batch.metadata(device)
+        gen = torch.Generator(device=device).manual_seed(1000 + 17 * shard.rank)
+        std = HEAD_DIM ** -0.5
+        Q = batch.total_queries
+        self.q = (torch.randn((Q, heads * GROUPS, HEAD_DIM), generator=gen, device=device) * std).bfloat16()
+        self.k_nodes = (torch.randn((Q, heads, HEAD_DIM), generator=gen, device=device) * std).bfloat16()
+        self.v_nodes = (torch.randn((Q, heads, HEAD_DIM), generator=gen, device=device) * std).bfloat16()
+        # Pool in the reference's layout [2, layers, blocks, bs, kv_heads, dim] (1 layer).
+        self.kv_pool = torch.full((2, 1, batch.num_blocks, BLOCK, heads, HEAD_DIM), float("nan"),
+                                  dtype=torch.bfloat16, device=device)
+        live = torch.from_numpy(batch.live_slots()).to(device)
+        for axis in range(2):
+            flat = self.kv_pool[axis, 0].view(-1, heads, HEAD_DIM)
+            flat[live] = (torch.randn((live.numel(), heads, HEAD_DIM), generator=gen,
+                                      device=device) * std).bfloat16()
+        self.k_pool, self.v_pool = self.kv_pool[0, 0], self.kv_pool[1, 0]
+        src, dst = batch.commit_slots()
+        self.src = torch.tensor(src, dtype=torch.int64, device=device)
+        self.dst = torch.tensor(dst, dtype=torch.int64, device=device)
+        self.scale = HEAD_DIM ** -0.5
+        self.out = None
+
+    def store(self):
+        jb.scatter_tree_kv(self.k_nodes, self.v_nodes, self.k_pool, self.v_pool, self.meta.tree_slots)
+
+    def attend(self):
+        self.out = jb.packed_tree_attention_gqa(self.q, self.k_pool, self.v_pool, self.meta,
+                                                self.scale, GROUPS)
+        return self.out
+
+    def commit(self):
+        jb.copy_accepted_kv(self.kv_pool, self.src, self.dst, BLOCK)
+
+    def __call__(self):
+        self.store()
+        self.attend()
+        self.commit()
+
+    # Byte accounting of the attention launch (algorithmic, per call).
+    def attention_bytes(self):
+        b = self.batch
+        kv = b.kv_bytes(kv_heads=self.heads)
+        q_o = 2 * self.q.numel() * 2
+        meta = sum(t.numel() * t.element_size() for t in (
+            self.meta.cu_seqlens_q, self.meta.query_to_request, self.meta.query_local_row,
+            self.meta.prefix_lens, self.meta.block_tables, self.meta.tree_slots,
+            self.meta.qq_bias, self.meta.qq_bias_offsets, self.meta.node_counts))
+        return kv, q_o + meta
+
+
+def time_device(step: Step, steps: int, warmup: int, world: int, device):
+    for _ in range(warmup):
+        step()
+    torch.cuda.synchronize(device)
+    if world > 1:
+        torch.distributed.barrier()
+    stream = torch.cuda.current_stream(device)
+    start = torch.cuda.Event(enable_timing=True)
+    end = torch.cuda.Event(enable_timing=True)
+    attn_events = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+                   for _ in range(steps)]
+    with ClockSampler(device.index) as clocks:
+        start.record(stream)
+        for i in range(steps):
+            step.store()
+            attn_events[i][0].record(stream)
+            step.attend()
+            attn_events[i][1].record(stream)
+            step.commit()
+        end.record(stream)
+        torch.cuda.synchronize(device)
+    if world > 1:
+        torch.distributed.barrier()
+    total_ms = start.elapsed_time(end)
+    attn_ms = sum(a.elapsed_time(b) for a, b in attn_events) / steps
+    return total_ms, attn_ms, clocks.report()
+
+
+def time_e2e(step: Step, steps: int, warmup: int, world: int, device):
+    """Public-API path with host buffers: H2D of the step's inputs, D2H of the output."""
+    meta = step.meta
+    names = ("cu_seqlens_q", "query_to_request", "query_local_row", "prefix_lens",
+             "block_tables", "tree_slots", "qq_bias", "qq_bias_offsets", "node_counts")
+    host_inputs = [(getattr(meta, n).cpu().pin_memory(), getattr(meta, n)) for n in names]
+    host_inputs += [(t.cpu().pin_memory(), t) for t in (step.q, step.k_nodes, step.v_nodes)]
+    h2d = sum(h.numel() * h.element_size() for h, _ in host_inputs)
+    out_host = torch.empty(step.q.shape, dtype=step.q.dtype).pin_memory()
+    d2h = out_host.numel() * out_host.element_size()
+
+    def one():
+        for host, dev in host_inputs:
+            dev.copy_(host, non_blocking=True)
+        step.store()
+        out = step.attend()
+        step.commit()
+        out_host.copy_(out, non_blocking=True)
+
+    for _ in range(warmup):
+        one()
+    torch.cuda.synchronize(device)
+    if world > 1:
+        torch.distributed.barrier()
+    stream = torch.cuda.current_stream(device)
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record(stream)
+    for _ in range(steps):
+        one()
+    end.record(stream)
+    torch.cuda.synchronize(device)
+    return start.elapsed_time(end), h2d, d2h
+
+
+def max_over_ranks(values, world, device):
+    t = torch.tensor(values, dtype=torch.float64, device=device)
+    if world > 1:
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+    return t.tolist()
+
+
+def traffic_from_profiles(workload: str):
+    path = ROOT / "profiles" / "traffic.json"
+    if not path.exists():
+        return None
+    data = json.loads(path.read_text())
+    entry = data.get(workload)
+    return None if entry is None else entry.get("dram_bytes_per_launch")
+
+
+def main():
+    args = parse()
+    rank = int(os.environ.get("RANK", 0))
+    world = int(os.environ.get("WORLD_SIZE", args.gpus))
+    local_rank = int(os.environ.get("LOCAL_RANK", 0))
+    if args.impl == "reference":
+        return run_reference(args, rank, world)
+    if world != args.gpus and "WORLD_SIZE" in os.environ:
+        args.gpus = world
+    device = torch.device("cuda", local_rank)
+    torch.cuda.set_device(device)
+    if world > 1:
+        torch.distributed.init_process_group("nccl", timeout=timedelta(seconds=300),
+                                             device_id=device)
+    try:
+        batch = global_batch(world, args.requests_per_gpu)
+        shard = shard_for_rank(KV_HEADS, GROUPS, world, rank)
+        step = Step(batch, shard, device)
+        steps, warmup = max(args.steps, 1), max(args.warmup, 3)
+        total_ms, attn_ms, clocks = time_device(step, steps, warmup, world, device)
+        if not torch.isfinite(step.out).all():
+            raise RuntimeError("non-finite attention output: a poisoned KV row was read")
+        e2e_ms, h2d, d2h = time_e2e(step, steps, warmup, world, device)
+        total_ms, attn_ms, e2e_ms = max_over_ranks([total_ms, attn_ms, e2e_ms], world, device)
+        cpu = None
+        if rank == 0 and world == 1 and not args.no_cpu_baseline:
+            rate, sample, cores = cpu_oracle_rate(batch, args.cpu_seconds)
+            cpu = {"value": rate, "unit": UNIT, "cores": cores, "kind": "port", "sample": sample}
+        if rank == 0:
+            pk = peaks()
+            tokens = batch.total_queries
+            ms = total_ms / steps
+            kv_bytes, other_bytes = step.attention_bytes()
+            kv_total = kv_bytes * world
+            achieved = (kv_bytes + other_bytes) / (attn_ms * 1e-3) / 1e9
+            flops = batch.attention_flops(kv_heads=step.heads)
+            workload = f"config3x{world}"
+            line = {
+                "metric": METRIC, "value": tokens / (ms * 1e-3), "unit": UNIT, "n_gpus": world,
+                "steps": steps, "warmup": warmup, "ms_per_step": ms, "higher_is_better": True,
+                "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+                "config": {
+                    "workload": (f"config3 serving mix x{world}: {batch.num_requests} requests, "
+                                 f"ctx log-uniform[512,16384], trees {{16,32,64,128}}, "
+                                 f"GQA 32/8 D128 bf16, KV heads {KV_HEADS // world} per GPU"),
+                    "requests": batch.num_requests, "tree_tokens": tokens,
+                    "kv_bytes_per_step_all_gpus": kv_total,
+                    "parallelism": f"kv-head shard x{world}",
+                    "l2": "inputs larger than L2 (KV per GPU per step > 126 MB)"},
+                "effective_kv_gbs": kv_total / (attn_ms * 1e-3) / 1e9,
+                "attention_ms": attn_ms,
+                "roofline": {"bound": "hbm", "achieved": achieved, "peak": pk["hbm_gbs"],
+                             "unit": "GB/s", "frac": achieved / pk["hbm_gbs"],
+                             "peak_source": pk["source"],
+                             "traffic": traffic_from_profiles(workload),
+                             "tensor_tflops": flops / (attn_ms * 1e-3) / 1e12,
+                             "tensor_frac": flops / (attn_ms * 1e-3) / 1e12 / pk["bf16_tflops"]},
+                "e2e": {"value": tokens / (e2e_ms / steps * 1e-3), "unit": UNIT,
+                        "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
+                "gpu_launches": steps * 4,
+                "clocks": clocks,
+            }
+            if cpu is not None:
+                line["cpu_baseline"] = cpu
+            print(json.dumps(line), flush=True)
+    finally:
+        if world > 1:
+            torch.distributed.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

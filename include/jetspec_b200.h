@@ -1,0 +1,172 @@
+/*
+ * jetspec_b200.h -- C ABI of the B200 (sm_100a) JetSpec tree-verification kernels.
+ *
+ * Everything here is plain C: POD parameter structs holding device pointers, element
+ * strides and sizes, plus a cudaStream_t.  No PyTorch (or other framework) type
+ * appears in any signature.  Every launcher enqueues work on the given stream and
+ * returns immediately: it never synchronises, never allocates device memory and is
+ * safe to call inside CUDA-graph stream capture.  Return value: JT_OK (0) or a
+ * negative JT_ERR_* code; jt_last_error() then holds a one-line message (thread-local).
+ *
+ * Paths below are relative to the nano-vllm-jetspec reference project.
+ */
+#ifndef JETSPEC_B200_H
+#define JETSPEC_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+#include <cuda_runtime_api.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define JT_ABI_VERSION 1
+
+enum JtStatus {
+  JT_OK = 0,
+  JT_ERR_INVALID = -1,     /* bad geometry / dtype / stride / null pointer */
+  JT_ERR_WORKSPACE = -2,   /* workspace missing or smaller than jt_tree_attn_workspace_size */
+  JT_ERR_CUDA = -3,        /* a CUDA runtime call failed (message has the CUDA error) */
+  JT_ERR_UNSUPPORTED = -4  /* valid request this build does not implement */
+};
+
+enum JtDtype { JT_BF16 = 0, JT_F16 = 1, JT_F32 = 2 };
+
+/* Flags for JtTreeAttnParams.flags */
+#define JT_FLAG_FP32_PROBABILITY 1u  /* PV with near-fp32 probabilities (hi+lo bf16 split)  */
+
+/*
+ * Packed ragged tree attention over a paged KV cache.
+ *
+ * Replaces the Triton launch inside packed_tree_attention_gqa
+ * (nanovllm/speculative/jetspec/tree_gqa.py:114-140, kernel :32-111) and the packed
+ * dispatcher's backends (nanovllm/speculative/jetspec/paged_backend.py:240-306).
+ *
+ * Semantics per packed query row i of request r (local node j), query head hq,
+ * kv head h = hq / groups: keys are positions 0..P_r+T_r-1 of the request
+ * (prefix pages from block_tables, then the T_r tree nodes at tree_slots); key
+ * position p is visible iff p < P_r, or p = P_r+n with n <= j and
+ * qq_bias[qq_bias_offsets[r] + j*T_r + n] == 0.  Scores are (q.k)*scale with fp32
+ * accumulation, softmax in fp32, probabilities rounded to the input dtype for the
+ * PV product (unless JT_FLAG_FP32_PROBABILITY), output = acc / sum.
+ *
+ * Metadata arrays are the device tensors of PackedTreeMetadata
+ * (nanovllm/speculative/jetspec/packed_metadata.py:16-33).  Strides are in elements;
+ * the last dimension of q, out, k_pool and v_pool must be contiguous, the row
+ * strides must be multiples of 8 elements and every base 16-byte aligned.
+ */
+typedef struct JtTreeAttnParams {
+  void* out;                       /* [total_queries, q_heads, head_dim], out_dtype      */
+  const void* q;                   /* [total_queries, q_heads, head_dim], dtype          */
+  const void* k_pool;              /* [num_blocks, block_size, kv_heads, head_dim]      */
+  const void* v_pool;              /* same geometry as k_pool                           */
+  const int32_t* cu_seqlens_q;     /* [num_requests + 1]                                */
+  const int32_t* query_to_request; /* [total_queries]                                   */
+  const int32_t* query_local_row;  /* [total_queries]                                   */
+  const int32_t* prefix_lens;      /* [num_requests]                                    */
+  const int32_t* node_counts;      /* [num_requests]                                    */
+  const int32_t* block_tables;     /* [num_requests, table_width] (row stride below)     */
+  const int64_t* tree_slots;       /* [total_queries] physical slot = page*bs + offset  */
+  const float* qq_bias;            /* [sum T_r^2] 0 / -inf                              */
+  const int64_t* qq_bias_offsets;  /* [num_requests + 1]                                */
+  int32_t num_requests;
+  int32_t total_queries;
+  int32_t num_kv_heads;
+  int32_t groups;                  /* query heads per kv head                           */
+  int32_t head_dim;                /* 64 or 128                                         */
+  int32_t block_size;              /* tokens per page                                   */
+  int32_t table_width;             /* columns of block_tables                           */
+  int32_t dtype;                   /* JT_BF16 or JT_F16                                 */
+  int32_t out_dtype;               /* dtype or JT_F32                                   */
+  uint32_t flags;                  /* JT_FLAG_*                                         */
+  int64_t num_blocks;              /* pages in the pool                                 */
+  int64_t q_stride0, q_stride1;
+  int64_t out_stride0, out_stride1;
+  int64_t table_stride0;
+  int64_t k_stride0, k_stride1, k_stride2;
+  int64_t v_stride0, v_stride1, v_stride2;
+  float scale;
+  int32_t split_keys;              /* 0 = automatic; else keys per split (multiple of 1024) */
+  void* workspace;                 /* device scratch, >= jt_tree_attn_workspace_size     */
+  size_t workspace_bytes;
+} JtTreeAttnParams;
+
+/* Bytes of device workspace jt_tree_attn_launch needs for this geometry.  Depends only
+ * on (num_requests, total_queries, num_kv_heads, groups, head_dim), never on prefix
+ * lengths or node counts, so one workspace serves every CUDA-graph replay of a shape. */
+int jt_tree_attn_workspace_size(int32_t num_requests, int32_t total_queries,
+                                int32_t num_kv_heads, int32_t groups, int32_t head_dim,
+                                size_t* bytes);
+
+int jt_tree_attn_launch(const JtTreeAttnParams* params, cudaStream_t stream);
+
+/*
+ * Paged KV store: for token i with slot s = slot_mapping[i] (skipped when s < 0),
+ * k_cache[s / block_size, s % block_size, :, :] = key[i]; same for value.
+ *
+ * Replaces store_kvcache (nanovllm/layers/attention.py:38-45, kernel :15-35) and the
+ * tree-node scratch write in forward_paged_tree (nanovllm/models/qwen3.py:255-258).
+ */
+typedef struct JtKvStoreParams {
+  const void* key;      /* [num_tokens, kv_heads, head_dim] */
+  const void* value;
+  void* k_cache;        /* [num_blocks, block_size, kv_heads, head_dim] */
+  void* v_cache;
+  const void* slot_mapping;   /* [num_tokens] int32 or int64 */
+  int32_t slot_is_int64;
+  int32_t num_tokens;
+  int32_t num_kv_heads;
+  int32_t head_dim;
+  int32_t elem_bytes;   /* 2 or 4 */
+  int32_t block_size;
+  int64_t num_blocks;
+  int64_t key_stride0, key_stride1;
+  int64_t value_stride0, value_stride1;
+  int64_t k_stride0, k_stride1, k_stride2;
+  int64_t v_stride0, v_stride1, v_stride2;
+} JtKvStoreParams;
+
+int jt_kv_store_launch(const JtKvStoreParams* params, cudaStream_t stream);
+
+/*
+ * Accepted-only KV commit across both KV axes and every layer of a 6-D pool
+ * [2, layers, num_blocks, block_size, kv_heads, head_dim]:
+ *   pool[:, :, dst//bs, dst%bs] = pool[:, :, src//bs, src%bs]   (gather before scatter)
+ *
+ * Replaces copy_accepted_kv (nanovllm/speculative/jetspec/state.py:64-86).  The whole
+ * gather completes before any write of the same (axis, layer, head) plane, so
+ * overlapping source/destination sets behave like the reference's materialised copy.
+ * Supports up to jt_kv_commit_max_slots() slots per call.
+ */
+typedef struct JtKvCommitParams {
+  void* kv_pool;
+  const void* source_slots;       /* [num_slots] int32 or int64 */
+  const void* destination_slots;  /* [num_slots] int32 or int64 */
+  int32_t slot_is_int64;
+  int32_t num_slots;
+  int32_t num_layers;
+  int32_t num_kv_heads;
+  int32_t head_dim;
+  int32_t elem_bytes;
+  int32_t block_size;
+  int64_t num_blocks;
+  int64_t stride_axis, stride_layer, stride_block, stride_offset, stride_head; /* elements */
+} JtKvCommitParams;
+
+int jt_kv_commit_launch(const JtKvCommitParams* params, cudaStream_t stream);
+int32_t jt_kv_commit_max_slots(void);
+
+/* Library information / diagnostics. */
+int32_t jt_abi_version(void);
+const char* jt_last_error(void);
+/* Reads and clears the device-side error word of the current device (synchronises;
+ * diagnostics only).  Bit 0: a slot/page index outside the pool was skipped;
+ * bit 1: a tree larger than the kernel's mask capacity was skipped. */
+int jt_read_device_errors(uint32_t* errors);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* JETSPEC_B200_H */

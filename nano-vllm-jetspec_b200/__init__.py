@@ -1,0 +1,30 @@
+"""B200-native (sm_100a) JetSpec tree-verification hot path.
+
+Public operators keep the reference's Python signatures so the nano-vLLM JetSpec
+verifier, scratch arena and block tables work unchanged:
+
+* packed_tree_attention_gqa  - nanovllm/speculative/jetspec/tree_gqa.py:114
+* packed_tree_attention      - nanovllm/speculative/jetspec/paged_backend.py:240
+* store_kvcache              - nanovllm/layers/attention.py:38
+* copy_accepted_kv           - nanovllm/speculative/jetspec/state.py:64
+* PackedTreeMetadata         - nanovllm/speculative/jetspec/packed_metadata.py:16
+
+All compute runs in libjetspec_b200.so (hand-written CUDA for sm_100a) through a C ABI
+(include/jetspec_b200.h).  There is no CPU or library fallback: without the built
+library every operator raises LibraryMissingError.
+"""
+from ._lib import KernelLaunchError, LibraryMissingError, load_library, read_device_errors
+from .attention import store_kvcache
+from .packed_metadata import PackedTreeMetadata, ancestor_mask_from_parents
+from .paged_backend import packed_tree_attention, packed_tree_attention_reference
+from .sharding import KvHeadShard, shard_for_rank
+from .state import _slots_for_blocks, copy_accepted_kv
+from .tree_fusion import scatter_tree_kv
+from .tree_gqa import packed_tree_attention_gqa
+
+__all__ = [
+    "KernelLaunchError", "LibraryMissingError", "load_library", "read_device_errors",
+    "store_kvcache", "PackedTreeMetadata", "ancestor_mask_from_parents",
+    "packed_tree_attention", "packed_tree_attention_reference", "KvHeadShard",
+    "shard_for_rank", "copy_accepted_kv", "scatter_tree_kv", "packed_tree_attention_gqa",
+]

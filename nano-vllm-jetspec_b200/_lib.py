@@ -1,0 +1,162 @@
+"""ctypes binding of the C ABI in include/jetspec_b200.h.
+
+The shared library is the only compute path: if it is missing or fails to load, every
+public operator raises ``LibraryMissingError``.  There is no fallback of any kind.
+"""
+from __future__ import annotations
+
+import ctypes
+from pathlib import Path
+import threading
+
+LIBRARY_PATH = Path(__file__).resolve().parent / "libjetspec_b200.so"
+ABI_VERSION = 1
+
+JT_OK = 0
+JT_ERR_INVALID = -1
+JT_ERR_WORKSPACE = -2
+JT_ERR_CUDA = -3
+JT_ERR_UNSUPPORTED = -4
+
+JT_BF16, JT_F16, JT_F32 = 0, 1, 2
+JT_FLAG_FP32_PROBABILITY = 1
+
+EXPORTED_SYMBOLS = (
+    "jt_tree_attn_workspace_size",
+    "jt_tree_attn_launch",
+    "jt_kv_store_launch",
+    "jt_kv_commit_launch",
+    "jt_kv_commit_max_slots",
+    "jt_abi_version",
+    "jt_last_error",
+    "jt_read_device_errors",
+)
+
+
+class LibraryMissingError(RuntimeError):
+    """The sm_100a kernel library is not built or cannot be loaded."""
+
+
+class KernelLaunchError(RuntimeError):
+    """The C ABI rejected or failed a launch; the message comes from jt_last_error()."""
+
+
+c_void_p = ctypes.c_void_p
+c_i32 = ctypes.c_int32
+c_u32 = ctypes.c_uint32
+c_i64 = ctypes.c_int64
+
+
+class JtTreeAttnParams(ctypes.Structure):
+    _fields_ = [
+        ("out", c_void_p), ("q", c_void_p), ("k_pool", c_void_p), ("v_pool", c_void_p),
+        ("cu_seqlens_q", c_void_p), ("query_to_request", c_void_p),
+        ("query_local_row", c_void_p), ("prefix_lens", c_void_p), ("node_counts", c_void_p),
+        ("block_tables", c_void_p), ("tree_slots", c_void_p), ("qq_bias", c_void_p),
+        ("qq_bias_offsets", c_void_p),
+        ("num_requests", c_i32), ("total_queries", c_i32), ("num_kv_heads", c_i32),
+        ("groups", c_i32), ("head_dim", c_i32), ("block_size", c_i32), ("table_width", c_i32),
+        ("dtype", c_i32), ("out_dtype", c_i32), ("flags", c_u32),
+        ("num_blocks", c_i64),
+        ("q_stride0", c_i64), ("q_stride1", c_i64), ("out_stride0", c_i64),
+        ("out_stride1", c_i64), ("table_stride0", c_i64),
+        ("k_stride0", c_i64), ("k_stride1", c_i64), ("k_stride2", c_i64),
+        ("v_stride0", c_i64), ("v_stride1", c_i64), ("v_stride2", c_i64),
+        ("scale", ctypes.c_float), ("split_keys", c_i32),
+        ("workspace", c_void_p), ("workspace_bytes", ctypes.c_size_t),
+    ]
+
+
+class JtKvStoreParams(ctypes.Structure):
+    _fields_ = [
+        ("key", c_void_p), ("value", c_void_p), ("k_cache", c_void_p), ("v_cache", c_void_p),
+        ("slot_mapping", c_void_p), ("slot_is_int64", c_i32), ("num_tokens", c_i32),
+        ("num_kv_heads", c_i32), ("head_dim", c_i32), ("elem_bytes", c_i32),
+        ("block_size", c_i32), ("num_blocks", c_i64),
+        ("key_stride0", c_i64), ("key_stride1", c_i64),
+        ("value_stride0", c_i64), ("value_stride1", c_i64),
+        ("k_stride0", c_i64), ("k_stride1", c_i64), ("k_stride2", c_i64),
+        ("v_stride0", c_i64), ("v_stride1", c_i64), ("v_stride2", c_i64),
+    ]
+
+
+class JtKvCommitParams(ctypes.Structure):
+    _fields_ = [
+        ("kv_pool", c_void_p), ("source_slots", c_void_p), ("destination_slots", c_void_p),
+        ("slot_is_int64", c_i32), ("num_slots", c_i32), ("num_layers", c_i32),
+        ("num_kv_heads", c_i32), ("head_dim", c_i32), ("elem_bytes", c_i32),
+        ("block_size", c_i32), ("num_blocks", c_i64),
+        ("stride_axis", c_i64), ("stride_layer", c_i64), ("stride_block", c_i64),
+        ("stride_offset", c_i64), ("stride_head", c_i64),
+    ]
+
+
+_lock = threading.Lock()
+_lib = None
+
+
+def _declare(lib):
+    P = ctypes.POINTER
+    lib.jt_tree_attn_workspace_size.argtypes = [c_i32, c_i32, c_i32, c_i32, c_i32,
+                                                P(ctypes.c_size_t)]
+    lib.jt_tree_attn_workspace_size.restype = ctypes.c_int
+    lib.jt_tree_attn_launch.argtypes = [P(JtTreeAttnParams), c_void_p]
+    lib.jt_tree_attn_launch.restype = ctypes.c_int
+    lib.jt_kv_store_launch.argtypes = [P(JtKvStoreParams), c_void_p]
+    lib.jt_kv_store_launch.restype = ctypes.c_int
+    lib.jt_kv_commit_launch.argtypes = [P(JtKvCommitParams), c_void_p]
+    lib.jt_kv_commit_launch.restype = ctypes.c_int
+    lib.jt_kv_commit_max_slots.argtypes = []
+    lib.jt_kv_commit_max_slots.restype = c_i32
+    lib.jt_abi_version.argtypes = []
+    lib.jt_abi_version.restype = c_i32
+    lib.jt_last_error.argtypes = []
+    lib.jt_last_error.restype = ctypes.c_char_p
+    lib.jt_read_device_errors.argtypes = [P(c_u32)]
+    lib.jt_read_device_errors.restype = ctypes.c_int
+
+
+def load_library(path: Path | None = None):
+    """Load (once) and return the ctypes handle of libjetspec_b200.so."""
+    global _lib
+    if _lib is not None and path is None:
+        return _lib
+    with _lock:
+        if _lib is not None and path is None:
+            return _lib
+        target = Path(path) if path is not None else LIBRARY_PATH
+        if not target.exists():
+            raise LibraryMissingError(
+                f"{target.name} is not built; run `python -c \"import __graft_entry__ as g; "
+                f"g.build()\"` from the repository root (needs nvcc for sm_100a)")
+        try:
+            lib = ctypes.CDLL(str(target))
+        except OSError as error:
+            raise LibraryMissingError(f"cannot load {target}: {error}") from error
+        missing = [name for name in EXPORTED_SYMBOLS if not hasattr(lib, name)]
+        if missing:
+            raise LibraryMissingError(f"{target.name} lacks symbols {missing}")
+        _declare(lib)
+        if lib.jt_abi_version() != ABI_VERSION:
+            raise LibraryMissingError(
+                f"{target.name} ABI {lib.jt_abi_version()} != expected {ABI_VERSION}")
+        if path is None:
+            _lib = lib
+        return lib
+
+
+def check(status: int) -> None:
+    if status == JT_OK:
+        return
+    message = load_library().jt_last_error().decode(errors="replace")
+    if status in (JT_ERR_INVALID, JT_ERR_UNSUPPORTED):
+        raise ValueError(message)
+    raise KernelLaunchError(f"status {status}: {message}")
+
+
+def read_device_errors() -> int:
+    """Read and clear the device error words (synchronises; diagnostics only)."""
+    lib = load_library()
+    bits = c_u32(0)
+    check(lib.jt_read_device_errors(ctypes.byref(bits)))
+    return int(bits.value)

@@ -1,0 +1,767 @@
+// Packed ragged GQA tree-verification attention over a paged KV cache (sm_100a).
+//
+// Replaces the Triton kernel _packed_tree_gqa_dot and its launcher
+// (nanovllm/speculative/jetspec/tree_gqa.py:32-140).  Same semantics: for every packed
+// tree node, each of the `groups` query heads of one KV head attends to the request's
+// prefix (through its block table) plus the tree nodes its ancestor bias admits;
+// scores and softmax in fp32, probabilities rounded to the operand type for PV.
+//
+// Structure (two launches on the caller's stream, both graph-capturable):
+//   1. plan kernel   - block 0 builds the work list from the DEVICE prefix lengths and
+//                      node counts (split-KV plan, longest-first order, partial-slot
+//                      offsets); the other blocks turn qq_bias rows into ancestor
+//                      bitmasks (one warp per tree node, one ballot per 32 nodes).
+//   2. attention     - persistent CTAs pull work items (request, split, kv head,
+//                      m-block) from an atomic queue.  One item = BM score rows
+//                      (BM/groups tree nodes x groups query heads of one KV head)
+//                      against a contiguous key range, streamed in 64-key tiles
+//                      through a 3-stage cp.async ring with 16-byte loads.  QK^T and
+//                      PV run on tensor cores (m16n8k16, fp32 accumulate); online
+//                      softmax in fp32 registers.  Items of split requests write
+//                      unnormalised partials; the last CTA of a (request, head,
+//                      m-block) merges them (counter in the workspace).
+#include <algorithm>
+
+#include "common.cuh"
+
+namespace {
+
+__device__ uint32_t g_attn_errors;
+
+constexpr int kTileKeys = 64;     // keys per KV tile
+constexpr int kStages = 3;        // cp.async ring depth
+constexpr int kMaxMaskWords = 32; // tree nodes per request <= 1024
+constexpr int kPlanThreads = 256;
+constexpr int kBuckets = 32;
+constexpr int kSplitCandidates = 16;  // split lengths 1024 << c
+constexpr int64_t kPartialBudgetBytes = 256ll << 20;
+
+// ---- workspace layout ---------------------------------------------------------------
+struct Layout {
+  int bm;           // score rows per item (64 or 128)
+  int mask_words;   // 32-bit words of ancestor bitmask per tree node
+  int max_items;
+  int max_slots;    // partial-result slots (split items)
+  size_t off_header, off_req, off_items, off_counters, off_masks, off_part_o, off_part_ml;
+  size_t total;
+};
+
+size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
+
+int choose_bm(int32_t num_requests, int32_t total_queries, int32_t groups) {
+  // 128-row items (8 warps) once the average request carries >= 128 score rows per KV
+  // head; otherwise 64-row items (4 warps).  Depends only on the launch shape.
+  return static_cast<int64_t>(total_queries) * groups >= 128ll * num_requests ? 128 : 64;
+}
+
+Layout make_layout(int32_t R, int32_t Q, int32_t H, int32_t G, int32_t D) {
+  Layout L{};
+  L.bm = choose_bm(R, Q, G);
+  L.mask_words = static_cast<int>(std::min<int64_t>((std::max<int32_t>(Q, 1) + 31) / 32,
+                                                    kMaxMaskWords));
+  const int64_t mblocks_bound = (static_cast<int64_t>(Q) * G) / L.bm + R;
+  const int64_t per_slot = static_cast<int64_t>(L.bm) * D * 4;
+  int64_t slots = std::min<int64_t>(4 * mblocks_bound * H, kPartialBudgetBytes / per_slot);
+  slots = std::max<int64_t>(slots, 1);
+  L.max_slots = static_cast<int>(slots);
+  L.max_items = static_cast<int>(mblocks_bound * H + slots);
+  size_t o = 0;
+  L.off_header = o;   o = align_up(o + 64, 256);
+  L.off_req = o;      o = align_up(o + sizeof(int4) * static_cast<size_t>(R), 256);
+  L.off_items = o;    o = align_up(o + sizeof(int4) * static_cast<size_t>(L.max_items), 256);
+  L.off_counters = o; o = align_up(o + sizeof(int) * static_cast<size_t>(L.max_slots), 256);
+  L.off_masks = o;
+  o = align_up(o + sizeof(uint32_t) * static_cast<size_t>(Q) * L.mask_words, 256);
+  L.off_part_o = o;   o = align_up(o + static_cast<size_t>(per_slot) * L.max_slots, 256);
+  L.off_part_ml = o;
+  o = align_up(o + sizeof(float2) * static_cast<size_t>(L.bm) * L.max_slots, 256);
+  L.total = o;
+  return L;
+}
+
+struct DevLayout {
+  int* header;      // [0] queue head, [1] item count, [2] split keys
+  int4* req;        // per request: n_split, partial base, counter base, m-blocks
+  int4* items;      // request, split, kv head, m-block
+  int* counters;
+  uint32_t* masks;
+  float* part_o;
+  float2* part_ml;
+  int bm, mask_words, max_items, max_slots;
+};
+
+DevLayout device_layout(const Layout& L, void* ws) {
+  char* b = static_cast<char*>(ws);
+  DevLayout d;
+  d.header = reinterpret_cast<int*>(b + L.off_header);
+  d.req = reinterpret_cast<int4*>(b + L.off_req);
+  d.items = reinterpret_cast<int4*>(b + L.off_items);
+  d.counters = reinterpret_cast<int*>(b + L.off_counters);
+  d.masks = reinterpret_cast<uint32_t*>(b + L.off_masks);
+  d.part_o = reinterpret_cast<float*>(b + L.off_part_o);
+  d.part_ml = reinterpret_cast<float2*>(b + L.off_part_ml);
+  d.bm = L.bm;
+  d.mask_words = L.mask_words;
+  d.max_items = L.max_items;
+  d.max_slots = L.max_slots;
+  return d;
+}
+
+// ---- plan kernel --------------------------------------------------------------------
+__device__ __forceinline__ int64_t block_sum_i64(int64_t v, int64_t* scratch) {
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  __syncthreads();
+  if (lane == 0) scratch[warp] = v;
+  __syncthreads();
+  int64_t total = 0;
+  for (int w = 0; w < kPlanThreads / 32; ++w) total += scratch[w];
+  return total;
+}
+
+__device__ __forceinline__ int request_mblocks(int nodes, int groups, int bm) {
+  return static_cast<int>((static_cast<int64_t>(nodes) * groups + bm - 1) / bm);
+}
+
+__device__ __forceinline__ int request_splits(int prefix, int split_keys) {
+  return prefix > split_keys ? (prefix + split_keys - 1) / split_keys : 1;
+}
+
+__global__ void __launch_bounds__(kPlanThreads)
+    tree_plan_kernel(JtTreeAttnParams p, DevLayout w, int num_ctas) {
+  const int tid = threadIdx.x;
+  if (blockIdx.x > 0) {
+    // Ancestor bitmask of one packed tree node per warp.
+    const int q = (blockIdx.x - 1) * (kPlanThreads / 32) + (tid >> 5);
+    const int lane = tid & 31;
+    if (q >= p.total_queries) return;
+    const int r = p.query_to_request[q];
+    const int j = p.query_local_row[q];
+    const int nodes = p.node_counts[r];
+    if (nodes > w.mask_words * 32) {
+      if (lane == 0) atomicOr(&g_attn_errors, JT_DEVERR_TREE_TOO_LARGE);
+      return;
+    }
+    const float* bias = p.qq_bias + p.qq_bias_offsets[r] + static_cast<int64_t>(j) * nodes;
+    for (int word = 0; word < w.mask_words; ++word) {
+      const int n = word * 32 + lane;
+      const bool visible = n < nodes && n <= j && bias[n] == 0.0f;
+      const uint32_t bits = __ballot_sync(0xffffffffu, visible);
+      if (lane == 0) w.masks[static_cast<int64_t>(q) * w.mask_words + word] = bits;
+    }
+    return;
+  }
+
+  __shared__ int64_t red[kPlanThreads / 32];
+  __shared__ int64_t cand_slots[kSplitCandidates];
+  __shared__ int bucket_count[kBuckets];
+  __shared__ int bucket_start[kBuckets];
+  __shared__ int s_split;
+  __shared__ int s_carry[2];
+  __shared__ int warp_tot[2][kPlanThreads / 32];
+
+  const int R = p.num_requests, G = p.groups, H = p.num_kv_heads, bm = w.bm;
+  const int cap = w.mask_words * 32;
+
+  // Total work in key x m-block units and, per candidate split length, the partial
+  // slots it would need.
+  int64_t work = 0;
+  int64_t cand[kSplitCandidates];
+#pragma unroll
+  for (int c = 0; c < kSplitCandidates; ++c) cand[c] = 0;
+  for (int r = tid; r < R; r += kPlanThreads) {
+    const int nodes = p.node_counts[r];
+    const int prefix = p.prefix_lens[r];
+    if (nodes < 1 || nodes > cap || prefix < 0) continue;
+    const int mb = request_mblocks(nodes, G, bm);
+    work += static_cast<int64_t>(prefix + nodes) * mb * H;
+#pragma unroll
+    for (int c = 0; c < kSplitCandidates; ++c) {
+      const int s = request_splits(prefix, 1024 << c);
+      if (s > 1) cand[c] += static_cast<int64_t>(s) * mb * H;
+    }
+  }
+  work = block_sum_i64(work, red);
+  for (int c = 0; c < kSplitCandidates; ++c) {
+    const int64_t v = block_sum_i64(cand[c], red);
+    if (tid == 0) cand_slots[c] = v;
+  }
+  if (tid < kBuckets) bucket_count[tid] = 0;
+  if (tid == 0) {
+    int split;
+    if (p.split_keys > 0) {
+      split = p.split_keys;
+      int c = 0;
+      while (c < kSplitCandidates && (1024 << c) < split) ++c;
+      // An explicit split that would overflow the partial budget is coarsened.
+      while (c < kSplitCandidates && cand_slots[c] > w.max_slots) { ++c; split = 1024 << c; }
+    } else {
+      // Aim for ~2 items per resident CTA; never below 1024 keys per split.
+      const int64_t target = work / (2ll * num_ctas);
+      int c = 0;
+      while (c < kSplitCandidates - 1 &&
+             ((1024ll << c) < target || cand_slots[c] > w.max_slots))
+        ++c;
+      split = 1024 << c;
+    }
+    s_split = split;
+    s_carry[0] = s_carry[1] = 0;
+  }
+  __syncthreads();
+  const int split = s_split;
+
+  // Per-request split count plus exclusive scans of partial slots and counters.
+  const int warp = tid >> 5, lane = tid & 31;
+  for (int base = 0; base < R; base += kPlanThreads) {
+    const int r = base + tid;
+    int n_split = 1, mb = 0, slots = 0, counters = 0;
+    if (r < R) {
+      const int nodes = p.node_counts[r];
+      const int prefix = p.prefix_lens[r];
+      if (nodes >= 1 && nodes <= cap && prefix >= 0) {
+        mb = request_mblocks(nodes, G, bm);
+        n_split = request_splits(prefix, split);
+        if (n_split > 1) {
+          slots = n_split * mb * H;
+          counters = mb * H;
+        }
+      } else {
+        n_split = 0;  // skipped request (flagged by the mask blocks)
+      }
+    }
+    int a = slots, b = counters;
+    for (int o = 1; o < 32; o <<= 1) {
+      const int ya = __shfl_up_sync(0xffffffffu, a, o);
+      const int yb = __shfl_up_sync(0xffffffffu, b, o);
+      if (lane >= o) { a += ya; b += yb; }
+    }
+    if (lane == 31) { warp_tot[0][warp] = a; warp_tot[1][warp] = b; }
+    __syncthreads();
+    int pa = s_carry[0], pb = s_carry[1];
+    for (int k = 0; k < warp; ++k) { pa += warp_tot[0][k]; pb += warp_tot[1][k]; }
+    if (r < R) w.req[r] = make_int4(n_split, pa + a - slots, pb + b - counters, mb);
+    __syncthreads();
+    if (tid == kPlanThreads - 1) { s_carry[0] = pa + a; s_carry[1] = pb + b; }
+    __syncthreads();
+  }
+  // Reset split counters for this launch.
+  for (int i = tid; i < s_carry[1]; i += kPlanThreads) w.counters[i] = 0;
+
+  // Longest-first item order: bucket units (request, split) by floor(log2(keys)).
+  for (int r = tid; r < R; r += kPlanThreads) {
+    const int4 info = w.req[r];
+    if (info.x == 0) continue;
+    const int prefix = p.prefix_lens[r], nodes = p.node_counts[r];
+    for (int s = 0; s < info.x; ++s) {
+      const int keys = (s + 1 < info.x) ? split : prefix + nodes - s * split;
+      const int bkt = 31 - __clz(max(keys, 1));
+      atomicAdd(&bucket_count[bkt], info.w * H);
+    }
+  }
+  __syncthreads();
+  if (tid == 0) {
+    int run = 0;
+    for (int b = kBuckets - 1; b >= 0; --b) { bucket_start[b] = run; run += bucket_count[b]; }
+    w.header[1] = run <= w.max_items ? run : 0;
+    if (run > w.max_items) atomicOr(&g_attn_errors, JT_DEVERR_OUT_OF_RANGE);
+    w.header[0] = 0;
+    w.header[2] = split;
+  }
+  __syncthreads();
+  for (int r = tid; r < R; r += kPlanThreads) {
+    const int4 info = w.req[r];
+    if (info.x == 0) continue;
+    const int prefix = p.prefix_lens[r], nodes = p.node_counts[r];
+    for (int s = 0; s < info.x; ++s) {
+      const int keys = (s + 1 < info.x) ? split : prefix + nodes - s * split;
+      const int bkt = 31 - __clz(max(keys, 1));
+      const int pos = atomicAdd(&bucket_start[bkt], info.w * H);
+      if (pos + info.w * H > w.max_items) continue;
+      for (int h = 0; h < H; ++h)
+        for (int m = 0; m < info.w; ++m) w.items[pos + h * info.w + m] = make_int4(r, s, h, m);
+    }
+  }
+}
+
+// ---- attention kernel ---------------------------------------------------------------
+template <int D>
+__device__ __forceinline__ uint32_t swz(int row, int chunk) {
+  // 16-byte chunk XOR swizzle: conflict-free cp.async writes and ldmatrix reads.
+  return static_cast<uint32_t>(row * (D * 2) + ((chunk ^ (row & 7)) << 4));
+}
+
+template <typename Elem, int WARPS, int D, bool FP32P>
+struct AttnKernel {
+  static constexpr int kThreads = WARPS * 32;
+  static constexpr int kBM = WARPS * 16;
+  static constexpr int kRowBytes = D * 2;
+  static constexpr int kChunks = D / 8;  // 16-byte chunks per row
+  static constexpr int kQBytes = kBM * kRowBytes;
+  static constexpr int kTileBytes = kTileKeys * kRowBytes;
+  static constexpr int kSmem = kQBytes + 2 * kStages * kTileBytes;
+  static constexpr int kNT = kTileKeys / 8;  // score n-tiles per warp
+  static constexpr int kDT = D / 8;          // output n-tiles per warp
+  static constexpr int kKS = D / 16;         // k-steps over head_dim
+};
+
+template <typename Elem, int WARPS, int D, bool FP32P>
+__global__ void __launch_bounds__(WARPS * 32)
+    tree_attn_kernel(JtTreeAttnParams p, DevLayout w) {
+  using K = AttnKernel<Elem, WARPS, D, FP32P>;
+  using Mma = jt::MmaOp<Elem>;
+  extern __shared__ __align__(128) unsigned char smem[];
+  __shared__ int s_item;
+  __shared__ int s_last;
+  const uint32_t sbase = jt::smem_u32(smem);
+  const uint32_t sq = sbase;
+  const uint32_t sk = sbase + K::kQBytes;
+  const uint32_t sv = sk + kStages * K::kTileBytes;
+
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int g4 = lane >> 2, t4 = lane & 3;
+  const int G = p.groups, H = p.num_kv_heads, bs = p.block_size;
+  const int num_items = w.header[1];
+  const int split_keys = w.header[2];
+  const float scale_log2 = p.scale * 1.4426950408889634f;
+  const int64_t pool_slots = p.num_blocks * static_cast<int64_t>(bs);
+  const char* kbase = static_cast<const char*>(p.k_pool);
+  const char* vbase = static_cast<const char*>(p.v_pool);
+
+  for (;;) {
+    if (tid == 0) s_item = atomicAdd(&w.header[0], 1);
+    __syncthreads();
+    const int item = s_item;
+    if (item >= num_items) break;
+    const int4 it = w.items[item];
+    const int r = it.x, split = it.y, h = it.z, mb = it.w;
+    const int4 info = w.req[r];
+    const int n_split = info.x, mblocks = info.w;
+    const int P = p.prefix_lens[r];
+    const int T = p.node_counts[r];
+    const int q_start = p.cu_seqlens_q[r];
+    const int row0 = mb * K::kBM;
+    const int key_begin = split * split_keys;
+    int key_end;
+    if (split + 1 < n_split) {
+      key_end = key_begin + split_keys;
+    } else {
+      // Tree nodes after the last one any row of this block can see are pruned.
+      const int vis_nodes = min(T, (row0 + K::kBM + G - 1) / G);
+      key_end = P + vis_nodes;
+    }
+    const int n_tiles = (key_end - key_begin + kTileKeys - 1) / kTileKeys;
+    const int32_t* table = p.block_tables + static_cast<int64_t>(r) * p.table_stride0;
+
+    // --- async loads ------------------------------------------------------------------
+    auto load_q = [&]() {
+      for (int c = tid; c < K::kBM * K::kChunks; c += K::kThreads) {
+        const int row = c / K::kChunks, ch = c - row * K::kChunks;
+        const int gm = row0 + row;
+        const int j = gm / G, g = gm - j * G;
+        const bool ok = j < T;
+        const char* src = static_cast<const char*>(p.q);
+        if (ok)
+          src += ((static_cast<int64_t>(q_start + j) * p.q_stride0) +
+                  static_cast<int64_t>(h * G + g) * p.q_stride1 + ch * 8) * 2;
+        jt::cp_async_16(sq + swz<D>(row, ch), src, ok ? 16 : 0);
+      }
+    };
+    auto load_kv = [&](int tile, int stage) {
+      const int kb = key_begin + tile * kTileKeys;
+      for (int c = tid; c < kTileKeys * K::kChunks; c += K::kThreads) {
+        const int row = c / K::kChunks, ch = c - row * K::kChunks;
+        const int pos = kb + row;
+        int64_t page = 0, off = 0;
+        bool ok = pos < key_end;
+        if (ok) {
+          int64_t slot = -1;
+          if (pos < P) {
+            const int col = pos / bs;
+            if (col < p.table_width) slot = static_cast<int64_t>(__ldg(table + col)) * bs + pos % bs;
+          } else {
+            slot = __ldg(p.tree_slots + q_start + (pos - P));
+          }
+          if (slot < 0 || slot >= pool_slots) {
+            ok = false;
+            if (ch == 0) atomicOr(&g_attn_errors, JT_DEVERR_OUT_OF_RANGE);
+          } else {
+            page = slot / bs;
+            off = slot - page * bs;
+          }
+        }
+        const char* ks = kbase;
+        const char* vs = vbase;
+        if (ok) {
+          ks += (page * p.k_stride0 + off * p.k_stride1 + static_cast<int64_t>(h) * p.k_stride2 +
+                 ch * 8) * 2;
+          vs += (page * p.v_stride0 + off * p.v_stride1 + static_cast<int64_t>(h) * p.v_stride2 +
+                 ch * 8) * 2;
+        }
+        const uint32_t o = static_cast<uint32_t>(stage * K::kTileBytes) + swz<D>(row, ch);
+        jt::cp_async_16(sk + o, ks, ok ? 16 : 0);
+        jt::cp_async_16(sv + o, vs, ok ? 16 : 0);
+      }
+    };
+
+    load_q();
+#pragma unroll
+    for (int st = 0; st < kStages - 1; ++st) {
+      if (st < n_tiles) load_kv(st, st);
+      jt::cp_async_commit();
+    }
+
+    // Per-thread score rows: g4 and g4 + 8 of this warp's 16.
+    int row_j[2];
+    bool row_ok[2];
+    const uint32_t* row_mask[2];
+#pragma unroll
+    for (int hrow = 0; hrow < 2; ++hrow) {
+      const int gm = row0 + warp * 16 + g4 + hrow * 8;
+      row_j[hrow] = gm / G;
+      row_ok[hrow] = row_j[hrow] < T;
+      row_mask[hrow] = w.masks + static_cast<int64_t>(q_start + (row_ok[hrow] ? row_j[hrow] : 0)) *
+                                    w.mask_words;
+    }
+
+    uint32_t qf[K::kKS][4];
+    float o_acc[K::kDT][4];
+#pragma unroll
+    for (int i = 0; i < K::kDT; ++i) o_acc[i][0] = o_acc[i][1] = o_acc[i][2] = o_acc[i][3] = 0.f;
+    float m_run[2] = {-INFINITY, -INFINITY};
+    float l_run[2] = {0.f, 0.f};
+
+    for (int tile = 0; tile < n_tiles; ++tile) {
+      jt::cp_async_wait<kStages - 2>();
+      __syncthreads();
+      if (tile == 0) {
+#pragma unroll
+        for (int ks = 0; ks < K::kKS; ++ks) {
+          const int row = warp * 16 + (lane & 15);
+          const int ch = ks * 2 + (lane >> 4);
+          jt::ldmatrix_x4(qf[ks], sq + swz<D>(row, ch));
+        }
+      }
+      {
+        const int nxt = tile + kStages - 1;
+        if (nxt < n_tiles) load_kv(nxt, nxt % kStages);
+        jt::cp_async_commit();
+      }
+      const int stage = tile % kStages;
+      const uint32_t ks_base = sk + stage * K::kTileBytes;
+      const uint32_t vs_base = sv + stage * K::kTileBytes;
+
+      // S = Q K^T for this warp's 16 rows x 64 keys.
+      float s[K::kNT][4];
+#pragma unroll
+      for (int i = 0; i < K::kNT; ++i) s[i][0] = s[i][1] = s[i][2] = s[i][3] = 0.f;
+#pragma unroll
+      for (int ks = 0; ks < K::kKS; ++ks) {
+#pragma unroll
+        for (int np = 0; np < K::kNT / 2; ++np) {
+          uint32_t b[4];
+          const int key = np * 16 + (lane & 7) + ((lane >> 4) << 3);
+          const int ch = ks * 2 + ((lane >> 3) & 1);
+          jt::ldmatrix_x4(b, ks_base + swz<D>(key, ch));
+          Mma::run(s[2 * np], qf[ks], b[0], b[1]);
+          Mma::run(s[2 * np + 1], qf[ks], b[2], b[3]);
+        }
+      }
+
+      // Scale into the log2 domain and mask.
+      const int kb = key_begin + tile * kTileKeys;
+      const bool full = kb + kTileKeys <= min(P, key_end);
+#pragma unroll
+      for (int nt = 0; nt < K::kNT; ++nt) {
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          float v = s[nt][e] * scale_log2;
+          if (!full) {
+            const int hrow = e >> 1;
+            const int pos = kb + nt * 8 + t4 * 2 + (e & 1);
+            bool vis = row_ok[hrow] && pos < key_end;
+            if (vis && pos >= P) {
+              const int n = pos - P;
+              vis = (__ldg(row_mask[hrow] + (n >> 5)) >> (n & 31)) & 1u;
+            }
+            if (!vis) v = -INFINITY;
+          }
+          s[nt][e] = v;
+        }
+      }
+
+      // Online softmax (row max over the quad, guarded exponent base).
+      float alpha[2], m_use[2];
+#pragma unroll
+      for (int hrow = 0; hrow < 2; ++hrow) {
+        float mx = -INFINITY;
+#pragma unroll
+        for (int nt = 0; nt < K::kNT; ++nt)
+          mx = fmaxf(mx, fmaxf(s[nt][2 * hrow], s[nt][2 * hrow + 1]));
+        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+        const float m_new = fmaxf(m_run[hrow], mx);
+        m_use[hrow] = m_new == -INFINITY ? 0.f : m_new;
+        alpha[hrow] = jt::fast_exp2(m_run[hrow] - m_use[hrow]);
+        m_run[hrow] = m_new;
+      }
+      float rsum[2] = {0.f, 0.f};
+      uint32_t pa[K::kNT / 2][4];
+      uint32_t pl[FP32P ? K::kNT / 2 : 1][4];
+#pragma unroll
+      for (int nt = 0; nt < K::kNT; ++nt) {
+        float pr[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          pr[e] = jt::fast_exp2(s[nt][e] - m_use[e >> 1]);
+          rsum[e >> 1] += pr[e];
+        }
+        const int kk = nt >> 1, hi = (nt & 1) * 2;
+        pa[kk][hi + 0] = Mma::pack(pr[0], pr[1]);
+        pa[kk][hi + 1] = Mma::pack(pr[2], pr[3]);
+        if constexpr (FP32P) {
+          const float2 r01 = Mma::unpack(pa[kk][hi + 0]);
+          const float2 r23 = Mma::unpack(pa[kk][hi + 1]);
+          pl[kk][hi + 0] = Mma::pack(pr[0] - r01.x, pr[1] - r01.y);
+          pl[kk][hi + 1] = Mma::pack(pr[2] - r23.x, pr[3] - r23.y);
+        }
+      }
+#pragma unroll
+      for (int hrow = 0; hrow < 2; ++hrow) l_run[hrow] = l_run[hrow] * alpha[hrow] + rsum[hrow];
+#pragma unroll
+      for (int dt = 0; dt < K::kDT; ++dt) {
+        o_acc[dt][0] *= alpha[0];
+        o_acc[dt][1] *= alpha[0];
+        o_acc[dt][2] *= alpha[1];
+        o_acc[dt][3] *= alpha[1];
+      }
+
+      // O += P V.
+#pragma unroll
+      for (int kk = 0; kk < K::kNT / 2; ++kk) {
+#pragma unroll
+        for (int dp = 0; dp < K::kDT / 2; ++dp) {
+          uint32_t b[4];
+          const int key = kk * 16 + (lane & 7) + (((lane >> 3) & 1) << 3);
+          const int ch = dp * 2 + (lane >> 4);
+          jt::ldmatrix_x4_trans(b, vs_base + swz<D>(key, ch));
+          Mma::run(o_acc[2 * dp], pa[kk], b[0], b[1]);
+          Mma::run(o_acc[2 * dp + 1], pa[kk], b[2], b[3]);
+          if constexpr (FP32P) {
+            Mma::run(o_acc[2 * dp], pl[kk], b[0], b[1]);
+            Mma::run(o_acc[2 * dp + 1], pl[kk], b[2], b[3]);
+          }
+        }
+      }
+    }
+    jt::cp_async_wait<0>();
+
+    // Row sums across the quad.
+#pragma unroll
+    for (int hrow = 0; hrow < 2; ++hrow) {
+      l_run[hrow] += __shfl_xor_sync(0xffffffffu, l_run[hrow], 1);
+      l_run[hrow] += __shfl_xor_sync(0xffffffffu, l_run[hrow], 2);
+    }
+
+    auto store_row = [&](int gm, int d, float x0, float x1) {
+      const int j = gm / G, g = gm - j * G;
+      if (j >= T) return;
+      const int64_t off = static_cast<int64_t>(q_start + j) * p.out_stride0 +
+                          static_cast<int64_t>(h * G + g) * p.out_stride1 + d;
+      if (p.out_dtype == JT_F32) {
+        *reinterpret_cast<float2*>(static_cast<float*>(p.out) + off) = make_float2(x0, x1);
+      } else {
+        *reinterpret_cast<uint32_t*>(static_cast<Elem*>(p.out) + off) = Mma::pack(x0, x1);
+      }
+    };
+
+    if (n_split == 1) {
+#pragma unroll
+      for (int hrow = 0; hrow < 2; ++hrow) {
+        const float inv = 1.f / l_run[hrow];
+        const int gm = row0 + warp * 16 + g4 + hrow * 8;
+#pragma unroll
+        for (int dt = 0; dt < K::kDT; ++dt)
+          store_row(gm, dt * 8 + t4 * 2, o_acc[dt][2 * hrow] * inv,
+                    o_acc[dt][2 * hrow + 1] * inv);
+      }
+    } else {
+      // Unnormalised partial + (max, sum); the last CTA of this group merges.
+      const int64_t slot = info.y + (static_cast<int64_t>(h) * mblocks + mb) * n_split + split;
+      float* po = w.part_o + slot * K::kBM * D;
+      float2* pml = w.part_ml + slot * K::kBM;
+#pragma unroll
+      for (int hrow = 0; hrow < 2; ++hrow) {
+        const int row = warp * 16 + g4 + hrow * 8;
+#pragma unroll
+        for (int dt = 0; dt < K::kDT; ++dt)
+          *reinterpret_cast<float2*>(po + row * D + dt * 8 + t4 * 2) =
+              make_float2(o_acc[dt][2 * hrow], o_acc[dt][2 * hrow + 1]);
+        if (t4 == 0) pml[row] = make_float2(m_run[hrow], l_run[hrow]);
+      }
+      __threadfence();
+      __syncthreads();
+      if (tid == 0) {
+        int* counter = w.counters + info.z + h * mblocks + mb;
+        const int done = atomicAdd(counter, 1);
+        s_last = done == n_split - 1;
+        if (s_last) *counter = 0;
+      }
+      __syncthreads();
+      if (s_last) {
+        __threadfence();
+        const int64_t slot0 = info.y + (static_cast<int64_t>(h) * mblocks + mb) * n_split;
+        for (int idx = tid; idx < K::kBM * (D / 4); idx += K::kThreads) {
+          const int row = idx / (D / 4), d4 = (idx - row * (D / 4)) * 4;
+          if ((row0 + row) / G >= T) continue;
+          float mmax = -INFINITY;
+          for (int s2 = 0; s2 < n_split; ++s2)
+            mmax = fmaxf(mmax, __ldcg(w.part_ml + (slot0 + s2) * K::kBM + row).x);
+          const float mref = mmax == -INFINITY ? 0.f : mmax;
+          float den = 0.f;
+          float4 num = make_float4(0.f, 0.f, 0.f, 0.f);
+          for (int s2 = 0; s2 < n_split; ++s2) {
+            const float2 ml = __ldcg(w.part_ml + (slot0 + s2) * K::kBM + row);
+            const float wgt = jt::fast_exp2(ml.x - mref);
+            const float4 o = __ldcg(reinterpret_cast<const float4*>(
+                w.part_o + ((slot0 + s2) * K::kBM + row) * D + d4));
+            den += wgt * ml.y;
+            num.x += wgt * o.x;
+            num.y += wgt * o.y;
+            num.z += wgt * o.z;
+            num.w += wgt * o.w;
+          }
+          const float inv = 1.f / den;
+          store_row(row0 + row, d4, num.x * inv, num.y * inv);
+          store_row(row0 + row, d4 + 2, num.z * inv, num.w * inv);
+        }
+      }
+    }
+    __syncthreads();
+  }
+}
+
+// ---- host side ----------------------------------------------------------------------
+struct DeviceInfo {
+  int sms = 0;
+};
+DeviceInfo g_devices[64];
+
+int device_sms(int* sms) {
+  int dev = 0;
+  int rc = jt_cuda_check(cudaGetDevice(&dev), "cudaGetDevice");
+  if (rc != JT_OK) return rc;
+  if (dev < 0 || dev >= 64) return jt_fail(JT_ERR_UNSUPPORTED, "device index %d >= 64", dev);
+  if (g_devices[dev].sms == 0) {
+    int v = 0;
+    rc = jt_cuda_check(cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev),
+                       "SM count");
+    if (rc != JT_OK) return rc;
+    g_devices[dev].sms = v;
+  }
+  *sms = g_devices[dev].sms;
+  return JT_OK;
+}
+
+template <typename Elem, int WARPS, int D, bool FP32P>
+int launch_attn(const JtTreeAttnParams& p, const Layout& L, const DevLayout& d,
+                cudaStream_t stream) {
+  using K = AttnKernel<Elem, WARPS, D, FP32P>;
+  auto kernel = tree_attn_kernel<Elem, WARPS, D, FP32P>;
+  int rc = jt_cuda_check(
+      cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, K::kSmem),
+      "attention smem attribute");
+  if (rc != JT_OK) return rc;
+  int sms = 0;
+  rc = device_sms(&sms);
+  if (rc != JT_OK) return rc;
+  int per_sm = 0;
+  rc = jt_cuda_check(
+      cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, K::kThreads, K::kSmem),
+      "attention occupancy");
+  if (rc != JT_OK) return rc;
+  per_sm = std::max(per_sm, 1);
+  const int num_ctas = sms * per_sm;
+  const int plan_blocks = 1 + (p.total_queries + kPlanThreads / 32 - 1) / (kPlanThreads / 32);
+  tree_plan_kernel<<<plan_blocks, kPlanThreads, 0, stream>>>(p, d, num_ctas);
+  rc = jt_cuda_check(cudaGetLastError(), "plan launch");
+  if (rc != JT_OK) return rc;
+  const int grid = std::min(num_ctas, L.max_items);
+  kernel<<<grid, K::kThreads, K::kSmem, stream>>>(p, d);
+  return jt_cuda_check(cudaGetLastError(), "attention launch");
+}
+
+template <typename Elem, int D>
+int dispatch_bm(const JtTreeAttnParams& p, const Layout& L, const DevLayout& d,
+                cudaStream_t stream) {
+  const bool fp32p = (p.flags & JT_FLAG_FP32_PROBABILITY) != 0;
+  if (L.bm == 128)
+    return fp32p ? launch_attn<Elem, 8, D, true>(p, L, d, stream)
+                 : launch_attn<Elem, 8, D, false>(p, L, d, stream);
+  return fp32p ? launch_attn<Elem, 4, D, true>(p, L, d, stream)
+               : launch_attn<Elem, 4, D, false>(p, L, d, stream);
+}
+
+bool al16(const void* ptr) { return (reinterpret_cast<uintptr_t>(ptr) & 15u) == 0; }
+
+}  // namespace
+
+int jt_read_errors_attn(uint32_t* bits) {
+  uint32_t zero = 0;
+  int rc = jt_cuda_check(cudaMemcpyFromSymbol(bits, g_attn_errors, sizeof(uint32_t)),
+                         "read attention error word");
+  if (rc != JT_OK) return rc;
+  return jt_cuda_check(cudaMemcpyToSymbol(g_attn_errors, &zero, sizeof(uint32_t)),
+                       "clear attention error word");
+}
+
+extern "C" int jt_tree_attn_workspace_size(int32_t num_requests, int32_t total_queries,
+                                           int32_t num_kv_heads, int32_t groups,
+                                           int32_t head_dim, size_t* bytes) {
+  if (bytes == nullptr) return jt_fail(JT_ERR_INVALID, "workspace_size: null output");
+  if (num_requests < 1 || total_queries < 1 || num_kv_heads < 1 || groups < 1 ||
+      head_dim < 1)
+    return jt_fail(JT_ERR_INVALID, "workspace_size: invalid geometry");
+  *bytes = make_layout(num_requests, total_queries, num_kv_heads, groups, head_dim).total;
+  return JT_OK;
+}
+
+extern "C" int jt_tree_attn_launch(const JtTreeAttnParams* pp, cudaStream_t stream) {
+  if (pp == nullptr) return jt_fail(JT_ERR_INVALID, "tree_attn: null params");
+  const JtTreeAttnParams& p = *pp;
+  if (p.num_requests < 1 || p.total_queries < 1 || p.num_kv_heads < 1 || p.groups < 1 ||
+      p.block_size < 1 || p.num_blocks < 1 || p.table_width < 1)
+    return jt_fail(JT_ERR_INVALID, "tree_attn: invalid geometry");
+  if (p.head_dim != 64 && p.head_dim != 128)
+    return jt_fail(JT_ERR_UNSUPPORTED, "tree_attn: head_dim %d not in {64, 128}", p.head_dim);
+  if (p.dtype != JT_BF16 && p.dtype != JT_F16)
+    return jt_fail(JT_ERR_UNSUPPORTED, "tree_attn: operands must be bf16 or f16");
+  if (p.out_dtype != p.dtype && p.out_dtype != JT_F32)
+    return jt_fail(JT_ERR_INVALID, "tree_attn: output dtype must match input or be f32");
+  if (!p.out || !p.q || !p.k_pool || !p.v_pool || !p.cu_seqlens_q || !p.query_to_request ||
+      !p.query_local_row || !p.prefix_lens || !p.node_counts || !p.block_tables ||
+      !p.tree_slots || !p.qq_bias || !p.qq_bias_offsets)
+    return jt_fail(JT_ERR_INVALID, "tree_attn: null tensor pointer");
+  if (!al16(p.q) || !al16(p.k_pool) || !al16(p.v_pool) || !al16(p.out) ||
+      (p.q_stride0 | p.q_stride1 | p.k_stride0 | p.k_stride1 | p.k_stride2 | p.v_stride0 |
+       p.v_stride1 | p.v_stride2) % 8 != 0 ||
+      (p.out_stride0 | p.out_stride1) % 2 != 0)
+    return jt_fail(JT_ERR_INVALID,
+                   "tree_attn: q/k/v need 16-byte aligned bases and rows (strides multiple "
+                   "of 8 elements); out strides must be even");
+  if (p.split_keys < 0 ||
+      (p.split_keys > 0 && (p.split_keys % 1024 != 0 ||
+                            ((p.split_keys / 1024) & (p.split_keys / 1024 - 1)) != 0)))
+    return jt_fail(JT_ERR_INVALID,
+                   "tree_attn: split_keys must be 0 or 1024 times a power of two");
+  const Layout L =
+      make_layout(p.num_requests, p.total_queries, p.num_kv_heads, p.groups, p.head_dim);
+  if (p.workspace == nullptr || p.workspace_bytes < L.total || !al16(p.workspace))
+    return jt_fail(JT_ERR_WORKSPACE, "tree_attn: workspace of %zu bytes required (got %zu)",
+                   L.total, p.workspace_bytes);
+  const DevLayout d = device_layout(L, p.workspace);
+  if (p.dtype == JT_BF16)
+    return p.head_dim == 128 ? dispatch_bm<__nv_bfloat16, 128>(p, L, d, stream)
+                             : dispatch_bm<__nv_bfloat16, 64>(p, L, d, stream);
+  return p.head_dim == 128 ? dispatch_bm<__half, 128>(p, L, d, stream)
+                           : dispatch_bm<__half, 64>(p, L, d, stream);
+}

@@ -1,0 +1,281 @@
+"""Packed ragged tree-verification metadata: the attention kernel's input contract.
+
+Mirrors ``PackedTreeMetadata`` of the reference
+(nanovllm/speculative/jetspec/packed_metadata.py:16-237): the same device fields with the
+same dtypes and layouts, the same host tuples, and the same validation rules, so that
+objects of either class can be passed to the kernels here.  Only tree nodes are packed:
+each request keeps its own prefix page table, node slots and ancestor matrix.
+
+Device fields (R requests, Q = sum of node counts):
+  cu_seqlens_q i32[R+1], query_to_request i32[Q], query_local_row i32[Q],
+  prefix_lens i32[R], block_tables i32[R, W] padded with -1 (W >= 1),
+  tree_slots i64[Q], qq_bias f32[sum T_r^2] (0 visible / -inf hidden, row-major per
+  request), qq_bias_offsets i64[R+1], node_counts i32[R].
+"""
+from __future__ import annotations
+
+from dataclasses import dataclass
+from typing import Sequence
+
+import numpy as np
+import torch
+
+
+def ancestor_mask_from_parents(parents: Sequence[int]) -> np.ndarray:
+    """Boolean [T, T] matrix: row j marks node j and every ancestor of j.
+
+    ``parents[0]`` must be -1 (the root) and every other parent must precede its
+    child, which is the topological order the kernels rely on.
+    """
+    count = len(parents)
+    if count < 1 or int(parents[0]) != -1:
+        raise ValueError("a tree needs a root at index 0 with parent -1")
+    mask = np.zeros((count, count), dtype=bool)
+    mask[0, 0] = True
+    for node in range(1, count):
+        parent = int(parents[node])
+        if not 0 <= parent < node:
+            raise ValueError("tree parents must precede their children")
+        mask[node] = mask[parent]
+        mask[node, node] = True
+    return mask
+
+
+def _bias_rows(mask: np.ndarray) -> np.ndarray:
+    return np.where(mask, np.float32(0.0), np.float32(-np.inf)).astype(np.float32).reshape(-1)
+
+
+@dataclass(frozen=True)
+class PackedTreeMetadata:
+    cu_seqlens_q: torch.Tensor
+    query_to_request: torch.Tensor
+    query_local_row: torch.Tensor
+    prefix_lens: torch.Tensor
+    block_tables: torch.Tensor
+    tree_slots: torch.Tensor
+    qq_bias: torch.Tensor
+    qq_bias_offsets: torch.Tensor
+    node_counts: torch.Tensor
+    block_size: int
+    prefix_lengths: tuple[int, ...]
+    query_offsets: tuple[int, ...]
+    node_counts_host: tuple[int, ...]
+    block_tables_host: tuple[tuple[int, ...], ...]
+    tree_slot_ids: tuple[int, ...]
+    request_ids: tuple
+
+    # ---- construction -------------------------------------------------------------------
+    @classmethod
+    def build(cls, prefix_lens, block_tables, tree_slots, ancestor_masks, block_size, *,
+              request_ids=None) -> "PackedTreeMetadata":
+        """Validate host-side once and build the compact device buffers.
+
+        Follows PackedTreeMetadata.build (packed_metadata.py:35-126): rejects
+        non-tight page tables, malformed or non-causal ancestor masks, negative or
+        overlapping scratch slots and scratch pages shared with a live prefix.
+        Outputs live on the device of ``tree_slots[0]``.
+        """
+        prefixes = tuple(int(v) for v in prefix_lens)
+        count = len(prefixes)
+        if count < 1 or not (len(block_tables) == len(tree_slots) == len(ancestor_masks) == count):
+            raise ValueError("packed metadata requires equally sized nonempty request lists")
+        block_size = int(block_size)
+        if block_size <= 0 or any(v < 0 for v in prefixes):
+            raise ValueError("invalid packed prefix length or page geometry")
+        ids = tuple(range(count)) if request_ids is None else tuple(request_ids)
+        if len(ids) != count or len(set(ids)) != count:
+            raise ValueError("request IDs must be unique and match the request count")
+        device = tree_slots[0].device
+        tables, slot_lists, masks = [], [], []
+        for prefix, table, slots, ancestors in zip(prefixes, block_tables, tree_slots,
+                                                   ancestor_masks):
+            pages = tuple(int(v) for v in table)
+            if (len(pages) != -(-prefix // block_size) or len(set(pages)) != len(pages)
+                    or any(v < 0 for v in pages)):
+                raise ValueError("prefix block table must be a tight canonical page table")
+            if (slots.ndim != 1 or slots.dtype not in (torch.int32, torch.int64)
+                    or slots.device != device):
+                raise ValueError("tree slots must be integer vectors on one common device")
+            nodes = int(slots.numel())
+            if (nodes < 1 or tuple(ancestors.shape) != (nodes, nodes)
+                    or ancestors.dtype != torch.bool or ancestors.device != device):
+                raise ValueError("ancestor masks must be request-local boolean [nodes,nodes] matrices")
+            mask = ancestors.detach().cpu().numpy()
+            if not mask.diagonal().all() or np.triu(mask, 1).any():
+                raise ValueError("ancestor mask must include self and be causal in local flat order")
+            ids_here = [int(v) for v in slots.detach().cpu().tolist()]
+            if any(v < 0 for v in ids_here):
+                raise ValueError("scratch slot IDs cannot be negative")
+            tables.append(pages)
+            slot_lists.append(ids_here)
+            masks.append(mask)
+        return cls._assemble(prefixes, tables, slot_lists, masks, block_size, ids, device)
+
+    @classmethod
+    def from_host_trees(cls, prefix_lens, block_tables, trees, arena_blocks, block_size, *,
+                        device, request_ids) -> "PackedTreeMetadata":
+        """Serving builder from validated CPU topology and scratch-page ownership.
+
+        Follows PackedTreeMetadata.from_host_trees (packed_metadata.py:128-198): each
+        tree provides ``num_nodes``, ``host_ancestor`` (CPU bool [T, T]),
+        ``host_parents`` and ``host_depths``; node j's scratch slot is the j-th slot of
+        the packed arena pages ``arena_blocks``.
+        """
+        prefixes = tuple(int(v) for v in prefix_lens)
+        tables = tuple(tuple(int(v) for v in table) for table in block_tables)
+        ids = tuple(request_ids)
+        count = len(prefixes)
+        if not count or not (len(tables) == len(trees) == len(ids) == count):
+            raise ValueError("packed metadata request lists must align")
+        if block_size <= 0 or any(v < 0 for v in prefixes) or len(set(ids)) != count:
+            raise ValueError("invalid packed prefix geometry or duplicate request ID")
+        masks = []
+        for prefix, table, tree in zip(prefixes, tables, trees):
+            if (len(table) != -(-prefix // block_size) or len(set(table)) != len(table)
+                    or any(v < 0 for v in table)):
+                raise ValueError("prefix block table must be a tight canonical page table")
+            nodes = int(tree.num_nodes)
+            ancestor = tree.host_ancestor
+            if (ancestor.device.type != "cpu" or ancestor.dtype != torch.bool
+                    or tuple(ancestor.shape) != (nodes, nodes) or nodes < 1):
+                raise ValueError("host ancestor must be a nonempty boolean square matrix")
+            mask = ancestor.numpy()
+            if not mask.diagonal().all() or np.triu(mask, 1).any():
+                raise ValueError("ancestor mask must include self and be locally causal")
+            parents, depths = tree.host_parents, tree.host_depths
+            if len(parents) != nodes or len(depths) != nodes or parents[0] != -1 or depths[0] != 0:
+                raise ValueError("invalid root topology")
+            for node in range(1, nodes):
+                parent = parents[node]
+                if not 0 <= parent < node or depths[node] != depths[parent] + 1:
+                    raise ValueError("tree parent/depth mismatch")
+                expected = mask[parent].copy()
+                expected[node] = True
+                if not np.array_equal(expected, mask[node]):
+                    raise ValueError("ancestor visibility differs from parent topology")
+            masks.append(mask)
+        pages = tuple(int(v) for v in arena_blocks)
+        total = sum(m.shape[0] for m in masks)
+        if len(pages) * block_size < total or len(set(pages)) != len(pages) or any(v < 0 for v in pages):
+            raise ValueError("invalid or insufficient scratch page ownership")
+        if set(pages).intersection(v for table in tables for v in table):
+            raise ValueError("scratch pages overlap a live committed prefix")
+        flat = [pages[j // block_size] * block_size + j % block_size for j in range(total)]
+        slot_lists, cursor = [], 0
+        for mask in masks:
+            slot_lists.append(flat[cursor:cursor + mask.shape[0]])
+            cursor += mask.shape[0]
+        return cls._assemble(prefixes, tables, slot_lists, masks, int(block_size), ids,
+                             torch.device(device), validate_slots=False)
+
+    @classmethod
+    def from_parents(cls, prefix_lens, block_tables, parents, tree_slots, block_size, *,
+                     device, request_ids=None) -> "PackedTreeMetadata":
+        """Convenience builder from per-request parent lists and integer slot lists."""
+        prefixes = tuple(int(v) for v in prefix_lens)
+        if not (len(prefixes) == len(block_tables) == len(parents) == len(tree_slots)) or not prefixes:
+            raise ValueError("packed metadata requires equally sized nonempty request lists")
+        ids = tuple(range(len(prefixes))) if request_ids is None else tuple(request_ids)
+        tables = []
+        for prefix, table in zip(prefixes, block_tables):
+            pages = tuple(int(v) for v in table)
+            if (len(pages) != -(-prefix // int(block_size)) or len(set(pages)) != len(pages)
+                    or any(v < 0 for v in pages)):
+                raise ValueError("prefix block table must be a tight canonical page table")
+            tables.append(pages)
+        masks = [ancestor_mask_from_parents(p) for p in parents]
+        slot_lists = [[int(v) for v in slots] for slots in tree_slots]
+        for mask, slots in zip(masks, slot_lists):
+            if len(slots) != mask.shape[0]:
+                raise ValueError("one scratch slot per tree node is required")
+            if any(v < 0 for v in slots):
+                raise ValueError("scratch slot IDs cannot be negative")
+        return cls._assemble(prefixes, tables, slot_lists, masks, int(block_size), ids,
+                             torch.device(device))
+
+    @classmethod
+    def _assemble(cls, prefixes, tables, slot_lists, masks, block_size, ids, device, *,
+                  validate_slots=True):
+        counts = [m.shape[0] for m in masks]
+        all_slots = [v for slots in slot_lists for v in slots]
+        if validate_slots:
+            if len(set(all_slots)) != len(all_slots):
+                raise ValueError("packed requests have overlapping scratch slot ranges")
+            live = {v for table in tables for v in table}
+            if any(v // block_size in live for v in all_slots):
+                raise ValueError("scratch pages overlap a live committed prefix")
+        offsets = np.concatenate(([0], np.cumsum(counts))).astype(np.int64)
+        bias_sizes = np.asarray([c * c for c in counts], dtype=np.int64)
+        bias_offsets = np.concatenate(([0], np.cumsum(bias_sizes))).astype(np.int64)
+        width = max(1, max(len(t) for t in tables))
+        padded = np.full((len(tables), width), -1, dtype=np.int32)
+        for row, table in enumerate(tables):
+            padded[row, :len(table)] = table
+        q_req = np.repeat(np.arange(len(counts), dtype=np.int32), counts)
+        q_row = np.concatenate([np.arange(c, dtype=np.int32) for c in counts])
+        bias = np.concatenate([_bias_rows(m) for m in masks])
+
+        def dev(array, dtype):
+            return torch.from_numpy(np.ascontiguousarray(array)).to(dtype=dtype).to(device)
+
+        return cls(
+            cu_seqlens_q=dev(offsets, torch.int32),
+            query_to_request=dev(q_req, torch.int32),
+            query_local_row=dev(q_row, torch.int32),
+            prefix_lens=dev(np.asarray(prefixes, dtype=np.int64), torch.int32),
+            block_tables=dev(padded, torch.int32),
+            tree_slots=dev(np.asarray(all_slots, dtype=np.int64), torch.int64),
+            qq_bias=dev(bias, torch.float32),
+            qq_bias_offsets=dev(bias_offsets, torch.int64),
+            node_counts=dev(np.asarray(counts, dtype=np.int64), torch.int32),
+            block_size=block_size,
+            prefix_lengths=tuple(prefixes),
+            query_offsets=tuple(int(v) for v in offsets),
+            node_counts_host=tuple(counts),
+            block_tables_host=tuple(tuple(t) for t in tables),
+            tree_slot_ids=tuple(all_slots),
+            request_ids=tuple(ids),
+        )
+
+    # ---- queries ------------------------------------------------------------------------
+    @property
+    def num_requests(self) -> int:
+        return len(self.prefix_lengths)
+
+    @property
+    def total_queries(self) -> int:
+        return self.query_offsets[-1]
+
+    @property
+    def mask_elements(self) -> int:
+        return int(self.qq_bias.numel())
+
+    def request_slice(self, index: int) -> slice:
+        if index < 0 or index >= self.num_requests:
+            raise IndexError("packed request index is out of range")
+        return slice(self.query_offsets[index], self.query_offsets[index + 1])
+
+    def validate_pool_geometry(self, kv_pool: torch.Tensor) -> None:
+        """Host-only bounds check of tables and slots against a 6-D KV pool."""
+        if kv_pool.ndim != 6 or kv_pool.shape[0] != 2 or kv_pool.shape[3] != self.block_size:
+            raise ValueError("packed metadata and KV pool page geometry differ")
+        if kv_pool.device != self.tree_slots.device:
+            raise ValueError("packed metadata and KV pool must be on the same device")
+        pages = int(kv_pool.shape[2])
+        if any(page >= pages for table in self.block_tables_host for page in table):
+            raise ValueError("prefix page lies outside the KV pool")
+        if any(slot >= pages * self.block_size for slot in self.tree_slot_ids):
+            raise ValueError("tree slot lies outside the KV pool")
+
+    def report(self) -> dict:
+        tensors = (self.cu_seqlens_q, self.query_to_request, self.query_local_row,
+                   self.prefix_lens, self.block_tables, self.tree_slots, self.qq_bias,
+                   self.qq_bias_offsets, self.node_counts)
+        return {"requests": self.num_requests, "total_queries": self.total_queries,
+                "cu_seqlens_q": list(self.query_offsets),
+                "prefix_lengths": list(self.prefix_lengths),
+                "node_counts": list(self.node_counts_host), "mask_elements": self.mask_elements,
+                "total_query_square_not_allocated": self.total_queries ** 2,
+                "device_metadata_bytes": sum(t.numel() * t.element_size() for t in tensors),
+                "block_size": self.block_size,
+                "numerical_contract": "fp32_online_softmax_tile64"}
