@@ -4,9 +4,10 @@
  * Everything here is plain C: POD parameter structs holding device pointers, element
  * strides and sizes, plus a cudaStream_t.  No PyTorch (or other framework) type
  * appears in any signature.  Every launcher enqueues work on the given stream and
- * returns immediately: it never synchronises, never allocates device memory and is
- * safe to call inside CUDA-graph stream capture.  Return value: JT_OK (0) or a
- * negative JT_ERR_* code; jt_last_error() then holds a one-line message (thread-local).
+ * returns immediately: it never synchronises and never allocates device memory.
+ * jt_tree_attn_launch, jt_kv_store_launch and jt_kv_commit_launch may be called inside
+ * CUDA-graph stream capture.  Return value: JT_OK (0) or a negative JT_ERR_* code;
+ * jt_last_error() then holds a one-line message (thread-local).
  *
  * Paths below are relative to the nano-vllm-jetspec reference project.
  */
@@ -100,6 +101,26 @@ int jt_tree_attn_workspace_size(int32_t num_requests, int32_t total_queries,
                                 size_t* bytes);
 
 int jt_tree_attn_launch(const JtTreeAttnParams* params, cudaStream_t stream);
+
+/*
+ * jt_tree_attn_launch without a caller-provided workspace: it allocates nothing.
+ * No counterpart in the reference (which always allocates through PyTorch).
+ *
+ * For callers that cannot allocate device memory: a host that binds only this C ABI
+ * and owns all device memory through its own fixed arenas can pass the tensors it holds
+ * but has no allocator to obtain scratch from.  The scratch comes from one file-scope
+ * device array of 32 MiB (every GPU that loads the library holds it until exit); the
+ * split-KV partial results are confined to 16 MiB of it, so the device plan uses
+ * coarser splits than jt_tree_attn_launch.  Geometries whose scratch exceeds 32 MiB
+ * are rejected with JT_ERR_WORKSPACE.  `workspace` / `workspace_bytes` are ignored.
+ *
+ * The first call on a device looks up the array's device address
+ * (cudaGetSymbolAddress with that device current); make that first call before any
+ * stream capture.  All calls share the array and the plan kernel re-initialises what
+ * must start at zero on every call, but calls that overlap on the GPU (different
+ * streams, or concurrent graph replays) race on it: serialise them.
+ */
+int jt_tree_attn_launch_noalloc(const JtTreeAttnParams* params, cudaStream_t stream);
 
 /*
  * Paged KV store: for token i with slot s = slot_mapping[i] (skipped when s < 0),

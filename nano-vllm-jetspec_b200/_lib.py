@@ -24,6 +24,7 @@ JT_FLAG_FP32_PROBABILITY = 1
 EXPORTED_SYMBOLS = (
     "jt_tree_attn_workspace_size",
     "jt_tree_attn_launch",
+    "jt_tree_attn_launch_noalloc",
     "jt_kv_store_launch",
     "jt_kv_commit_launch",
     "jt_kv_commit_max_slots",
@@ -102,6 +103,8 @@ def _declare(lib):
     lib.jt_tree_attn_workspace_size.restype = ctypes.c_int
     lib.jt_tree_attn_launch.argtypes = [P(JtTreeAttnParams), c_void_p]
     lib.jt_tree_attn_launch.restype = ctypes.c_int
+    lib.jt_tree_attn_launch_noalloc.argtypes = [P(JtTreeAttnParams), c_void_p]
+    lib.jt_tree_attn_launch_noalloc.restype = ctypes.c_int
     lib.jt_kv_store_launch.argtypes = [P(JtKvStoreParams), c_void_p]
     lib.jt_kv_store_launch.restype = ctypes.c_int
     lib.jt_kv_commit_launch.argtypes = [P(JtKvCommitParams), c_void_p]

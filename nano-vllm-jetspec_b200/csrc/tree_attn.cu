@@ -54,14 +54,15 @@ int choose_bm(int32_t num_requests, int32_t total_queries, int32_t groups) {
   return static_cast<int64_t>(total_queries) * groups >= 128ll * num_requests ? 128 : 64;
 }
 
-Layout make_layout(int32_t R, int32_t Q, int32_t H, int32_t G, int32_t D) {
+Layout make_layout(int32_t R, int32_t Q, int32_t H, int32_t G, int32_t D,
+                   int64_t partial_budget = kPartialBudgetBytes) {
   Layout L{};
   L.bm = choose_bm(R, Q, G);
   L.mask_words = static_cast<int>(std::min<int64_t>((std::max<int32_t>(Q, 1) + 31) / 32,
                                                     kMaxMaskWords));
   const int64_t mblocks_bound = (static_cast<int64_t>(Q) * G) / L.bm + R;
   const int64_t per_slot = static_cast<int64_t>(L.bm) * D * 4;
-  int64_t slots = std::min<int64_t>(4 * mblocks_bound * H, kPartialBudgetBytes / per_slot);
+  int64_t slots = std::min<int64_t>(4 * mblocks_bound * H, partial_budget / per_slot);
   slots = std::max<int64_t>(slots, 1);
   L.max_slots = static_cast<int>(slots);
   L.max_items = static_cast<int>(mblocks_bound * H + slots);
@@ -725,9 +726,10 @@ extern "C" int jt_tree_attn_workspace_size(int32_t num_requests, int32_t total_q
   return JT_OK;
 }
 
-extern "C" int jt_tree_attn_launch(const JtTreeAttnParams* pp, cudaStream_t stream) {
-  if (pp == nullptr) return jt_fail(JT_ERR_INVALID, "tree_attn: null params");
-  const JtTreeAttnParams& p = *pp;
+namespace {
+
+// Checks every launch argument except the workspace (shared by both entry points).
+int validate_params(const JtTreeAttnParams& p) {
   if (p.num_requests < 1 || p.total_queries < 1 || p.num_kv_heads < 1 || p.groups < 1 ||
       p.block_size < 1 || p.num_blocks < 1 || p.table_width < 1)
     return jt_fail(JT_ERR_INVALID, "tree_attn: invalid geometry");
@@ -753,8 +755,14 @@ extern "C" int jt_tree_attn_launch(const JtTreeAttnParams* pp, cudaStream_t stre
                             ((p.split_keys / 1024) & (p.split_keys / 1024 - 1)) != 0)))
     return jt_fail(JT_ERR_INVALID,
                    "tree_attn: split_keys must be 0 or 1024 times a power of two");
-  const Layout L =
-      make_layout(p.num_requests, p.total_queries, p.num_kv_heads, p.groups, p.head_dim);
+  return JT_OK;
+}
+
+// Plans and launches with a workspace laid out for `partial_budget` bytes of split-KV
+// partial results (the plan coarsens splits to stay within it).
+int run_tree_attn(const JtTreeAttnParams& p, int64_t partial_budget, cudaStream_t stream) {
+  const Layout L = make_layout(p.num_requests, p.total_queries, p.num_kv_heads, p.groups,
+                               p.head_dim, partial_budget);
   if (p.workspace == nullptr || p.workspace_bytes < L.total || !al16(p.workspace))
     return jt_fail(JT_ERR_WORKSPACE, "tree_attn: workspace of %zu bytes required (got %zu)",
                    L.total, p.workspace_bytes);
@@ -764,4 +772,70 @@ extern "C" int jt_tree_attn_launch(const JtTreeAttnParams* pp, cudaStream_t stre
                              : dispatch_bm<__nv_bfloat16, 64>(p, L, d, stream);
   return p.head_dim == 128 ? dispatch_bm<__half, 128>(p, L, d, stream)
                            : dispatch_bm<__half, 64>(p, L, d, stream);
+}
+
+}  // namespace
+
+extern "C" int jt_tree_attn_launch(const JtTreeAttnParams* pp, cudaStream_t stream) {
+  if (pp == nullptr) return jt_fail(JT_ERR_INVALID, "tree_attn: null params");
+  const int rc = validate_params(*pp);
+  if (rc != JT_OK) return rc;
+  return run_tree_attn(*pp, kPartialBudgetBytes, stream);
+}
+
+// ---- entry point without allocation ------------------------------------------------
+// Some callers cannot allocate device memory: an engine that binds this library only
+// through its C ABI and owns every byte of device memory through its own fixed arenas
+// (a cgo / JNI / ctypes host with a frozen memory budget) can pass the tensors it holds
+// but has no allocator to hand out a workspace.  jt_tree_attn_launch_noalloc serves them
+// from this file-scope device array instead.  Every GPU that loads the library holds it
+// until the process exits.
+namespace {
+
+constexpr size_t kStaticWorkspaceBytes = 32u << 20;     // per device
+constexpr int64_t kStaticPartialBudget = 16ll << 20;    // split-KV partials within it
+
+__device__ __align__(256) unsigned char g_static_workspace[kStaticWorkspaceBytes];
+
+// Device address of g_static_workspace on each device.  In host code the symbol names
+// a host-side stand-in, not device memory, so the address comes from
+// cudaGetSymbolAddress with that device current.
+void* g_static_workspace_ptr[64];
+
+int static_workspace(void** out) {
+  int dev = 0;
+  int rc = jt_cuda_check(cudaGetDevice(&dev), "cudaGetDevice");
+  if (rc != JT_OK) return rc;
+  if (dev < 0 || dev >= 64) return jt_fail(JT_ERR_UNSUPPORTED, "device index %d >= 64", dev);
+  if (g_static_workspace_ptr[dev] == nullptr) {
+    void* ptr = nullptr;
+    rc = jt_cuda_check(cudaGetSymbolAddress(&ptr, g_static_workspace),
+                       "cudaGetSymbolAddress(static workspace)");
+    if (rc != JT_OK) return rc;
+    g_static_workspace_ptr[dev] = ptr;
+  }
+  *out = g_static_workspace_ptr[dev];
+  return JT_OK;
+}
+
+}  // namespace
+
+extern "C" int jt_tree_attn_launch_noalloc(const JtTreeAttnParams* pp, cudaStream_t stream) {
+  if (pp == nullptr) return jt_fail(JT_ERR_INVALID, "tree_attn_noalloc: null params");
+  int rc = validate_params(*pp);
+  if (rc != JT_OK) return rc;
+  const Layout L = make_layout(pp->num_requests, pp->total_queries, pp->num_kv_heads,
+                               pp->groups, pp->head_dim, kStaticPartialBudget);
+  if (L.total > kStaticWorkspaceBytes)
+    return jt_fail(JT_ERR_WORKSPACE,
+                   "tree_attn_noalloc: this geometry needs %zu bytes of scratch, above the "
+                   "static capacity of %zu bytes; use jt_tree_attn_launch with a workspace",
+                   L.total, kStaticWorkspaceBytes);
+  void* scratch = nullptr;
+  rc = static_workspace(&scratch);
+  if (rc != JT_OK) return rc;
+  JtTreeAttnParams p = *pp;
+  p.workspace = scratch;
+  p.workspace_bytes = kStaticWorkspaceBytes;
+  return run_tree_attn(p, kStaticPartialBudget, stream);
 }
