@@ -36,6 +36,7 @@ enum JtDtype { JT_BF16 = 0, JT_F16 = 1, JT_F32 = 2 };
 
 /* Flags for JtTreeAttnParams.flags */
 #define JT_FLAG_FP32_PROBABILITY 1u  /* PV with near-fp32 probabilities (hi+lo bf16 split)  */
+#define JT_FLAG_PORTABLE_CORE 2u     /* force the warp-level mma.sync core (A/B testing)     */
 
 /*
  * Packed ragged tree attention over a paged KV cache.
@@ -183,7 +184,8 @@ int32_t jt_abi_version(void);
 const char* jt_last_error(void);
 /* Reads and clears the device-side error word of the current device (synchronises;
  * diagnostics only).  Bit 0: a slot/page index outside the pool was skipped;
- * bit 1: a tree larger than the kernel's mask capacity was skipped. */
+ * bit 1: a tree larger than the kernel's mask capacity was skipped; bit 2: a bounded
+ * pipeline wait ran out (the launch's output is invalid). */
 int jt_read_device_errors(uint32_t* errors);
 
 #ifdef __cplusplus

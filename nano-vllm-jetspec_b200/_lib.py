@@ -20,6 +20,7 @@ JT_ERR_UNSUPPORTED = -4
 
 JT_BF16, JT_F16, JT_F32 = 0, 1, 2
 JT_FLAG_FP32_PROBABILITY = 1
+JT_FLAG_PORTABLE_CORE = 2
 
 EXPORTED_SYMBOLS = (
     "jt_tree_attn_workspace_size",

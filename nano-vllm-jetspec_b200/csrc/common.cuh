@@ -21,6 +21,7 @@ int jt_read_errors_attn(uint32_t* bits);
 
 #define JT_DEVERR_OUT_OF_RANGE 1u
 #define JT_DEVERR_TREE_TOO_LARGE 2u
+#define JT_DEVERR_TIMEOUT 4u
 
 // ---- device helpers ----------------------------------------------------------------
 namespace jt {

@@ -20,7 +20,11 @@
 //                      softmax in fp32 registers.  Items of split requests write
 //                      unnormalised partials; the last CTA of a (request, head,
 //                      m-block) merges them (counter in the workspace).
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
 #include <algorithm>
+#include <type_traits>
 
 #include "common.cuh"
 
@@ -55,9 +59,9 @@ int choose_bm(int32_t num_requests, int32_t total_queries, int32_t groups) {
 }
 
 Layout make_layout(int32_t R, int32_t Q, int32_t H, int32_t G, int32_t D,
-                   int64_t partial_budget = kPartialBudgetBytes) {
+                   int64_t partial_budget = kPartialBudgetBytes, int bm = 0) {
   Layout L{};
-  L.bm = choose_bm(R, Q, G);
+  L.bm = bm > 0 ? bm : choose_bm(R, Q, G);
   L.mask_words = static_cast<int>(std::min<int64_t>((std::max<int32_t>(Q, 1) + 31) / 32,
                                                     kMaxMaskWords));
   const int64_t mblocks_bound = (static_cast<int64_t>(Q) * G) / L.bm + R;
@@ -641,6 +645,8 @@ __global__ void __launch_bounds__(WARPS * 32)
   }
 }
 
+#include "attn_tcgen05.cuh"
+
 // ---- host side ----------------------------------------------------------------------
 struct DeviceInfo {
   int sms = 0;
@@ -704,6 +710,94 @@ int dispatch_bm(const JtTreeAttnParams& p, const Layout& L, const DevLayout& d,
 
 bool al16(const void* ptr) { return (reinterpret_cast<uintptr_t>(ptr) & 15u) == 0; }
 
+// ---- tcgen05 path -------------------------------------------------------------------
+constexpr int kTcItemRows = 2 * tc::kM;  // score rows per tcgen05 work item
+
+PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  if (fn == nullptr) {
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult query{};
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &query) ==
+            cudaSuccess &&
+        query == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(ptr);
+  }
+  return fn;
+}
+
+// 4-D map over a paged pool [blocks, block_size, kv_heads, 128] (strides in elements) with
+// a 64-dim x 64-token box and the 128-byte swizzle of the MMA operand layout.
+bool encode_pool_map(CUtensorMap* map, const void* pool, int32_t dtype, int64_t blocks,
+                     int32_t block_size, int32_t heads, int64_t s0, int64_t s1, int64_t s2) {
+  auto encode = tensor_map_encoder();
+  if (encode == nullptr) return false;
+  const cuuint64_t dims[4] = {static_cast<cuuint64_t>(tc::kD), static_cast<cuuint64_t>(heads),
+                              static_cast<cuuint64_t>(block_size),
+                              static_cast<cuuint64_t>(blocks)};
+  const cuuint64_t strides[3] = {static_cast<cuuint64_t>(s2 * 2), static_cast<cuuint64_t>(s1 * 2),
+                                 static_cast<cuuint64_t>(s0 * 2)};
+  const cuuint32_t box[4] = {64, 1, static_cast<cuuint32_t>(tc::kN), 1};
+  const cuuint32_t elem[4] = {1, 1, 1, 1};
+  const CUresult rc = encode(map,
+                             dtype == JT_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
+                                              : CU_TENSOR_MAP_DATA_TYPE_FLOAT16,
+                             4, const_cast<void*>(pool), dims, strides, box, elem,
+                             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                             CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return rc == CUDA_SUCCESS;
+}
+
+// The tcgen05 core covers head_dim 128, pages that hold whole 64-key tiles and outputs
+// whose rows allow 16-byte stores; anything else runs on the portable core.
+bool tcgen05_eligible(const JtTreeAttnParams& p) {
+  if (p.flags & JT_FLAG_PORTABLE_CORE) return false;
+  if (p.head_dim != tc::kD || p.block_size % tc::kN != 0) return false;
+  if ((p.out_stride0 | p.out_stride1) % 8 != 0) return false;
+  int dev = 0, major = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return false;
+  if (cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev) != cudaSuccess)
+    return false;
+  return major == 10 && tensor_map_encoder() != nullptr;
+}
+
+template <typename Elem, bool FP32P>
+int launch_tc(const JtTreeAttnParams& p, const Layout& L, const DevLayout& d,
+              const CUtensorMap& kmap, const CUtensorMap& vmap, cudaStream_t stream) {
+  auto kernel = tc::tree_attn_tc_kernel<Elem, FP32P>;
+  int rc = jt_cuda_check(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                              tc::kSmemBytes),
+                         "tcgen05 attention smem attribute");
+  if (rc != JT_OK) return rc;
+  int sms = 0;
+  rc = device_sms(&sms);
+  if (rc != JT_OK) return rc;
+  const int plan_blocks = 1 + (p.total_queries + kPlanThreads / 32 - 1) / (kPlanThreads / 32);
+  tree_plan_kernel<<<plan_blocks, kPlanThreads, 0, stream>>>(p, d, sms);
+  rc = jt_cuda_check(cudaGetLastError(), "plan launch");
+  if (rc != JT_OK) return rc;
+  const int grid = std::min(sms, L.max_items);
+  kernel<<<grid, tc::kThreads, tc::kSmemBytes, stream>>>(p, d, kmap, vmap);
+  return jt_cuda_check(cudaGetLastError(), "tcgen05 attention launch");
+}
+
+int dispatch_tc(const JtTreeAttnParams& p, const Layout& L, const DevLayout& d,
+                cudaStream_t stream) {
+  CUtensorMap kmap, vmap;
+  if (!encode_pool_map(&kmap, p.k_pool, p.dtype, p.num_blocks, p.block_size, p.num_kv_heads,
+                       p.k_stride0, p.k_stride1, p.k_stride2) ||
+      !encode_pool_map(&vmap, p.v_pool, p.dtype, p.num_blocks, p.block_size, p.num_kv_heads,
+                       p.v_stride0, p.v_stride1, p.v_stride2))
+    return jt_fail(JT_ERR_CUDA, "tree_attn: cuTensorMapEncodeTiled rejected the KV pool layout");
+  const bool fp32p = (p.flags & JT_FLAG_FP32_PROBABILITY) != 0;
+  if (p.dtype == JT_BF16)
+    return fp32p ? launch_tc<__nv_bfloat16, true>(p, L, d, kmap, vmap, stream)
+                 : launch_tc<__nv_bfloat16, false>(p, L, d, kmap, vmap, stream);
+  return fp32p ? launch_tc<__half, true>(p, L, d, kmap, vmap, stream)
+               : launch_tc<__half, false>(p, L, d, kmap, vmap, stream);
+}
+
 }  // namespace
 
 int jt_read_errors_attn(uint32_t* bits) {
@@ -722,7 +816,12 @@ extern "C" int jt_tree_attn_workspace_size(int32_t num_requests, int32_t total_q
   if (num_requests < 1 || total_queries < 1 || num_kv_heads < 1 || groups < 1 ||
       head_dim < 1)
     return jt_fail(JT_ERR_INVALID, "workspace_size: invalid geometry");
-  *bytes = make_layout(num_requests, total_queries, num_kv_heads, groups, head_dim).total;
+  size_t total = make_layout(num_requests, total_queries, num_kv_heads, groups, head_dim).total;
+  if (head_dim == tc::kD)
+    total = std::max(total, make_layout(num_requests, total_queries, num_kv_heads, groups,
+                                        head_dim, kPartialBudgetBytes, kTcItemRows)
+                                .total);
+  *bytes = total;
   return JT_OK;
 }
 
@@ -761,12 +860,14 @@ int validate_params(const JtTreeAttnParams& p) {
 // Plans and launches with a workspace laid out for `partial_budget` bytes of split-KV
 // partial results (the plan coarsens splits to stay within it).
 int run_tree_attn(const JtTreeAttnParams& p, int64_t partial_budget, cudaStream_t stream) {
+  const bool tc_core = tcgen05_eligible(p);
   const Layout L = make_layout(p.num_requests, p.total_queries, p.num_kv_heads, p.groups,
-                               p.head_dim, partial_budget);
+                               p.head_dim, partial_budget, tc_core ? kTcItemRows : 0);
   if (p.workspace == nullptr || p.workspace_bytes < L.total || !al16(p.workspace))
     return jt_fail(JT_ERR_WORKSPACE, "tree_attn: workspace of %zu bytes required (got %zu)",
                    L.total, p.workspace_bytes);
   const DevLayout d = device_layout(L, p.workspace);
+  if (tc_core) return dispatch_tc(p, L, d, stream);
   if (p.dtype == JT_BF16)
     return p.head_dim == 128 ? dispatch_bm<__nv_bfloat16, 128>(p, L, d, stream)
                              : dispatch_bm<__nv_bfloat16, 64>(p, L, d, stream);
@@ -825,7 +926,8 @@ extern "C" int jt_tree_attn_launch_noalloc(const JtTreeAttnParams* pp, cudaStrea
   int rc = validate_params(*pp);
   if (rc != JT_OK) return rc;
   const Layout L = make_layout(pp->num_requests, pp->total_queries, pp->num_kv_heads,
-                               pp->groups, pp->head_dim, kStaticPartialBudget);
+                               pp->groups, pp->head_dim, kStaticPartialBudget,
+                               tcgen05_eligible(*pp) ? kTcItemRows : 0);
   if (L.total > kStaticWorkspaceBytes)
     return jt_fail(JT_ERR_WORKSPACE,
                    "tree_attn_noalloc: this geometry needs %zu bytes of scratch, above the "

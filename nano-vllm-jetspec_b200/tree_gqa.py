@@ -63,8 +63,12 @@ def _check_metadata(metadata):
 
 
 def launch_tree_attention(out, q, k_pool, v_pool, metadata, scale, groups, *,
-                          fp32_probability=False, split_keys=0):
-    """Fill ``out`` through jt_tree_attn_launch on the current stream (validated args)."""
+                          fp32_probability=False, split_keys=0, portable_core=False):
+    """Fill ``out`` through jt_tree_attn_launch on the current stream (validated args).
+
+    ``portable_core`` forces the warp-level mma.sync core instead of the tcgen05 core
+    (used to cross-check the two kernels); head_dim 64 always runs on it.
+    """
     lib = _lib.load_library()
     if q.shape[-1] not in SUPPORTED_HEAD_DIMS:
         raise ValueError(f"head_dim {q.shape[-1]} is not in {SUPPORTED_HEAD_DIMS}")
@@ -99,7 +103,8 @@ def launch_tree_attention(out, q, k_pool, v_pool, metadata, scale, groups, *,
     p.table_width = int(metadata.block_tables.shape[1])
     p.dtype = _launch.DTYPE_CODES[q.dtype]
     p.out_dtype = _launch.DTYPE_CODES[out.dtype]
-    p.flags = _lib.JT_FLAG_FP32_PROBABILITY if fp32_probability else 0
+    p.flags = ((_lib.JT_FLAG_FP32_PROBABILITY if fp32_probability else 0)
+               | (_lib.JT_FLAG_PORTABLE_CORE if portable_core else 0))
     p.num_blocks = int(k_pool.shape[0])
     p.q_stride0, p.q_stride1 = q.stride(0), q.stride(1)
     p.out_stride0, p.out_stride1 = out.stride(0), out.stride(1)

@@ -69,6 +69,25 @@ def test_reference_backends_use_fp32_probabilities():
     assert_bf16_close(gqa, expected)
 
 
+@pytest.mark.parametrize("prefix", (0, 1, 63, 65, 256, 257, 2048))
+def test_tcgen05_and_portable_cores_agree(prefix):
+    batch = ragged_batch((prefix, max(0, prefix - 1), prefix // 2, prefix + 5),
+                         counts=(63, 31, 47, 128))
+    q, k, v = tensors(batch)
+    meta = batch.metadata(DEVICE)
+    outs = []
+    for portable in (False, True):
+        out = torch.empty(q.shape, dtype=torch.float32, device=DEVICE)
+        tree_gqa.launch_tree_attention(out, q, k, v, meta, batch.head_dim ** -0.5, batch.groups,
+                                       portable_core=portable)
+        outs.append(out)
+    expected = oracle_output(batch, q, k, v)
+    assert_bf16_close(outs[0], expected)
+    assert_bf16_close(outs[1], expected)
+    assert (outs[0] - outs[1]).abs().max().item() < 2e-3
+    assert jb.read_device_errors() == 0
+
+
 @pytest.mark.parametrize("split_keys", (1024, 2048))
 def test_split_kv_partials_match_single_pass(split_keys):
     batch = ragged_batch((4096, 1500, 7000), counts=(64, 17, 128), kv_heads=2)
@@ -80,9 +99,13 @@ def test_split_kv_partials_match_single_pass(split_keys):
     split = torch.empty_like(whole)
     tree_gqa.launch_tree_attention(split, q, k, v, meta, batch.head_dim ** -0.5, batch.groups,
                                    split_keys=split_keys)
+    portable = torch.empty_like(whole)
+    tree_gqa.launch_tree_attention(portable, q, k, v, meta, batch.head_dim ** -0.5, batch.groups,
+                                   split_keys=split_keys, portable_core=True)
     expected = oracle_output(batch, q, k, v)
     assert_bf16_close(whole, expected)
     assert_bf16_close(split, expected)
+    assert_bf16_close(portable, expected)
     assert (whole - split).abs().max().item() < 1e-3
 
 
