@@ -52,6 +52,9 @@ def parse():
     parser.add_argument("--no-cpu-baseline", action="store_true")
     parser.add_argument("--cpu-seconds", type=float, default=12.0,
                         help="CPU-baseline sample budget (seconds of oracle work)")
+    parser.add_argument("--pool-blocks", type=int, default=None,
+                        help="physical pool pages (default: the configuration's 16384 x GPUs); "
+                             "a smaller pool keeps profiler captures small")
     return parser.parse_args()
 
 
@@ -64,9 +67,10 @@ def peaks():
     return dict(PEAKS_FALLBACK, source="fallback")
 
 
-def global_batch(world: int, requests_per_gpu: int):
+def global_batch(world: int, requests_per_gpu: int, pool_blocks=None):
     """config3 statistics with world x requests_per_gpu requests (one seed per rank block)."""
-    return workloads.config3(seed=1003, num_requests=requests_per_gpu * world)
+    return workloads.config3(seed=1003, num_requests=requests_per_gpu * world,
+                             num_blocks=pool_blocks)
 
 
 # ---- clocks ---------------------------------------------------------------------------
@@ -335,7 +339,7 @@ def main():
         torch.distributed.init_process_group("nccl", timeout=timedelta(seconds=300),
                                              device_id=device)
     try:
-        batch = global_batch(world, args.requests_per_gpu)
+        batch = global_batch(world, args.requests_per_gpu, args.pool_blocks)
         shard = shard_for_rank(KV_HEADS, GROUPS, world, rank)
         step = Step(batch, shard, device)
         steps, warmup = max(args.steps, 1), max(args.warmup, 3)

@@ -40,28 +40,34 @@ constexpr int kOffQ = 0;
 constexpr int kOffK = kOffQ + 2 * kQTileBytes;
 constexpr int kOffV = kOffK + kStages * kKVBytes;
 constexpr int kOffBar = kOffV + kStages * kKVBytes;
-constexpr int kNumBars = 2 * kStages + 2 + 4 * 2 + 1;
 constexpr int kOffRows = kOffBar + 8 * 32;              // 64 x (K, V) row byte offsets
+static_assert(8 * 32 >= 8 * 28, "barrier area");
 constexpr int kOffMisc = kOffRows + 64 * 2 * 8;
 constexpr int kSmemBytes = kOffMisc + 64 + 1024;        // + alignment slack
 constexpr long long kWaitLimit = 4000000000ll;          // cycles (~2 s) per wait
 
-// TMEM column map (512 columns x 128 lanes x 32 bit).
-__host__ __device__ constexpr uint32_t col_o(int i) { return 128u * i; }          // O_i: 128 cols
-__host__ __device__ constexpr uint32_t col_s(int i) { return 256u + 64u * i; }    // S_i: 64 cols
-__host__ __device__ constexpr uint32_t col_p(int i) { return 384u + 32u * i; }    // P_i: 32 cols
-__host__ __device__ constexpr uint32_t col_pl(int i) { return 448u + 32u * i; }   // P_i low part
+// TMEM column map (512 columns x 128 lanes x 32 bit): O_i (128 columns) and two S
+// buffers per query tile (64 columns each).  P (operand-type pairs, 32 columns) and, for
+// fp32 probabilities, its low part (32 more) are written over the S buffer they came from.
+__host__ __device__ constexpr uint32_t col_o(int i) { return 128u * i; }
+__host__ __device__ constexpr uint32_t col_s(int i, int b) { return 256u + 128u * i + 64u * b; }
 
 // Barrier indices.
-constexpr int kBarKvFull = 0;
-constexpr int kBarKvEmpty = kStages;
+constexpr int kBarKvFull = 0;                  // [kStages]
+constexpr int kBarKvEmpty = kStages;           // [kStages]
 constexpr int kBarQFull = 2 * kStages;
 constexpr int kBarQEmpty = kBarQFull + 1;
-constexpr int kBarSFull = kBarQEmpty + 1;    // [2]
-constexpr int kBarPFull = kBarSFull + 2;     // [2]
-constexpr int kBarODone = kBarPFull + 2;     // [2]
-constexpr int kBarOFree = kBarODone + 2;     // [2]
-constexpr int kBarDrain = kBarOFree + 2;
+constexpr int kBarSFull = kBarQEmpty + 1;      // [2 tiles][2 buffers]
+constexpr int kBarPFull = kBarSFull + 4;       // [2 tiles][2 buffers], 128 arrivals
+constexpr int kBarPvDone = kBarPFull + 4;      // [2 tiles], one commit per PV
+constexpr int kBarOFree = kBarPvDone + 2;      // [2 tiles], 128 arrivals
+constexpr int kBarItemDone = kBarOFree + 2;    // every MMA of an item completed
+constexpr int kBarDrain = kBarItemDone + 1;
+constexpr int kBarItemFull = kBarDrain + 1;    // [2] work-item ring
+constexpr int kBarItemEmpty = kBarItemFull + 2;  // [2]
+constexpr int kItemConsumers = 12;               // every warp of the CTA reads each item
+constexpr int kLoaderWarps = 3;                  // q_full / kv_full arrivals (one per warp)
+constexpr int kNumBars = kBarItemEmpty + 2;
 
 // ---- PTX wrappers ------------------------------------------------------------------
 __device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
@@ -113,9 +119,6 @@ __device__ __forceinline__ void tc_commit(uint32_t bar) {
   asm volatile(
       "tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];\n" ::"r"(bar)
       : "memory");
-}
-__device__ __forceinline__ void named_sync(int id, int count) {
-  asm volatile("bar.sync %0, %1;\n" ::"r"(id), "r"(count) : "memory");
 }
 
 // Shared-memory matrix descriptor, 128-byte swizzle (sm_100 descriptor version 1).
@@ -244,21 +247,25 @@ __global__ void __launch_bounds__(kThreads, 1)
   const uint32_t raw = jt::smem_u32(smem_raw);
   const uint32_t base = (raw + 1023u) & ~1023u;
   unsigned char* sbase = smem_raw + (base - raw);
-  auto bar = [&](int i) { return base + kOffBar + 8u * static_cast<uint32_t>(i); };
-  int64_t* row_off = reinterpret_cast<int64_t*>(sbase + kOffRows);  // [64][2]
+  const uint32_t bar0 = base + kOffBar;
+#define JT_BAR(i) (bar0 + 8u * static_cast<uint32_t>(i))
   volatile int* misc = reinterpret_cast<volatile int*>(sbase + kOffMisc);
-  // misc[0]: TMEM base, misc[1]: abort, misc[2..3]: split-merge flags
+  // misc[0]: TMEM base, misc[1]: abort, misc[4..5]: item ring
   volatile int* abort = misc + 1;
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   if (tid == 0) {
     for (int i = 0; i < kNumBars; ++i) {
       uint32_t count = 1;
-      if (i == kBarPFull || i == kBarPFull + 1 || i == kBarOFree || i == kBarOFree + 1) count = 128;
-      mbar_init(bar(i), count);
+      if ((i >= kBarPFull && i < kBarPFull + 4) || i == kBarOFree || i == kBarOFree + 1)
+        count = 128;
+      if (i == kBarItemEmpty || i == kBarItemEmpty + 1) count = kItemConsumers;
+      if (i == kBarQFull || (i >= kBarKvFull && i < kBarKvFull + kStages)) count = kLoaderWarps;
+      mbar_init(JT_BAR(i), count);
     }
     misc[1] = 0;
     misc[2] = misc[3] = 0;
+    misc[4] = misc[5] = -1;
     asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
   }
   if (warp == 0) {
@@ -276,88 +283,131 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int split_keys = w.header[2];
   const int G = p.groups, bs = p.block_size;
 
+  // Work items come from the device queue (longest first).  Loader thread 0 takes the
+  // next one and publishes it through a two-entry ring; every warp reads each entry.
+  // Lane 0 of each warp reads the entry and broadcasts it, so a warp always agrees with
+  // itself; after an abort every reader sees -1 and leaves its loop.
+  auto next_item = [&](uint32_t seq) -> int {
+    const int slot = seq & 1;
+    int index = -1;
+    if (lane == 0) {
+      if (mbar_wait(JT_BAR(kBarItemFull + slot), (seq >> 1) & 1, abort) && !*abort)
+        index = misc[4 + slot];
+      mbar_arrive(JT_BAR(kBarItemEmpty + slot));
+    }
+    return __shfl_sync(0xffffffffu, index, 0);
+  };
+
   if (warp == 0) {
     // ------------------------------------------------------------------ MMA issuer
-    if (lane == 0) {
-      uint32_t kv_count = 0, q_count = 0, pf[2] = {0, 0}, of[2] = {0, 0};
-      const uint32_t sq0 = base + kOffQ;
-      for (int index = blockIdx.x; index < num_items; index += gridDim.x) {
-        const Item it = decode(p, w, index, split_keys);
-        mbar_wait(bar(kBarQFull), q_count & 1, abort);
-        ++q_count;
-        tc_fence_after();
-        auto issue_qk = [&](int i, int stage) {
-          const uint32_t qa = sq0 + i * kQTileBytes;
-          const uint32_t ka = base + kOffK + stage * kKVBytes;
+    // Per query tile i and 64-key tile t: S_i[t%2] = Q_i K_t^T, then (after the softmax
+    // wrote P into that buffer) O_i += P V_t.  QK(t+1) is issued as soon as PV(t-1) has
+    // released the buffer, so the softmax of tile t+1 never waits for the PV of tile t.
+    uint32_t kv_count = 0, q_count = 0, items_done = 0;
+    // Phase parities kept as bits: pv_par bit i = parity of the next PV commit of tile i,
+    // pf_par bit (2i+b) = parity of the next p_full phase of buffer b, of_par bit i =
+    // parity of the next o_free phase to wait for, of_seen bit i = tile i used before.
+    uint32_t pv_par = 0, pf_par = 0, of_par = 0, of_seen = 0;
+    for (uint32_t seq = 0;; ++seq) {
+      const int index = next_item(seq);
+      if (index < 0) break;
+      if (lane != 0) continue;
+      const Item it = decode(p, w, index, split_keys);
+      const int nq = it.nq, n_tiles = it.n_tiles;
+      if (items_done > 0) mbar_wait(JT_BAR(kBarItemDone), (items_done - 1) & 1, abort);
+      mbar_wait(JT_BAR(kBarQFull), q_count & 1, abort);
+      ++q_count;
+      tc_fence_after();
+      auto issue_qk = [&](int i, int t, int stage) {
+        const uint32_t qa = base + kOffQ + i * kQTileBytes;
+        const uint32_t ka = base + kOffK + stage * kKVBytes;
 #pragma unroll
-          for (int kk = 0; kk < kD / 16; ++kk) {
-            const uint32_t off = (kk & 3) * 32;
-            const uint64_t a = smem_desc(qa + (kk >> 2) * kQHalfBytes + off, 16, 1024);
-            const uint64_t b = smem_desc(ka + (kk >> 2) * kKVHalfBytes + off, 16, 1024);
-            mma_ss(tmem + col_s(i), a, b, kIdescQK, kk > 0 ? 1u : 0u);
+        for (int kk = 0; kk < kD / 16; ++kk) {
+          const uint32_t off = (kk & 3) * 32;
+          mma_ss(tmem + col_s(i, t & 1), smem_desc(qa + (kk >> 2) * kQHalfBytes + off, 16, 1024),
+                 smem_desc(ka + (kk >> 2) * kKVHalfBytes + off, 16, 1024), kIdescQK,
+                 kk > 0 ? 1u : 0u);
+        }
+        tc_commit(JT_BAR(kBarSFull + 2 * i + (t & 1)));
+      };
+      {
+        const int stage = kv_count % kStages;
+        mbar_wait(JT_BAR(kBarKvFull + stage), (kv_count / kStages) & 1, abort);
+        tc_fence_after();
+        for (int i = 0; i < nq; ++i) issue_qk(i, 0, stage);
+        if (n_tiles == 1) tc_commit(JT_BAR(kBarQEmpty));
+      }
+      for (int t = 0; t < n_tiles; ++t) {
+        const int stage = kv_count % kStages;
+        if (t + 1 < n_tiles) {
+          const int next = (kv_count + 1) % kStages;
+          mbar_wait(JT_BAR(kBarKvFull + next), ((kv_count + 1) / kStages) & 1, abort);
+          for (int i = 0; i < nq; ++i) {
+            // Buffer (t+1)%2 last held P(t-1): wait until PV(t-1) has read it.
+            if (t >= 1) mbar_wait(JT_BAR(kBarPvDone + i), ((pv_par >> i) & 1u) ^ 1u, abort);
+            tc_fence_after();
+            issue_qk(i, t + 1, next);
           }
-          tc_commit(bar(kBarSFull + i));
-        };
-        auto issue_pv = [&](int i, int stage, bool accumulate) {
-          const uint32_t va = base + kOffV + stage * kKVBytes;
+          if (t + 2 == n_tiles) tc_commit(JT_BAR(kBarQEmpty));
+        }
+        const uint32_t va = base + kOffV + stage * kKVBytes;
+        for (int i = 0; i < nq; ++i) {
+          if (t == 0 && ((of_seen >> i) & 1u)) {
+            mbar_wait(JT_BAR(kBarOFree + i), (of_par >> i) & 1u, abort);
+            of_par ^= 1u << i;
+          }
+          const int pb = 2 * i + (t & 1);
+          mbar_wait(JT_BAR(kBarPFull + pb), (pf_par >> pb) & 1u, abort);
+          pf_par ^= 1u << pb;
+          tc_fence_after();
+          const uint32_t pa = tmem + col_s(i, t & 1);
 #pragma unroll
           for (int kk = 0; kk < kN / 16; ++kk) {
             const uint64_t b = smem_desc(va + kk * 2048, kKVHalfBytes, 1024);
-            mma_ts(tmem + col_o(i), tmem + col_p(i) + kk * 8, b, kIdescPV,
-                   (accumulate || kk > 0) ? 1u : 0u);
-            if constexpr (FP32P)
-              mma_ts(tmem + col_o(i), tmem + col_pl(i) + kk * 8, b, kIdescPV, 1u);
+            mma_ts(tmem + col_o(i), pa + kk * 8, b, kIdescPV, (t > 0 || kk > 0) ? 1u : 0u);
+            if constexpr (FP32P) mma_ts(tmem + col_o(i), pa + 32 + kk * 8, b, kIdescPV, 1u);
           }
-          tc_commit(bar(kBarODone + i));
-        };
-        {
-          const int stage = kv_count % kStages;
-          mbar_wait(bar(kBarKvFull + stage), (kv_count / kStages) & 1, abort);
-          tc_fence_after();
-          for (int i = 0; i < it.nq; ++i) issue_qk(i, stage);
-          if (it.n_tiles == 1) tc_commit(bar(kBarQEmpty));
+          tc_commit(JT_BAR(kBarPvDone + i));
+          pv_par ^= 1u << i;
         }
-        for (int t = 0; t < it.n_tiles; ++t) {
-          const int stage = kv_count % kStages;
-          for (int i = 0; i < it.nq; ++i) {
-            if (t == 0 && of[i] > 0) mbar_wait(bar(kBarOFree + i), (of[i] - 1) & 1, abort);
-            mbar_wait(bar(kBarPFull + i), pf[i] & 1, abort);
-            ++pf[i];
-            tc_fence_after();
-            issue_pv(i, stage, t > 0);
-            if (t + 1 < it.n_tiles) {
-              const int next = (kv_count + 1) % kStages;
-              if (i == 0) {
-                mbar_wait(bar(kBarKvFull + next), ((kv_count + 1) / kStages) & 1, abort);
-                tc_fence_after();
-              }
-              issue_qk(i, next);
-              if (t + 2 == it.n_tiles && i == it.nq - 1) tc_commit(bar(kBarQEmpty));
-            }
-          }
-          tc_commit(bar(kBarKvEmpty + stage));
-          ++kv_count;
-        }
-        for (int i = 0; i < it.nq; ++i) ++of[i];
+        tc_commit(JT_BAR(kBarKvEmpty + stage));
+        ++kv_count;
       }
+      tc_commit(JT_BAR(kBarItemDone));
+      ++items_done;
+      for (int i = 0; i < nq; ++i) of_seen |= 1u << i;
+    }
+    if (lane == 0) {
       // Drain: every MMA this thread issued has completed before TMEM is released.
-      tc_commit(bar(kBarDrain));
-      mbar_wait(bar(kBarDrain), 0, abort, false);
+      tc_commit(JT_BAR(kBarDrain));
+      mbar_wait(JT_BAR(kBarDrain), 0, abort, false);
     }
   } else if (warp < 4) {
     // ------------------------------------------------------------------ loaders
     const int ltid = tid - 32;
-    uint32_t kv_count = 0, q_count = 0;
+    uint32_t kv_count = 0;
     uint32_t filled = 0;       // stages whose last fill went through TMA (drain bookkeeping)
     uint32_t last_parity = 0;  // bit s: phase parity of stage s's last TMA fill
     const char* kbase = static_cast<const char*>(p.k_pool);
     const char* vbase = static_cast<const char*>(p.v_pool);
     const int64_t pool_slots = p.num_blocks * static_cast<int64_t>(bs);
-    for (int index = blockIdx.x; index < num_items; index += gridDim.x) {
+    for (uint32_t seq = 0;; ++seq) {
+      if (ltid == 0) {
+        // Publish the next work item (or -1 when the queue is exhausted).
+        const int slot = seq & 1;
+        if (seq >= 2) mbar_wait(JT_BAR(kBarItemEmpty + slot), ((seq >> 1) - 1) & 1, abort);
+        const int index = atomicAdd(&w.header[0], 1);
+        misc[4 + slot] = index < num_items ? index : -1;
+        mbar_arrive(JT_BAR(kBarItemFull + slot));
+      }
+      const int index = next_item(seq);
+      if (index < 0) break;
       const Item it = decode(p, w, index, split_keys);
       const int32_t* table = p.block_tables + static_cast<int64_t>(it.r) * p.table_stride0;
-      // Query tiles (cp.async, swizzled).  Rows past the request's nodes are zero.
-      if (q_count > 0) mbar_wait(bar(kBarQEmpty), (q_count - 1) & 1, abort);
+      // Query tiles (cp.async, swizzled).  Rows past the request's nodes are zero.  Each
+      // loader warp waits for its own copies, fences them for the tensor core (async
+      // proxy) and arrives once.
+      if (seq > 0) mbar_wait(JT_BAR(kBarQEmpty), (seq - 1) & 1, abort);
       const int qrows = it.nq * kM;
       for (int c = ltid; c < qrows * 16; c += 96) {
         const int row = c >> 4, chunk = c & 15;
@@ -373,9 +423,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       asm volatile("cp.async.wait_all;\n" ::: "memory");
       fence_proxy_async();
-      named_sync(2, 96);
-      if (ltid == 0) mbar_arrive(bar(kBarQFull));
-      ++q_count;
+      __syncwarp();
+      if (lane == 0) mbar_arrive(JT_BAR(kBarQFull));
 
       for (int t = 0; t < it.n_tiles; ++t) {
         const int stage = kv_count % kStages;
@@ -384,23 +433,31 @@ __global__ void __launch_bounds__(kThreads, 1)
         const bool full = kb + kN <= min(it.P, it.key_end);
         const uint32_t kdst = base + kOffK + stage * kKVBytes;
         const uint32_t vdst = base + kOffV + stage * kKVBytes;
+        const uint32_t full_bar = JT_BAR(kBarKvFull + stage);
+        // Every loader thread waits for every refill, in order: a parity wait is only
+        // unambiguous while the waiter is at most one phase behind the barrier.
+        const int page = (full && ltid == 0) ? __ldg(table + kb / bs) : 0;
+        if (kv_count >= kStages) mbar_wait(JT_BAR(kBarKvEmpty + stage), parity ^ 1, abort);
         if (full) {
-          if (ltid == 0) {
-            if (kv_count >= kStages) mbar_wait(bar(kBarKvEmpty + stage), parity ^ 1, abort);
-            const int page = __ldg(table + kb / bs);
-            const int off = kb % bs;
-            mbar_arrive_tx(bar(kBarKvFull + stage), 2 * kKVBytes);
-            tma_load_4d(kdst, &kmap, 0, it.h, off, page, bar(kBarKvFull + stage));
-            tma_load_4d(kdst + kKVHalfBytes, &kmap, 64, it.h, off, page, bar(kBarKvFull + stage));
-            tma_load_4d(vdst, &vmap, 0, it.h, off, page, bar(kBarKvFull + stage));
-            tma_load_4d(vdst + kKVHalfBytes, &vmap, 64, it.h, off, page, bar(kBarKvFull + stage));
-            filled |= 1u << stage;
-            last_parity = (last_parity & ~(1u << stage)) | (parity << stage);
+          if (lane == 0) {
+            if (ltid == 0) {
+              const int off = kb % bs;
+              mbar_arrive_tx(full_bar, 2 * kKVBytes);
+              tma_load_4d(kdst, &kmap, 0, it.h, off, page, full_bar);
+              tma_load_4d(kdst + kKVHalfBytes, &kmap, 64, it.h, off, page, full_bar);
+              tma_load_4d(vdst, &vmap, 0, it.h, off, page, full_bar);
+              tma_load_4d(vdst + kKVHalfBytes, &vmap, 64, it.h, off, page, full_bar);
+              filled |= 1u << stage;
+              last_parity = (last_parity & ~(1u << stage)) | (parity << stage);
+            } else {
+              mbar_arrive(full_bar);
+            }
           }
         } else {
-          if (kv_count >= kStages) mbar_wait(bar(kBarKvEmpty + stage), parity ^ 1, abort);
+          // Tile that touches the tree nodes (or a page tail): one key row per thread.
           if (ltid < kN) {
-            const int pos = kb + ltid;
+            const int row = ltid;
+            const int pos = kb + row;
             int64_t ko = -1, vo = -1;
             if (pos < it.key_end) {
               int64_t slot = -1;
@@ -421,23 +478,19 @@ __global__ void __launch_bounds__(kThreads, 1)
                 atomicOr(&g_attn_errors, JT_DEVERR_OUT_OF_RANGE);
               }
             }
-            row_off[2 * ltid] = ko;
-            row_off[2 * ltid + 1] = vo;
-          }
-          named_sync(2, 96);
-          for (int c = ltid; c < kN * 16; c += 96) {
-            const int row = c >> 4, chunk = c & 15;
-            const int64_t ko = row_off[2 * row], vo = row_off[2 * row + 1];
-            const uint32_t o = swz128(row, chunk, kN);
-            jt::cp_async_16(kdst + o, ko >= 0 ? kbase + ko + chunk * 16 : kbase, ko >= 0 ? 16 : 0);
-            jt::cp_async_16(vdst + o, vo >= 0 ? vbase + vo + chunk * 16 : vbase, vo >= 0 ? 16 : 0);
+#pragma unroll
+            for (int chunk = 0; chunk < 16; ++chunk) {
+              const uint32_t o = swz128(row, chunk, kN);
+              jt::cp_async_16(kdst + o, ko >= 0 ? kbase + ko + chunk * 16 : kbase, ko >= 0 ? 16 : 0);
+              jt::cp_async_16(vdst + o, vo >= 0 ? vbase + vo + chunk * 16 : vbase, vo >= 0 ? 16 : 0);
+            }
           }
           asm volatile("cp.async.wait_all;\n" ::: "memory");
           fence_proxy_async();
-          named_sync(2, 96);
-          if (ltid == 0) {
-            mbar_arrive(bar(kBarKvFull + stage));
-            filled &= ~(1u << stage);
+          __syncwarp();
+          if (lane == 0) {
+            mbar_arrive(full_bar);
+            if (ltid == 0) filled &= ~(1u << stage);
           }
         }
         ++kv_count;
@@ -446,7 +499,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     // Drain: the TMA copies this thread issued have landed before the CTA exits.
     if (ltid == 0) {
       for (int s = 0; s < kStages; ++s)
-        if (filled & (1u << s)) mbar_wait(bar(kBarKvFull + s), (last_parity >> s) & 1u, abort, false);
+        if (filled & (1u << s))
+          mbar_wait(JT_BAR(kBarKvFull + s), (last_parity >> s) & 1u, abort, false);
     }
   } else {
     // ------------------------------------------------------------------ softmax + epilogue
@@ -454,44 +508,74 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int t128 = tid - 128 - i * 128;   // row within the query tile
     const uint32_t lane_base = static_cast<uint32_t>((t128 >> 5) * 32) << 16;
     const float scale_log2 = p.scale * 1.4426950408889634f;
-    uint32_t sf = 0, od = 0;
-    for (int index = blockIdx.x; index < num_items; index += gridDim.x) {
+    uint32_t sf_par = 0, pv = 0;  // sf_par bit b: parity of the next s_full phase of buffer b
+    for (uint32_t seq = 0;; ++seq) {
+      const int index = next_item(seq);
+      if (index < 0) break;
       const Item it = decode(p, w, index, split_keys);
       if (i >= it.nq) continue;
       const int gm = it.tp * 2 * kM + i * kM + t128;
       const int j = gm / G, g = gm - j * G;
       const bool row_ok = j < it.T;
+      const bool warp_live = __any_sync(0xffffffffu, row_ok);
       const uint32_t* mask_row =
           w.masks + static_cast<int64_t>(it.q_start + (row_ok ? j : 0)) * w.mask_words;
-      float m_run = -INFINITY, l_run = 0.f;
+      float m_run = -INFINITY;  // running max in log2 units (scaled scores)
+      float l_run = 0.f;
       for (int t = 0; t < it.n_tiles; ++t) {
-        mbar_wait(bar(kBarSFull + i), sf & 1, abort);
-        ++sf;
-        tc_fence_after();
-        uint32_t sraw[2][32];
-        tmem_ld32(tmem + lane_base + col_s(i), sraw[0]);
-        tmem_ld32(tmem + lane_base + col_s(i) + 32, sraw[1]);
-        tmem_wait_ld();
         const int kb = it.key_begin + t * kN;
         const bool full = kb + kN <= min(it.P, it.key_end);
+        // Ancestor bits of this row for the tile's tree keys, fetched before the wait.
+        uint32_t mw0 = 0, mw1 = 0, mw2 = 0;
+        int n_first = 0;
+        if (!full && row_ok) {
+          n_first = kb - it.P;  // node of column 0 (negative while the tile is prefix)
+          const int w0 = n_first >= 0 ? (n_first >> 5) : 0;
+          const int last = min(it.T - 1, n_first + kN - 1);
+          if (last >= 0) {
+            mw0 = __ldg(mask_row + w0);
+            if (w0 + 1 <= (last >> 5)) mw1 = __ldg(mask_row + w0 + 1);
+            if (w0 + 2 <= (last >> 5)) mw2 = __ldg(mask_row + w0 + 2);
+          }
+        }
+        const int buf = t & 1;
+        mbar_wait(JT_BAR(kBarSFull + 2 * i + buf), (sf_par >> buf) & 1u, abort);
+        sf_par ^= 1u << buf;
+        tc_fence_after();
+        const uint32_t s_addr = tmem + lane_base + col_s(i, buf);
+        uint32_t sraw[2][32];
+        tmem_ld32(s_addr, sraw[0]);
+        tmem_ld32(s_addr + 32, sraw[1]);
+        tmem_wait_ld();
         float s[64];
 #pragma unroll
-        for (int c = 0; c < 64; ++c) s[c] = __uint_as_float(sraw[c >> 5][c & 31]) * scale_log2;
+        for (int c = 0; c < 64; ++c) s[c] = __uint_as_float(sraw[c >> 5][c & 31]);
         if (!full) {
+          const int wbase = n_first >= 0 ? (n_first >> 5) : 0;
 #pragma unroll
           for (int c = 0; c < 64; ++c) {
             const int pos = kb + c;
             bool vis = row_ok && pos < it.key_end;
             if (vis && pos >= it.P) {
               const int n = pos - it.P;
-              vis = (__ldg(mask_row + (n >> 5)) >> (n & 31)) & 1u;
+              const int wi = (n >> 5) - wbase;
+              const uint32_t word = wi == 0 ? mw0 : (wi == 1 ? mw1 : mw2);
+              vis = (word >> (n & 31)) & 1u;
             }
             if (!vis) s[c] = -INFINITY;
           }
         }
-        float mx = -INFINITY;
+        // Row max of the raw scores (scale > 0 keeps the order), as a tree.
+        float mx4[4];
 #pragma unroll
-        for (int c = 0; c < 64; ++c) mx = fmaxf(mx, s[c]);
+        for (int q = 0; q < 4; ++q) {
+          float a = fmaxf(s[q * 16 + 0], s[q * 16 + 1]), b = fmaxf(s[q * 16 + 2], s[q * 16 + 3]);
+          float c2 = fmaxf(s[q * 16 + 4], s[q * 16 + 5]), d = fmaxf(s[q * 16 + 6], s[q * 16 + 7]);
+          float e = fmaxf(s[q * 16 + 8], s[q * 16 + 9]), f = fmaxf(s[q * 16 + 10], s[q * 16 + 11]);
+          float g2 = fmaxf(s[q * 16 + 12], s[q * 16 + 13]), h = fmaxf(s[q * 16 + 14], s[q * 16 + 15]);
+          mx4[q] = fmaxf(fmaxf(fmaxf(a, b), fmaxf(c2, d)), fmaxf(fmaxf(e, f), fmaxf(g2, h)));
+        }
+        const float mx = fmaxf(fmaxf(mx4[0], mx4[1]), fmaxf(mx4[2], mx4[3])) * scale_log2;
         // Lazy max: move only when it grows by more than 8 (log2 units).
         float alpha = 1.f;
         bool rescale = false;
@@ -502,53 +586,62 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
           m_run = mx;
         }
-        const float m_use = m_run == -INFINITY ? 0.f : m_run;
-        float rsum = 0.f;
+        const float neg_m = m_run == -INFINITY ? 0.f : -m_run;
         uint32_t ph[32];
         uint32_t pl[FP32P ? 32 : 1];
+        float r4[4] = {0.f, 0.f, 0.f, 0.f};
+        if (warp_live) {
 #pragma unroll
-        for (int c = 0; c < 32; ++c) {
-          const float p0 = jt::fast_exp2(s[2 * c] - m_use);
-          const float p1 = jt::fast_exp2(s[2 * c + 1] - m_use);
-          rsum += p0 + p1;
-          ph[c] = Mma::pack(p0, p1);
-          if constexpr (FP32P) {
-            const float2 r = Mma::unpack(ph[c]);
-            pl[c] = Mma::pack(p0 - r.x, p1 - r.y);
-          }
-        }
-        l_run = l_run * alpha + rsum;
-        if (t > 0) {
-          mbar_wait(bar(kBarODone + i), od & 1, abort);
-          ++od;
-          tc_fence_after();
-          if (__any_sync(0xffffffffu, rescale)) {
-#pragma unroll 1
-            for (int chunk = 0; chunk < 4; ++chunk) {
-              uint32_t o[32];
-              const uint32_t ta = tmem + lane_base + col_o(i) + chunk * 32;
-              tmem_ld32(ta, o);
-              tmem_wait_ld();
-#pragma unroll
-              for (int c = 0; c < 32; ++c) o[c] = __float_as_uint(__uint_as_float(o[c]) * alpha);
-              tmem_st32(ta, o);
+          for (int c = 0; c < 32; ++c) {
+            const float p0 = jt::fast_exp2(fmaf(s[2 * c], scale_log2, neg_m));
+            const float p1 = jt::fast_exp2(fmaf(s[2 * c + 1], scale_log2, neg_m));
+            r4[c & 3] += p0 + p1;
+            ph[c] = Mma::pack(p0, p1);
+            if constexpr (FP32P) {
+              const float2 r = Mma::unpack(ph[c]);
+              pl[c] = Mma::pack(p0 - r.x, p1 - r.y);
             }
           }
+        } else {
+#pragma unroll
+          for (int c = 0; c < 32; ++c) {
+            ph[c] = 0u;
+            if constexpr (FP32P) pl[c] = 0u;
+          }
         }
-        tmem_st32(tmem + lane_base + col_p(i), ph);
+        l_run = l_run * alpha + ((r4[0] + r4[1]) + (r4[2] + r4[3]));
+        // PV(t-1) must be done before O_i is rescaled; it normally is by now.
+        if (t > 0) {
+          mbar_wait(JT_BAR(kBarPvDone + i), pv & 1, abort);
+          ++pv;
+          tc_fence_after();
+        }
+        if (t > 0 && __any_sync(0xffffffffu, rescale)) {
+#pragma unroll 1
+          for (int chunk = 0; chunk < 4; ++chunk) {
+            uint32_t o[32];
+            const uint32_t ta = tmem + lane_base + col_o(i) + chunk * 32;
+            tmem_ld32(ta, o);
+            tmem_wait_ld();
+#pragma unroll
+            for (int c = 0; c < 32; ++c) o[c] = __float_as_uint(__uint_as_float(o[c]) * alpha);
+            tmem_st32(ta, o);
+          }
+        }
+        tmem_st32(s_addr, ph);
         if constexpr (FP32P) {
           uint32_t lo[32];
 #pragma unroll
           for (int c = 0; c < 32; ++c) lo[c] = pl[c];
-          tmem_st32(tmem + lane_base + col_pl(i), lo);
+          tmem_st32(s_addr + 32, lo);
         }
         tmem_wait_st();
         tc_fence_before();
-        mbar_arrive(bar(kBarPFull + i));
+        mbar_arrive(JT_BAR(kBarPFull + 2 * i + buf));
       }
-      // Epilogue: last PV done -> O / l, or an unnormalised partial for split items.
-      mbar_wait(bar(kBarODone + i), od & 1, abort);
-      ++od;
+      // Epilogue: wait for the item's last PV into O_i.
+      mbar_wait(JT_BAR(kBarPvDone + i), pv & 1, abort);
+      ++pv;
       tc_fence_after();
       const bool split_item = it.n_split > 1;
       const int64_t slot = it.slot_base +
@@ -590,64 +683,61 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
       tc_fence_before();
-      mbar_arrive(bar(kBarOFree + i));
+      mbar_arrive(JT_BAR(kBarOFree + i));
       if (split_item) {
+        // Per-row merge: each row publishes its partial (max in log2 units, sum), then bumps
+        // its own counter; the split that completes a row merges that row.  Rows never
+        // wait for one another.
         w.part_ml[slot * (2 * kM) + item_row] = make_float2(m_run, l_run);
         __threadfence();
-        const int barrier_id = it.nq == 2 ? 1 : 3;
-        const int members = it.nq * kM;
-        named_sync(barrier_id, members);
-        // Flag slot by the item's position in this CTA's sequence (same for both tiles).
-        volatile int* flag = misc + 2 + (((index - static_cast<int>(blockIdx.x)) /
-                                         static_cast<int>(gridDim.x)) & 1);
-        if (i == 0 && t128 == 0) {
-          int* counter = w.counters + it.counter_base + it.h * it.mblocks + it.tp;
-          const int done = atomicAdd(counter, 1);
-          const int last = done == it.n_split - 1;
-          if (last) *counter = 0;
-          *flag = last;
-        }
-        named_sync(barrier_id, members);
-        if (*flag && row_ok) {
+        int* counter = w.counters +
+                       (static_cast<int64_t>(it.counter_base) + it.h * it.mblocks + it.tp) * (2 * kM) +
+                       item_row;
+        const int done = atomicAdd(counter, 1);
+        if (done == it.n_split - 1) {
+          *counter = 0;
           __threadfence();
-          const int64_t slot0 =
-              it.slot_base + (static_cast<int64_t>(it.h) * it.mblocks + it.tp) * it.n_split;
-          float mmax = -INFINITY;
-          for (int s2 = 0; s2 < it.n_split; ++s2)
-            mmax = fmaxf(mmax, __ldcg(w.part_ml + (slot0 + s2) * (2 * kM) + item_row).x);
-          const float mref = mmax == -INFINITY ? 0.f : mmax;
-          float den = 0.f;
-          for (int s2 = 0; s2 < it.n_split; ++s2) {
-            const float2 ml = __ldcg(w.part_ml + (slot0 + s2) * (2 * kM) + item_row);
-            den += jt::fast_exp2(ml.x - mref) * ml.y;
-          }
-          const float dinv = 1.f / den;
-          const int64_t off = static_cast<int64_t>(it.q_start + j) * p.out_stride0 +
-                              static_cast<int64_t>(it.h * G + g) * p.out_stride1;
-          for (int d = 0; d < kD; d += 4) {
-            float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+          if (row_ok) {
+            const int64_t slot0 =
+                it.slot_base + (static_cast<int64_t>(it.h) * it.mblocks + it.tp) * it.n_split;
+            float mmax = -INFINITY;
+            for (int s2 = 0; s2 < it.n_split; ++s2)
+              mmax = fmaxf(mmax, __ldcg(w.part_ml + (slot0 + s2) * (2 * kM) + item_row).x);
+            const float mref = mmax == -INFINITY ? 0.f : mmax;
+            float den = 0.f;
             for (int s2 = 0; s2 < it.n_split; ++s2) {
-              const float wv =
-                  jt::fast_exp2(__ldcg(w.part_ml + (slot0 + s2) * (2 * kM) + item_row).x - mref);
-              const float4 o = __ldcg(reinterpret_cast<const float4*>(
-                  w.part_o + ((slot0 + s2) * (2 * kM) + item_row) * kD + d));
-              acc.x += wv * o.x;
-              acc.y += wv * o.y;
-              acc.z += wv * o.z;
-              acc.w += wv * o.w;
+              const float2 ml = __ldcg(w.part_ml + (slot0 + s2) * (2 * kM) + item_row);
+              den += jt::fast_exp2(ml.x - mref) * ml.y;
             }
-            if (p.out_dtype == JT_F32) {
-              *reinterpret_cast<float4*>(static_cast<float*>(p.out) + off + d) =
-                  make_float4(acc.x * dinv, acc.y * dinv, acc.z * dinv, acc.w * dinv);
-            } else {
-              *reinterpret_cast<uint2*>(static_cast<Elem*>(p.out) + off + d) =
-                  make_uint2(Mma::pack(acc.x * dinv, acc.y * dinv), Mma::pack(acc.z * dinv, acc.w * dinv));
+            const float dinv = 1.f / den;
+            const int64_t off = static_cast<int64_t>(it.q_start + j) * p.out_stride0 +
+                                static_cast<int64_t>(it.h * G + g) * p.out_stride1;
+            for (int d = 0; d < kD; d += 4) {
+              float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+              for (int s2 = 0; s2 < it.n_split; ++s2) {
+                const float wv =
+                    jt::fast_exp2(__ldcg(w.part_ml + (slot0 + s2) * (2 * kM) + item_row).x - mref);
+                const float4 o = __ldcg(reinterpret_cast<const float4*>(
+                    w.part_o + ((slot0 + s2) * (2 * kM) + item_row) * kD + d));
+                acc.x += wv * o.x;
+                acc.y += wv * o.y;
+                acc.z += wv * o.z;
+                acc.w += wv * o.w;
+              }
+              if (p.out_dtype == JT_F32) {
+                *reinterpret_cast<float4*>(static_cast<float*>(p.out) + off + d) =
+                    make_float4(acc.x * dinv, acc.y * dinv, acc.z * dinv, acc.w * dinv);
+              } else {
+                *reinterpret_cast<uint2*>(static_cast<Elem*>(p.out) + off + d) = make_uint2(
+                    Mma::pack(acc.x * dinv, acc.y * dinv), Mma::pack(acc.z * dinv, acc.w * dinv));
+              }
             }
           }
         }
       }
     }
   }
+#undef JT_BAR
 
   tc_fence_before();
   __syncthreads();

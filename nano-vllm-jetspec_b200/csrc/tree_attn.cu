@@ -74,7 +74,11 @@ Layout make_layout(int32_t R, int32_t Q, int32_t H, int32_t G, int32_t D,
   L.off_header = o;   o = align_up(o + 64, 256);
   L.off_req = o;      o = align_up(o + sizeof(int4) * static_cast<size_t>(R), 256);
   L.off_items = o;    o = align_up(o + sizeof(int4) * static_cast<size_t>(L.max_items), 256);
-  L.off_counters = o; o = align_up(o + sizeof(int) * static_cast<size_t>(L.max_slots), 256);
+  // Split counters: one per (request, kv head, m-block) for the portable core, one per
+  // score row for the tcgen05 core (whose rows finish independently).
+  const size_t counter_stride = L.bm > 128 ? static_cast<size_t>(L.bm) : 1;
+  L.off_counters = o;
+  o = align_up(o + sizeof(int) * static_cast<size_t>(L.max_slots) * counter_stride, 256);
   L.off_masks = o;
   o = align_up(o + sizeof(uint32_t) * static_cast<size_t>(Q) * L.mask_words, 256);
   L.off_part_o = o;   o = align_up(o + static_cast<size_t>(per_slot) * L.max_slots, 256);
@@ -93,6 +97,7 @@ struct DevLayout {
   float* part_o;
   float2* part_ml;
   int bm, mask_words, max_items, max_slots;
+  int counter_stride;  // split counters per (request, kv head, m-block): 1, or one per row
 };
 
 DevLayout device_layout(const Layout& L, void* ws) {
@@ -109,6 +114,7 @@ DevLayout device_layout(const Layout& L, void* ws) {
   d.mask_words = L.mask_words;
   d.max_items = L.max_items;
   d.max_slots = L.max_slots;
+  d.counter_stride = L.bm > 128 ? L.bm : 1;
   return d;
 }
 
@@ -250,7 +256,8 @@ __global__ void __launch_bounds__(kPlanThreads)
     __syncthreads();
   }
   // Reset split counters for this launch.
-  for (int i = tid; i < s_carry[1]; i += kPlanThreads) w.counters[i] = 0;
+  for (int64_t i = tid; i < static_cast<int64_t>(s_carry[1]) * w.counter_stride; i += kPlanThreads)
+    w.counters[i] = 0;
 
   // Longest-first item order: bucket units (request, split) by floor(log2(keys)).
   for (int r = tid; r < R; r += kPlanThreads) {

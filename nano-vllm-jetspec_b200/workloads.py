@@ -213,17 +213,19 @@ def config2(seed=1002) -> TreeBatch:
                        name="config2")
 
 
-def config3(seed=1003, num_requests=64) -> TreeBatch:
+def config3(seed=1003, num_requests=64, num_blocks=None) -> TreeBatch:
     """Serving mix: 64 requests, context log-uniform [512, 16384], tree budgets from
     {16, 32, 64, 128}, accepted lengths Geometric(0.35) capped at the tree depth,
-    16384-page shuffled pool."""
+    shuffled pool of 16384 pages per 64 requests (``num_blocks`` overrides it)."""
     rng = np.random.default_rng(seed)
     prefixes = np.exp(rng.uniform(math.log(512), math.log(16384), size=num_requests))
     prefixes = prefixes.astype(np.int64).tolist()
     budgets = rng.choice([16, 32, 64, 128], size=num_requests).tolist()
     parents = [random_parents(rng, int(t), window=8) for t in budgets]
     accepted = _geometric(rng, parents, 0.35)
-    return build_batch(prefixes, parents, num_blocks=max(16384, 1), seed=seed,
+    if num_blocks is None:
+        num_blocks = 16384 * max(1, -(-num_requests // 64))
+    return build_batch(prefixes, parents, num_blocks=num_blocks, seed=seed,
                        accepted_lengths=accepted, name="config3")
 
 

@@ -109,6 +109,25 @@ def test_split_kv_partials_match_single_pass(split_keys):
     assert (whole - split).abs().max().item() < 1e-3
 
 
+@pytest.mark.parametrize("prefix,nodes", ((512, 16), (512, 33), (512, 64), (1024, 16), (2048, 32),
+                                          (500, 16), (0, 128), (4096, 128)))
+def test_constant_values_give_exact_normalisation(prefix, nodes):
+    # Every output row is a convex combination of V rows: with V constant the output is
+    # that constant, whatever the scores.  Tile-aligned prefixes make every prefix tile a
+    # TMA tile followed by a cp.async tree tile, the pattern that exposed a stage-reuse race.
+    rng = np.random.default_rng(5)
+    batch = workloads.build_batch([prefix], [workloads.random_parents(rng, nodes)], seed=11)
+    q, k, v = tensors(batch)
+    meta = batch.metadata(DEVICE)
+    v_const = torch.full_like(v, 0.25)
+    for _ in range(3):
+        out = torch.empty(q.shape, dtype=torch.float32, device=DEVICE)
+        tree_gqa.launch_tree_attention(out, q, k, v_const, meta, batch.head_dim ** -0.5,
+                                       batch.groups)
+        assert (out - 0.25).abs().max().item() < 1e-3
+    assert jb.read_device_errors() == 0
+
+
 def test_repeat_is_bitwise_deterministic():
     batch = ragged_batch((2048, 65, 0))
     q, k, v = tensors(batch)
