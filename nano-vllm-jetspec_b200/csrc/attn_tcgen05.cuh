@@ -1,73 +1,76 @@
 // Blackwell (sm_100a) tree-attention core: tcgen05 tensor cores with TMEM accumulators.
 //
 // Included by tree_attn.cu inside its anonymous namespace (uses DevLayout, the plan's
-// work items and g_attn_errors).  One persistent CTA per SM; work items come from the
-// device plan in longest-first order and are strided over the CTAs.  An item is up to
-// two 128-row query tiles (256 score rows = 256/groups tree nodes x groups query heads)
-// of one (request, KV head, key split).  Warp roles:
+// work items and g_attn_errors).  One persistent CTA per SM pulls work items from the
+// device plan's queue (longest first).  An item is up to two 128-row query tiles (256
+// score rows = 256/groups tree nodes x groups query heads) of one (request, KV head, key
+// split), streamed against 128-key K/V tiles.  Warp roles:
 //
 //   warp 0       MMA issuer (one thread) and TMEM owner (512 columns)
-//   warps 1-3    loaders: TMA for full prefix tiles (64 keys inside one page, 128-byte
+//   warps 1-3    loaders: TMA for prefix tiles (128 keys inside one page, 128-byte
 //                swizzle), cp.async for query tiles and for tiles that touch the tree
 //                nodes (scattered scratch slots), written in the same swizzled layout
 //   warps 4-7    softmax + epilogue of query tile 0 (one thread per score row)
 //   warps 8-11   softmax + epilogue of query tile 1
 //
-// Per 64-key tile j and query tile i: S_i = Q_i K_j^T (tcgen05.mma, A and B from shared
-// memory, fp32 accumulator in TMEM); the softmax warps read S_i from TMEM, apply the
-// tree mask, update the fp32 online softmax and write P_i (rounded to the operand type)
-// back to TMEM; O_i += P_i V_j (tcgen05.mma with A from TMEM, B = V in shared memory,
-// MN-major).  The two query tiles ping-pong: while one tile's softmax runs, the tensor
-// core works on the other tile.  The running max is only moved (and O rescaled in TMEM)
-// when it grows by more than 2^8, so P stays <= 256 and the rescale is rare.
+// Per key tile t and query tile i: S_i = Q_i K_t^T (tcgen05.mma M128 N128 K16, both
+// operands in shared memory, fp32 accumulator in TMEM); the softmax warps read S_i from
+// TMEM, apply the tree mask, update the fp32 online softmax and write P (rounded to the
+// operand type) back over S_i; O_i += P V_t (tcgen05.mma with A from TMEM and V MN-major
+// in shared memory).  The tensor core alternates between the two query tiles, so one
+// tile's softmax overlaps the other tile's MMAs.  The running max only moves (and O is
+// rescaled in TMEM) when it grows by more than 2^8, so P stays <= 256 and rescales are
+// rare.  K and V stages have separate barriers: K is released once both QKs read it.
 //
-// Every mbarrier wait is bounded; a wait that runs out sets JT_DEVERR_TIMEOUT and an
-// abort flag, after which all roles run to the end without waiting, drain their own
-// asynchronous copies and MMAs, and the CTA frees its TMEM and exits.
+// Every mbarrier wait is bounded and every waiter consumes every phase of the barriers it
+// waits on, in order (parity waits are unambiguous only within one phase).  A wait that
+// runs out sets JT_DEVERR_TIMEOUT and an abort flag; all roles then leave their loops,
+// drain their own asynchronous copies and MMAs, and the CTA frees its TMEM and exits.
 
 namespace tc {
 
-constexpr int kN = 64;        // keys per KV tile
+constexpr int kN = 128;       // keys per KV tile
 constexpr int kD = 128;       // head dim
 constexpr int kM = 128;       // rows per query tile (MMA M)
-constexpr int kStages = 4;    // KV ring depth
+constexpr int kStages = 2;    // K and V ring depth
 constexpr int kThreads = 384;
 constexpr int kQTileBytes = kM * kD * 2;   // 32 KB: two 64-dim halves of [128 rows][128 B]
 constexpr int kQHalfBytes = kM * 128;
-constexpr int kKVBytes = kN * kD * 2;      // 16 KB: two 64-dim halves of [64 keys][128 B]
+constexpr int kKVBytes = kN * kD * 2;      // 32 KB: two 64-dim halves of [128 keys][128 B]
 constexpr int kKVHalfBytes = kN * 128;
 constexpr int kOffQ = 0;
 constexpr int kOffK = kOffQ + 2 * kQTileBytes;
 constexpr int kOffV = kOffK + kStages * kKVBytes;
 constexpr int kOffBar = kOffV + kStages * kKVBytes;
-constexpr int kOffRows = kOffBar + 8 * 32;              // 64 x (K, V) row byte offsets
-static_assert(8 * 32 >= 8 * 28, "barrier area");
-constexpr int kOffMisc = kOffRows + 64 * 2 * 8;
+constexpr int kOffMisc = kOffBar + 8 * 32;
 constexpr int kSmemBytes = kOffMisc + 64 + 1024;        // + alignment slack
 constexpr long long kWaitLimit = 4000000000ll;          // cycles (~2 s) per wait
 
-// TMEM column map (512 columns x 128 lanes x 32 bit): O_i (128 columns) and two S
-// buffers per query tile (64 columns each).  P (operand-type pairs, 32 columns) and, for
-// fp32 probabilities, its low part (32 more) are written over the S buffer they came from.
+// TMEM column map (512 columns x 128 lanes x 32 bit): O_i and S_i, 128 columns each.
+// P (operand-type pairs, 64 columns) and, for fp32 probabilities, its low part (64 more)
+// are written over S_i.
 __host__ __device__ constexpr uint32_t col_o(int i) { return 128u * i; }
-__host__ __device__ constexpr uint32_t col_s(int i, int b) { return 256u + 128u * i + 64u * b; }
+__host__ __device__ constexpr uint32_t col_s(int i) { return 256u + 128u * i; }
 
 // Barrier indices.
-constexpr int kBarKvFull = 0;                  // [kStages]
-constexpr int kBarKvEmpty = kStages;           // [kStages]
-constexpr int kBarQFull = 2 * kStages;
-constexpr int kBarQEmpty = kBarQFull + 1;
-constexpr int kBarSFull = kBarQEmpty + 1;      // [2 tiles][2 buffers]
-constexpr int kBarPFull = kBarSFull + 4;       // [2 tiles][2 buffers], 128 arrivals
-constexpr int kBarPvDone = kBarPFull + 4;      // [2 tiles], one commit per PV
-constexpr int kBarOFree = kBarPvDone + 2;      // [2 tiles], 128 arrivals
-constexpr int kBarItemDone = kBarOFree + 2;    // every MMA of an item completed
-constexpr int kBarDrain = kBarItemDone + 1;
-constexpr int kBarItemFull = kBarDrain + 1;    // [2] work-item ring
-constexpr int kBarItemEmpty = kBarItemFull + 2;  // [2]
-constexpr int kItemConsumers = 12;               // every warp of the CTA reads each item
-constexpr int kLoaderWarps = 3;                  // q_full / kv_full arrivals (one per warp)
-constexpr int kNumBars = kBarItemEmpty + 2;
+constexpr int kBarKFull = 0;                   // [kStages]  loader warps (+ TMA bytes)
+constexpr int kBarKEmpty = 2;                  // [kStages]  MMA commit after the QKs
+constexpr int kBarVFull = 4;                   // [kStages]
+constexpr int kBarVEmpty = 6;                  // [kStages]  MMA commit after the PVs
+constexpr int kBarQFull = 8;                   // loader warps
+constexpr int kBarQEmpty = 9;                  // MMA commit after an item's last QK
+constexpr int kBarSFull = 10;                  // [2 tiles]  MMA commit per QK
+constexpr int kBarPFull = 12;                  // [2 tiles]  128 softmax threads
+constexpr int kBarPvDone = 14;                 // [2 tiles]  MMA commit per PV
+constexpr int kBarOReady = 16;                 // [2 tiles]  MMA commit after an item's last PV
+constexpr int kBarOFree = 18;                  // [2 tiles]  128 threads after the epilogue
+constexpr int kBarDrain = 20;
+constexpr int kBarItemFull = 21;               // [2] work-item ring
+constexpr int kBarItemEmpty = 23;              // [2]
+constexpr int kNumBars = 25;
+constexpr int kItemConsumers = 12;             // every warp of the CTA reads each item
+constexpr int kLoaderWarps = 3;
+static_assert(kNumBars * 8 <= 8 * 32, "barrier area");
 
 // ---- PTX wrappers ------------------------------------------------------------------
 __device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
@@ -175,6 +178,14 @@ __device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&v)[32
       "r"(v[22]), "r"(v[23]), "r"(v[24]), "r"(v[25]), "r"(v[26]), "r"(v[27]), "r"(v[28]),
       "r"(v[29]), "r"(v[30]), "r"(v[31]));
 }
+__device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t (&v)[16]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,"
+      "%13,%14,%15,%16};\n" ::"r"(taddr),
+      "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]),
+      "r"(v[8]), "r"(v[9]), "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]),
+      "r"(v[15]));
+}
 __device__ __forceinline__ void tmem_wait_ld() {
   asm volatile("tcgen05.wait::ld.sync.aligned;\n" ::: "memory");
 }
@@ -196,6 +207,29 @@ __device__ __forceinline__ void tma_load_4d(uint32_t dst, const CUtensorMap* map
 __device__ __forceinline__ uint32_t swz128(int row, int chunk, int rows) {
   const int half = chunk >> 3, c = chunk & 7;
   return static_cast<uint32_t>(half * rows * 128 + row * 128 + ((c ^ (row & 7)) << 4));
+}
+
+// Visibility of the 32 keys at positions p0..p0+31 for one score row: bit b is set when
+// position p0+b is a prefix key, or a tree node inside [P, key_end) whose ancestor bit
+// (from the row's bitmask) is set.
+__device__ __forceinline__ uint32_t visible_bits(int p0, int P, int key_end, int T,
+                                                 const uint32_t* mask_row) {
+  uint32_t bits = 0;
+  const int pre = min(P, key_end) - p0;  // prefix keys in this word
+  if (pre >= 32) return 0xffffffffu;
+  if (pre > 0) bits = (1u << pre) - 1u;
+  const int n0 = p0 - P;        // node index of bit 0
+  const int end = key_end - p0;  // bits below `end` are inside the key range
+  if (end > 0 && n0 + 31 >= 0) {
+    const int lo = max(0, -n0);  // first bit that is a tree node
+    const int nb = n0 + lo;      // its node index
+    const int widx = nb >> 5, sh = nb & 31;
+    uint32_t word = __ldg(mask_row + widx) >> sh;
+    if (sh != 0 && (widx + 1) * 32 < T) word |= __ldg(mask_row + widx + 1) << (32 - sh);
+    word <<= lo;
+    bits |= word & (end >= 32 ? 0xffffffffu : ((1u << end) - 1u));
+  }
+  return bits;
 }
 
 struct Item {
@@ -233,6 +267,139 @@ __device__ __forceinline__ Item decode(const JtTreeAttnParams& p, const DevLayou
   return it;
 }
 
+// Loads one 128-key K or V tile into its ring stage: TMA when the keys are one page's
+// prefix run, else one cp.async row per loader thread (rows past key_end zero-filled).
+__device__ __forceinline__ void load_kv_tile(const JtTreeAttnParams& p, const Item& it,
+                                             const int32_t* table, int kb, bool full, int ltid,
+                                             int lane, uint32_t dst, const CUtensorMap* map,
+                                             const char* pool, int64_t s0, int64_t s1,
+                                             int64_t s2, uint32_t full_bar, int64_t pool_slots,
+                                             int page) {
+  const int bs = p.block_size;
+  if (full) {
+    if (ltid == 0) {
+      const int off = kb % bs;
+      mbar_arrive_tx(full_bar, kKVBytes);
+      tma_load_4d(dst, map, 0, it.h, off, page, full_bar);
+      tma_load_4d(dst + kKVHalfBytes, map, 64, it.h, off, page, full_bar);
+    } else if (lane == 0) {
+      mbar_arrive(full_bar);
+    }
+    return;
+  }
+  for (int row = ltid; row < kN; row += 96) {
+    const int pos = kb + row;
+    int64_t off = -1;
+    if (pos < it.key_end) {
+      int64_t slot = -1;
+      if (pos < it.P) {
+        const int col = pos / bs;
+        if (col < p.table_width)
+          slot = static_cast<int64_t>(__ldg(table + col)) * bs + pos % bs;
+      } else {
+        slot = __ldg(p.tree_slots + it.q_start + (pos - it.P));
+      }
+      if (slot >= 0 && slot < pool_slots) {
+        const int64_t pg = slot / bs, o = slot - pg * bs;
+        off = (pg * s0 + o * s1 + static_cast<int64_t>(it.h) * s2) * 2;
+      } else {
+        atomicOr(&g_attn_errors, JT_DEVERR_OUT_OF_RANGE);
+      }
+    }
+#pragma unroll
+    for (int chunk = 0; chunk < 16; ++chunk)
+      jt::cp_async_16(dst + swz128(row, chunk, kN), off >= 0 ? pool + off + chunk * 16 : pool,
+                      off >= 0 ? 16 : 0);
+  }
+  asm volatile("cp.async.wait_all;\n" ::: "memory");
+  fence_proxy_async();
+  __syncwarp();
+  if (lane == 0) mbar_arrive(full_bar);
+}
+
+// Softmax helpers for one score row (the calling thread's TMEM lane) of one 128-key tile.
+// `vk` describes the tile for masked tiles: keys kb..kb+127, prefix P, range end, nodes T
+// and the row's ancestor bitmask (row_ok false masks the whole row).
+struct TileKeys {
+  int kb, P, key_end, T;
+  const uint32_t* mask_row;
+  bool row_ok;
+};
+
+template <bool kMasked>
+__device__ __forceinline__ uint32_t chunk_visibility(const TileKeys& vk, int h) {
+  if constexpr (!kMasked) return 0xffffffffu;
+  return vk.row_ok ? visible_bits(vk.kb + 32 * h, vk.P, vk.key_end, vk.T, vk.mask_row) : 0u;
+}
+
+template <bool kMasked>
+__device__ __forceinline__ float row_max(uint32_t s_addr, const TileKeys& vk) {
+  float m4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+#pragma unroll 1
+  for (int h = 0; h < 4; ++h) {
+    const uint32_t vw = chunk_visibility<kMasked>(vk, h);
+    uint32_t v[32];
+    tmem_ld32(s_addr + 32 * h, v);
+    tmem_wait_ld();
+#pragma unroll
+    for (int c = 0; c < 32; ++c) {
+      float x = __uint_as_float(v[c]);
+      if constexpr (kMasked) x = ((vw >> c) & 1u) ? x : -INFINITY;
+      m4[c & 3] = fmaxf(m4[c & 3], x);
+    }
+  }
+  return fmaxf(fmaxf(m4[0], m4[1]), fmaxf(m4[2], m4[3]));
+}
+
+// P = exp2(s * scale_log2 - m) rounded to the operand type, written over S (columns
+// 0..63; the fp32-probability low parts go to columns 64..127).  Returns the fp32 sum.
+template <typename Elem, bool FP32P, bool kMasked>
+__device__ __forceinline__ float write_probabilities(uint32_t s_addr, const TileKeys& vk,
+                                                     float scale_log2, float neg_m) {
+  using Mma = jt::MmaOp<Elem>;
+  float r4[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll 1
+  for (int h = 0; h < 4; ++h) {
+    const uint32_t vw = chunk_visibility<kMasked>(vk, h);
+    uint32_t v[32];
+    tmem_ld32(s_addr + 32 * h, v);
+    tmem_wait_ld();
+    uint32_t ph[16];
+    uint32_t pl[FP32P ? 16 : 1];
+#pragma unroll
+    for (int c = 0; c < 16; ++c) {
+      float x0 = __uint_as_float(v[2 * c]), x1 = __uint_as_float(v[2 * c + 1]);
+      if constexpr (kMasked) {
+        x0 = ((vw >> (2 * c)) & 1u) ? x0 : -INFINITY;
+        x1 = ((vw >> (2 * c + 1)) & 1u) ? x1 : -INFINITY;
+      }
+      const float p0 = jt::fast_exp2(fmaf(x0, scale_log2, neg_m));
+      const float p1 = jt::fast_exp2(fmaf(x1, scale_log2, neg_m));
+      r4[c & 3] += p0 + p1;
+      ph[c] = Mma::pack(p0, p1);
+      if constexpr (FP32P) {
+        const float2 r = Mma::unpack(ph[c]);
+        pl[c] = Mma::pack(p0 - r.x, p1 - r.y);
+      }
+    }
+    tmem_st16(s_addr + 16 * h, ph);
+    if constexpr (FP32P) tmem_st16(s_addr + 64 + 16 * h, pl);
+  }
+  return (r4[0] + r4[1]) + (r4[2] + r4[3]);
+}
+
+template <bool FP32P>
+__device__ __forceinline__ void write_zero_probabilities(uint32_t s_addr) {
+  uint32_t z[16];
+#pragma unroll
+  for (int c = 0; c < 16; ++c) z[c] = 0u;
+#pragma unroll
+  for (int h = 0; h < 4; ++h) {
+    tmem_st16(s_addr + 16 * h, z);
+    if constexpr (FP32P) tmem_st16(s_addr + 64 + 16 * h, z);
+  }
+}
+
 template <typename Elem, bool FP32P>
 __global__ void __launch_bounds__(kThreads, 1)
     tree_attn_tc_kernel(const JtTreeAttnParams p, const DevLayout w,
@@ -257,14 +424,15 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (tid == 0) {
     for (int i = 0; i < kNumBars; ++i) {
       uint32_t count = 1;
-      if ((i >= kBarPFull && i < kBarPFull + 4) || i == kBarOFree || i == kBarOFree + 1)
+      if (i == kBarPFull || i == kBarPFull + 1 || i == kBarOFree || i == kBarOFree + 1)
         count = 128;
       if (i == kBarItemEmpty || i == kBarItemEmpty + 1) count = kItemConsumers;
-      if (i == kBarQFull || (i >= kBarKvFull && i < kBarKvFull + kStages)) count = kLoaderWarps;
+      if (i == kBarQFull || (i >= kBarKFull && i < kBarKFull + kStages) ||
+          (i >= kBarVFull && i < kBarVFull + kStages))
+        count = kLoaderWarps;
       mbar_init(JT_BAR(i), count);
     }
     misc[1] = 0;
-    misc[2] = misc[3] = 0;
     misc[4] = misc[5] = -1;
     asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
   }
@@ -283,10 +451,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int split_keys = w.header[2];
   const int G = p.groups, bs = p.block_size;
 
-  // Work items come from the device queue (longest first).  Loader thread 0 takes the
-  // next one and publishes it through a two-entry ring; every warp reads each entry.
-  // Lane 0 of each warp reads the entry and broadcasts it, so a warp always agrees with
-  // itself; after an abort every reader sees -1 and leaves its loop.
+  // Work items: loader thread 0 takes the next one from the device queue and publishes it
+  // through a two-entry ring.  Lane 0 of every warp reads each entry and broadcasts it
+  // (a warp always agrees with itself); after an abort every reader sees -1.
   auto next_item = [&](uint32_t seq) -> int {
     const int slot = seq & 1;
     int index = -1;
@@ -300,81 +467,76 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   if (warp == 0) {
     // ------------------------------------------------------------------ MMA issuer
-    // Per query tile i and 64-key tile t: S_i[t%2] = Q_i K_t^T, then (after the softmax
-    // wrote P into that buffer) O_i += P V_t.  QK(t+1) is issued as soon as PV(t-1) has
-    // released the buffer, so the softmax of tile t+1 never waits for the PV of tile t.
-    uint32_t kv_count = 0, q_count = 0, items_done = 0;
-    // Phase parities kept as bits: pv_par bit i = parity of the next PV commit of tile i,
-    // pf_par bit (2i+b) = parity of the next p_full phase of buffer b, of_par bit i =
-    // parity of the next o_free phase to wait for, of_seen bit i = tile i used before.
-    uint32_t pv_par = 0, pf_par = 0, of_par = 0, of_seen = 0;
+    // Phase parities kept as bits.  qk/pv counters index the key tiles consumed so far;
+    // pv_pending bit i: PV_i issued but not yet waited for (S_i still holds its P).
+    uint32_t kc = 0, vc = 0, q_count = 0;
+    uint32_t pf_par = 0, pv_par = 0, pv_pending = 0, of_par = 0, of_seen = 0;
     for (uint32_t seq = 0;; ++seq) {
       const int index = next_item(seq);
       if (index < 0) break;
       if (lane != 0) continue;
       const Item it = decode(p, w, index, split_keys);
       const int nq = it.nq, n_tiles = it.n_tiles;
-      if (items_done > 0) mbar_wait(JT_BAR(kBarItemDone), (items_done - 1) & 1, abort);
       mbar_wait(JT_BAR(kBarQFull), q_count & 1, abort);
       ++q_count;
       tc_fence_after();
-      auto issue_qk = [&](int i, int t, int stage) {
-        const uint32_t qa = base + kOffQ + i * kQTileBytes;
-        const uint32_t ka = base + kOffK + stage * kKVBytes;
-#pragma unroll
-        for (int kk = 0; kk < kD / 16; ++kk) {
-          const uint32_t off = (kk & 3) * 32;
-          mma_ss(tmem + col_s(i, t & 1), smem_desc(qa + (kk >> 2) * kQHalfBytes + off, 16, 1024),
-                 smem_desc(ka + (kk >> 2) * kKVHalfBytes + off, 16, 1024), kIdescQK,
-                 kk > 0 ? 1u : 0u);
-        }
-        tc_commit(JT_BAR(kBarSFull + 2 * i + (t & 1)));
-      };
-      {
-        const int stage = kv_count % kStages;
-        mbar_wait(JT_BAR(kBarKvFull + stage), (kv_count / kStages) & 1, abort);
+      // S_i = Q_i K^T for one key tile; S_i must no longer hold an unread P.
+      auto issue_qk = [&](int last_qk_of_item) {
+        const int stage = kc % kStages;
+        mbar_wait(JT_BAR(kBarKFull + stage), (kc / kStages) & 1, abort);
         tc_fence_after();
-        for (int i = 0; i < nq; ++i) issue_qk(i, 0, stage);
-        if (n_tiles == 1) tc_commit(JT_BAR(kBarQEmpty));
-      }
-      for (int t = 0; t < n_tiles; ++t) {
-        const int stage = kv_count % kStages;
-        if (t + 1 < n_tiles) {
-          const int next = (kv_count + 1) % kStages;
-          mbar_wait(JT_BAR(kBarKvFull + next), ((kv_count + 1) / kStages) & 1, abort);
-          for (int i = 0; i < nq; ++i) {
-            // Buffer (t+1)%2 last held P(t-1): wait until PV(t-1) has read it.
-            if (t >= 1) mbar_wait(JT_BAR(kBarPvDone + i), ((pv_par >> i) & 1u) ^ 1u, abort);
+        const uint32_t ka = base + kOffK + stage * kKVBytes;
+        for (int i = 0; i < nq; ++i) {
+          if ((pv_pending >> i) & 1u) {
+            mbar_wait(JT_BAR(kBarPvDone + i), (pv_par >> i) & 1u, abort);
+            pv_par ^= 1u << i;
+            pv_pending &= ~(1u << i);
             tc_fence_after();
-            issue_qk(i, t + 1, next);
           }
-          if (t + 2 == n_tiles) tc_commit(JT_BAR(kBarQEmpty));
+          const uint32_t qa = base + kOffQ + i * kQTileBytes;
+#pragma unroll
+          for (int kk = 0; kk < kD / 16; ++kk) {
+            const uint32_t off = (kk & 3) * 32;
+            mma_ss(tmem + col_s(i), smem_desc(qa + (kk >> 2) * kQHalfBytes + off, 16, 1024),
+                   smem_desc(ka + (kk >> 2) * kKVHalfBytes + off, 16, 1024), kIdescQK,
+                   kk > 0 ? 1u : 0u);
+          }
+          tc_commit(JT_BAR(kBarSFull + i));
         }
+        tc_commit(JT_BAR(kBarKEmpty + stage));
+        if (last_qk_of_item) tc_commit(JT_BAR(kBarQEmpty));
+        ++kc;
+      };
+      issue_qk(n_tiles == 1);
+      for (int t = 0; t < n_tiles; ++t) {
+        const int stage = vc % kStages;
+        mbar_wait(JT_BAR(kBarVFull + stage), (vc / kStages) & 1, abort);
         const uint32_t va = base + kOffV + stage * kKVBytes;
         for (int i = 0; i < nq; ++i) {
           if (t == 0 && ((of_seen >> i) & 1u)) {
             mbar_wait(JT_BAR(kBarOFree + i), (of_par >> i) & 1u, abort);
             of_par ^= 1u << i;
           }
-          const int pb = 2 * i + (t & 1);
-          mbar_wait(JT_BAR(kBarPFull + pb), (pf_par >> pb) & 1u, abort);
-          pf_par ^= 1u << pb;
+          mbar_wait(JT_BAR(kBarPFull + i), (pf_par >> i) & 1u, abort);
+          pf_par ^= 1u << i;
           tc_fence_after();
-          const uint32_t pa = tmem + col_s(i, t & 1);
+          // O_i += P V (P over S_i in TMEM, V MN-major in shared memory).
+          const uint32_t pa = tmem + col_s(i);
 #pragma unroll
           for (int kk = 0; kk < kN / 16; ++kk) {
             const uint64_t b = smem_desc(va + kk * 2048, kKVHalfBytes, 1024);
             mma_ts(tmem + col_o(i), pa + kk * 8, b, kIdescPV, (t > 0 || kk > 0) ? 1u : 0u);
-            if constexpr (FP32P) mma_ts(tmem + col_o(i), pa + 32 + kk * 8, b, kIdescPV, 1u);
+            if constexpr (FP32P)
+              mma_ts(tmem + col_o(i), pa + 64 + kk * 8, b, kIdescPV, 1u);
           }
           tc_commit(JT_BAR(kBarPvDone + i));
-          pv_par ^= 1u << i;
+          pv_pending |= 1u << i;
+          if (t + 1 == n_tiles) tc_commit(JT_BAR(kBarOReady + i));
         }
-        tc_commit(JT_BAR(kBarKvEmpty + stage));
-        ++kv_count;
+        tc_commit(JT_BAR(kBarVEmpty + stage));
+        ++vc;
+        if (t + 1 < n_tiles) issue_qk(t + 2 == n_tiles);
       }
-      tc_commit(JT_BAR(kBarItemDone));
-      ++items_done;
       for (int i = 0; i < nq; ++i) of_seen |= 1u << i;
     }
     if (lane == 0) {
@@ -385,11 +547,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   } else if (warp < 4) {
     // ------------------------------------------------------------------ loaders
     const int ltid = tid - 32;
-    uint32_t kv_count = 0;
-    uint32_t filled = 0;       // stages whose last fill went through TMA (drain bookkeeping)
-    uint32_t last_parity = 0;  // bit s: phase parity of stage s's last TMA fill
-    const char* kbase = static_cast<const char*>(p.k_pool);
-    const char* vbase = static_cast<const char*>(p.v_pool);
+    uint32_t kc = 0, vc = 0;
+    uint32_t filled = 0;       // bit (2*stage + v): last fill of that ring slot was TMA
+    uint32_t last_parity = 0;  // same bits: phase parity of that fill
     const int64_t pool_slots = p.num_blocks * static_cast<int64_t>(bs);
     for (uint32_t seq = 0;; ++seq) {
       if (ltid == 0) {
@@ -427,88 +587,54 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (lane == 0) mbar_arrive(JT_BAR(kBarQFull));
 
       for (int t = 0; t < it.n_tiles; ++t) {
-        const int stage = kv_count % kStages;
-        const uint32_t parity = (kv_count / kStages) & 1;
         const int kb = it.key_begin + t * kN;
         const bool full = kb + kN <= min(it.P, it.key_end);
-        const uint32_t kdst = base + kOffK + stage * kKVBytes;
-        const uint32_t vdst = base + kOffV + stage * kKVBytes;
-        const uint32_t full_bar = JT_BAR(kBarKvFull + stage);
-        // Every loader thread waits for every refill, in order: a parity wait is only
-        // unambiguous while the waiter is at most one phase behind the barrier.
         const int page = (full && ltid == 0) ? __ldg(table + kb / bs) : 0;
-        if (kv_count >= kStages) mbar_wait(JT_BAR(kBarKvEmpty + stage), parity ^ 1, abort);
-        if (full) {
-          if (lane == 0) {
-            if (ltid == 0) {
-              const int off = kb % bs;
-              mbar_arrive_tx(full_bar, 2 * kKVBytes);
-              tma_load_4d(kdst, &kmap, 0, it.h, off, page, full_bar);
-              tma_load_4d(kdst + kKVHalfBytes, &kmap, 64, it.h, off, page, full_bar);
-              tma_load_4d(vdst, &vmap, 0, it.h, off, page, full_bar);
-              tma_load_4d(vdst + kKVHalfBytes, &vmap, 64, it.h, off, page, full_bar);
-              filled |= 1u << stage;
-              last_parity = (last_parity & ~(1u << stage)) | (parity << stage);
-            } else {
-              mbar_arrive(full_bar);
-            }
-          }
-        } else {
-          // Tile that touches the tree nodes (or a page tail): one key row per thread.
-          if (ltid < kN) {
-            const int row = ltid;
-            const int pos = kb + row;
-            int64_t ko = -1, vo = -1;
-            if (pos < it.key_end) {
-              int64_t slot = -1;
-              if (pos < it.P) {
-                const int col = pos / bs;
-                if (col < p.table_width)
-                  slot = static_cast<int64_t>(__ldg(table + col)) * bs + pos % bs;
-              } else {
-                slot = __ldg(p.tree_slots + it.q_start + (pos - it.P));
-              }
-              if (slot >= 0 && slot < pool_slots) {
-                const int64_t page = slot / bs, off = slot - page * bs;
-                ko = (page * p.k_stride0 + off * p.k_stride1 +
-                      static_cast<int64_t>(it.h) * p.k_stride2) * 2;
-                vo = (page * p.v_stride0 + off * p.v_stride1 +
-                      static_cast<int64_t>(it.h) * p.v_stride2) * 2;
-              } else {
-                atomicOr(&g_attn_errors, JT_DEVERR_OUT_OF_RANGE);
-              }
-            }
-#pragma unroll
-            for (int chunk = 0; chunk < 16; ++chunk) {
-              const uint32_t o = swz128(row, chunk, kN);
-              jt::cp_async_16(kdst + o, ko >= 0 ? kbase + ko + chunk * 16 : kbase, ko >= 0 ? 16 : 0);
-              jt::cp_async_16(vdst + o, vo >= 0 ? vbase + vo + chunk * 16 : vbase, vo >= 0 ? 16 : 0);
-            }
-          }
-          asm volatile("cp.async.wait_all;\n" ::: "memory");
-          fence_proxy_async();
-          __syncwarp();
-          if (lane == 0) {
-            mbar_arrive(full_bar);
-            if (ltid == 0) filled &= ~(1u << stage);
-          }
+        // Every loader thread waits for every refill, in order.
+        {
+          const int stage = kc % kStages;
+          const uint32_t parity = (kc / kStages) & 1;
+          if (kc >= kStages) mbar_wait(JT_BAR(kBarKEmpty + stage), parity ^ 1, abort);
+          load_kv_tile(p, it, table, kb, full, ltid, lane, base + kOffK + stage * kKVBytes, &kmap,
+                       static_cast<const char*>(p.k_pool), p.k_stride0, p.k_stride1, p.k_stride2,
+                       JT_BAR(kBarKFull + stage), pool_slots, page);
+          const uint32_t bit = 1u << (2 * stage);
+          if (full) { filled |= bit; last_parity = (last_parity & ~bit) | (parity ? bit : 0u); }
+          else filled &= ~bit;
+          ++kc;
         }
-        ++kv_count;
+        {
+          const int stage = vc % kStages;
+          const uint32_t parity = (vc / kStages) & 1;
+          if (vc >= kStages) mbar_wait(JT_BAR(kBarVEmpty + stage), parity ^ 1, abort);
+          load_kv_tile(p, it, table, kb, full, ltid, lane, base + kOffV + stage * kKVBytes, &vmap,
+                       static_cast<const char*>(p.v_pool), p.v_stride0, p.v_stride1, p.v_stride2,
+                       JT_BAR(kBarVFull + stage), pool_slots, page);
+          const uint32_t bit = 2u << (2 * stage);
+          if (full) { filled |= bit; last_parity = (last_parity & ~bit) | (parity ? bit : 0u); }
+          else filled &= ~bit;
+          ++vc;
+        }
       }
     }
     // Drain: the TMA copies this thread issued have landed before the CTA exits.
     if (ltid == 0) {
-      for (int s = 0; s < kStages; ++s)
-        if (filled & (1u << s))
-          mbar_wait(JT_BAR(kBarKvFull + s), (last_parity >> s) & 1u, abort, false);
+      for (int s = 0; s < kStages; ++s) {
+        if (filled & (1u << (2 * s)))
+          mbar_wait(JT_BAR(kBarKFull + s), (last_parity >> (2 * s)) & 1u, abort, false);
+        if (filled & (2u << (2 * s)))
+          mbar_wait(JT_BAR(kBarVFull + s), (last_parity >> (2 * s + 1)) & 1u, abort, false);
+      }
     }
   } else {
     // ------------------------------------------------------------------ softmax + epilogue
     const int i = (warp - 4) >> 2;          // query tile of this warpgroup
     const int t128 = tid - 128 - i * 128;   // row within the query tile
     const uint32_t lane_base = static_cast<uint32_t>((t128 >> 5) * 32) << 16;
+    const uint32_t s_addr = tmem + lane_base + col_s(i);
+    const uint32_t o_addr = tmem + lane_base + col_o(i);
     const float scale_log2 = p.scale * 1.4426950408889634f;
-    uint32_t sf_par = 0, pv = 0;  // sf_par bit b: parity of the next s_full phase of buffer b
+    uint32_t sf_par = 0, or_par = 0;
     for (uint32_t seq = 0;; ++seq) {
       const int index = next_item(seq);
       if (index < 0) break;
@@ -525,57 +651,14 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int t = 0; t < it.n_tiles; ++t) {
         const int kb = it.key_begin + t * kN;
         const bool full = kb + kN <= min(it.P, it.key_end);
-        // Ancestor bits of this row for the tile's tree keys, fetched before the wait.
-        uint32_t mw0 = 0, mw1 = 0, mw2 = 0;
-        int n_first = 0;
-        if (!full && row_ok) {
-          n_first = kb - it.P;  // node of column 0 (negative while the tile is prefix)
-          const int w0 = n_first >= 0 ? (n_first >> 5) : 0;
-          const int last = min(it.T - 1, n_first + kN - 1);
-          if (last >= 0) {
-            mw0 = __ldg(mask_row + w0);
-            if (w0 + 1 <= (last >> 5)) mw1 = __ldg(mask_row + w0 + 1);
-            if (w0 + 2 <= (last >> 5)) mw2 = __ldg(mask_row + w0 + 2);
-          }
-        }
-        const int buf = t & 1;
-        mbar_wait(JT_BAR(kBarSFull + 2 * i + buf), (sf_par >> buf) & 1u, abort);
-        sf_par ^= 1u << buf;
+        // Keys of this tile; prefix-only tiles skip masking entirely.
+        const TileKeys vk{kb, it.P, it.key_end, it.T, mask_row, row_ok};
+        mbar_wait(JT_BAR(kBarSFull + i), sf_par, abort);
+        sf_par ^= 1u;
         tc_fence_after();
-        const uint32_t s_addr = tmem + lane_base + col_s(i, buf);
-        uint32_t sraw[2][32];
-        tmem_ld32(s_addr, sraw[0]);
-        tmem_ld32(s_addr + 32, sraw[1]);
-        tmem_wait_ld();
-        float s[64];
-#pragma unroll
-        for (int c = 0; c < 64; ++c) s[c] = __uint_as_float(sraw[c >> 5][c & 31]);
-        if (!full) {
-          const int wbase = n_first >= 0 ? (n_first >> 5) : 0;
-#pragma unroll
-          for (int c = 0; c < 64; ++c) {
-            const int pos = kb + c;
-            bool vis = row_ok && pos < it.key_end;
-            if (vis && pos >= it.P) {
-              const int n = pos - it.P;
-              const int wi = (n >> 5) - wbase;
-              const uint32_t word = wi == 0 ? mw0 : (wi == 1 ? mw1 : mw2);
-              vis = (word >> (n & 31)) & 1u;
-            }
-            if (!vis) s[c] = -INFINITY;
-          }
-        }
-        // Row max of the raw scores (scale > 0 keeps the order), as a tree.
-        float mx4[4];
-#pragma unroll
-        for (int q = 0; q < 4; ++q) {
-          float a = fmaxf(s[q * 16 + 0], s[q * 16 + 1]), b = fmaxf(s[q * 16 + 2], s[q * 16 + 3]);
-          float c2 = fmaxf(s[q * 16 + 4], s[q * 16 + 5]), d = fmaxf(s[q * 16 + 6], s[q * 16 + 7]);
-          float e = fmaxf(s[q * 16 + 8], s[q * 16 + 9]), f = fmaxf(s[q * 16 + 10], s[q * 16 + 11]);
-          float g2 = fmaxf(s[q * 16 + 12], s[q * 16 + 13]), h = fmaxf(s[q * 16 + 14], s[q * 16 + 15]);
-          mx4[q] = fmaxf(fmaxf(fmaxf(a, b), fmaxf(c2, d)), fmaxf(fmaxf(e, f), fmaxf(g2, h)));
-        }
-        const float mx = fmaxf(fmaxf(mx4[0], mx4[1]), fmaxf(mx4[2], mx4[3])) * scale_log2;
+        // Pass 1: row max over the 128 scores (raw; scale > 0 keeps the order).
+        float mx = full ? row_max<false>(s_addr, vk) : row_max<true>(s_addr, vk);
+        mx *= scale_log2;
         // Lazy max: move only when it grows by more than 8 (log2 units).
         float alpha = 1.f;
         bool rescale = false;
@@ -587,61 +670,34 @@ __global__ void __launch_bounds__(kThreads, 1)
           m_run = mx;
         }
         const float neg_m = m_run == -INFINITY ? 0.f : -m_run;
-        uint32_t ph[32];
-        uint32_t pl[FP32P ? 32 : 1];
-        float r4[4] = {0.f, 0.f, 0.f, 0.f};
+        // Pass 2: probabilities, 64 keys at a time; P overwrites the S columns already read.
+        float rsum = 0.f;
         if (warp_live) {
-#pragma unroll
-          for (int c = 0; c < 32; ++c) {
-            const float p0 = jt::fast_exp2(fmaf(s[2 * c], scale_log2, neg_m));
-            const float p1 = jt::fast_exp2(fmaf(s[2 * c + 1], scale_log2, neg_m));
-            r4[c & 3] += p0 + p1;
-            ph[c] = Mma::pack(p0, p1);
-            if constexpr (FP32P) {
-              const float2 r = Mma::unpack(ph[c]);
-              pl[c] = Mma::pack(p0 - r.x, p1 - r.y);
-            }
-          }
+          rsum = full ? write_probabilities<Elem, FP32P, false>(s_addr, vk, scale_log2, neg_m)
+                      : write_probabilities<Elem, FP32P, true>(s_addr, vk, scale_log2, neg_m);
         } else {
-#pragma unroll
-          for (int c = 0; c < 32; ++c) {
-            ph[c] = 0u;
-            if constexpr (FP32P) pl[c] = 0u;
-          }
+          write_zero_probabilities<FP32P>(s_addr);
         }
-        l_run = l_run * alpha + ((r4[0] + r4[1]) + (r4[2] + r4[3]));
-        // PV(t-1) must be done before O_i is rescaled; it normally is by now.
-        if (t > 0) {
-          mbar_wait(JT_BAR(kBarPvDone + i), pv & 1, abort);
-          ++pv;
-          tc_fence_after();
-        }
+        l_run = l_run * alpha + rsum;
+        // S_i ready implies the previous PV into O_i completed: rescale O_i in place.
         if (t > 0 && __any_sync(0xffffffffu, rescale)) {
 #pragma unroll 1
           for (int chunk = 0; chunk < 4; ++chunk) {
             uint32_t o[32];
-            const uint32_t ta = tmem + lane_base + col_o(i) + chunk * 32;
-            tmem_ld32(ta, o);
+            tmem_ld32(o_addr + chunk * 32, o);
             tmem_wait_ld();
 #pragma unroll
             for (int c = 0; c < 32; ++c) o[c] = __float_as_uint(__uint_as_float(o[c]) * alpha);
-            tmem_st32(ta, o);
+            tmem_st32(o_addr + chunk * 32, o);
           }
-        }
-        tmem_st32(s_addr, ph);
-        if constexpr (FP32P) {
-          uint32_t lo[32];
-#pragma unroll
-          for (int c = 0; c < 32; ++c) lo[c] = pl[c];
-          tmem_st32(s_addr + 32, lo);
         }
         tmem_wait_st();
         tc_fence_before();
-        mbar_arrive(JT_BAR(kBarPFull + 2 * i + buf));
+        mbar_arrive(JT_BAR(kBarPFull + i));
       }
       // Epilogue: wait for the item's last PV into O_i.
-      mbar_wait(JT_BAR(kBarPvDone + i), pv & 1, abort);
-      ++pv;
+      mbar_wait(JT_BAR(kBarOReady + i), or_par, abort);
+      or_par ^= 1u;
       tc_fence_after();
       const bool split_item = it.n_split > 1;
       const int64_t slot = it.slot_base +
@@ -651,7 +707,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll 1
       for (int chunk = 0; chunk < 4; ++chunk) {
         uint32_t o[32];
-        tmem_ld32(tmem + lane_base + col_o(i) + chunk * 32, o);
+        tmem_ld32(o_addr + chunk * 32, o);
         tmem_wait_ld();
         if (split_item) {
           float4* dst = reinterpret_cast<float4*>(w.part_o + (slot * (2 * kM) + item_row) * kD +
