@@ -61,7 +61,7 @@ constexpr int kBarQFull = 8;                   // loader warps
 constexpr int kBarQEmpty = 9;                  // MMA commit after an item's last QK
 constexpr int kBarSFull = 10;                  // [2 tiles]  MMA commit per QK
 constexpr int kBarPFull = 12;                  // [2 tiles]  128 softmax threads
-constexpr int kBarPvDone = 14;                 // [2 tiles]  MMA commit per PV
+constexpr int kBarPvDone = 14;                 // [2 tiles]  (unused)
 constexpr int kBarOReady = 16;                 // [2 tiles]  MMA commit after an item's last PV
 constexpr int kBarOFree = 18;                  // [2 tiles]  128 threads after the epilogue
 constexpr int kBarDrain = 20;
@@ -467,10 +467,13 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   if (warp == 0) {
     // ------------------------------------------------------------------ MMA issuer
-    // Phase parities kept as bits.  qk/pv counters index the key tiles consumed so far;
-    // pv_pending bit i: PV_i issued but not yet waited for (S_i still holds its P).
+    // Issue order per key tile t and query tile i: PV_i(t) then QK_i(t+1).  tcgen05.mma
+    // instructions of one thread execute in issue order, so PV_i(t) has read P out of S_i
+    // before QK_i(t+1) overwrites S_i, and the commit that signals S_i(t+1) also covers
+    // PV_i(t): the softmax may then rescale O_i.  While the softmax of one query tile
+    // runs, the tensor core works on the other tile.
     uint32_t kc = 0, vc = 0, q_count = 0;
-    uint32_t pf_par = 0, pv_par = 0, pv_pending = 0, of_par = 0, of_seen = 0;
+    uint32_t pf_par = 0, of_par = 0, of_seen = 0;
     for (uint32_t seq = 0;; ++seq) {
       const int index = next_item(seq);
       if (index < 0) break;
@@ -480,38 +483,33 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_wait(JT_BAR(kBarQFull), q_count & 1, abort);
       ++q_count;
       tc_fence_after();
-      // S_i = Q_i K^T for one key tile; S_i must no longer hold an unread P.
-      auto issue_qk = [&](int last_qk_of_item) {
+      auto issue_qk = [&](int i, int stage) {
+        const uint32_t qa = base + kOffQ + i * kQTileBytes;
+        const uint32_t ka = base + kOffK + stage * kKVBytes;
+#pragma unroll
+        for (int kk = 0; kk < kD / 16; ++kk) {
+          const uint32_t off = (kk & 3) * 32;
+          mma_ss(tmem + col_s(i), smem_desc(qa + (kk >> 2) * kQHalfBytes + off, 16, 1024),
+                 smem_desc(ka + (kk >> 2) * kKVHalfBytes + off, 16, 1024), kIdescQK,
+                 kk > 0 ? 1u : 0u);
+        }
+        tc_commit(JT_BAR(kBarSFull + i));
+      };
+      {
         const int stage = kc % kStages;
         mbar_wait(JT_BAR(kBarKFull + stage), (kc / kStages) & 1, abort);
         tc_fence_after();
-        const uint32_t ka = base + kOffK + stage * kKVBytes;
-        for (int i = 0; i < nq; ++i) {
-          if ((pv_pending >> i) & 1u) {
-            mbar_wait(JT_BAR(kBarPvDone + i), (pv_par >> i) & 1u, abort);
-            pv_par ^= 1u << i;
-            pv_pending &= ~(1u << i);
-            tc_fence_after();
-          }
-          const uint32_t qa = base + kOffQ + i * kQTileBytes;
-#pragma unroll
-          for (int kk = 0; kk < kD / 16; ++kk) {
-            const uint32_t off = (kk & 3) * 32;
-            mma_ss(tmem + col_s(i), smem_desc(qa + (kk >> 2) * kQHalfBytes + off, 16, 1024),
-                   smem_desc(ka + (kk >> 2) * kKVHalfBytes + off, 16, 1024), kIdescQK,
-                   kk > 0 ? 1u : 0u);
-          }
-          tc_commit(JT_BAR(kBarSFull + i));
-        }
+        for (int i = 0; i < nq; ++i) issue_qk(i, stage);
         tc_commit(JT_BAR(kBarKEmpty + stage));
-        if (last_qk_of_item) tc_commit(JT_BAR(kBarQEmpty));
+        if (n_tiles == 1) tc_commit(JT_BAR(kBarQEmpty));
         ++kc;
-      };
-      issue_qk(n_tiles == 1);
+      }
       for (int t = 0; t < n_tiles; ++t) {
-        const int stage = vc % kStages;
-        mbar_wait(JT_BAR(kBarVFull + stage), (vc / kStages) & 1, abort);
-        const uint32_t va = base + kOffV + stage * kKVBytes;
+        const int vstage = vc % kStages;
+        const int kstage = kc % kStages;
+        const bool more = t + 1 < n_tiles;
+        mbar_wait(JT_BAR(kBarVFull + vstage), (vc / kStages) & 1, abort);
+        const uint32_t va = base + kOffV + vstage * kKVBytes;
         for (int i = 0; i < nq; ++i) {
           if (t == 0 && ((of_seen >> i) & 1u)) {
             mbar_wait(JT_BAR(kBarOFree + i), (of_par >> i) & 1u, abort);
@@ -529,13 +527,22 @@ __global__ void __launch_bounds__(kThreads, 1)
             if constexpr (FP32P)
               mma_ts(tmem + col_o(i), pa + 64 + kk * 8, b, kIdescPV, 1u);
           }
-          tc_commit(JT_BAR(kBarPvDone + i));
-          pv_pending |= 1u << i;
-          if (t + 1 == n_tiles) tc_commit(JT_BAR(kBarOReady + i));
+          if (!more) tc_commit(JT_BAR(kBarOReady + i));
+          if (more) {
+            if (i == 0) {
+              mbar_wait(JT_BAR(kBarKFull + kstage), (kc / kStages) & 1, abort);
+              tc_fence_after();
+            }
+            issue_qk(i, kstage);
+          }
         }
-        tc_commit(JT_BAR(kBarVEmpty + stage));
+        tc_commit(JT_BAR(kBarVEmpty + vstage));
         ++vc;
-        if (t + 1 < n_tiles) issue_qk(t + 2 == n_tiles);
+        if (more) {
+          tc_commit(JT_BAR(kBarKEmpty + kstage));
+          if (t + 2 == n_tiles) tc_commit(JT_BAR(kBarQEmpty));
+          ++kc;
+        }
       }
       for (int i = 0; i < nq; ++i) of_seen |= 1u << i;
     }
