@@ -332,60 +332,108 @@ __device__ __forceinline__ uint32_t chunk_visibility(const TileKeys& vk, int h) 
   return vk.row_ok ? visible_bits(vk.kb + 32 * h, vk.P, vk.key_end, vk.T, vk.mask_row) : 0u;
 }
 
-template <bool kMasked>
-__device__ __forceinline__ float row_max(uint32_t s_addr, const TileKeys& vk) {
-  float m4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
-#pragma unroll 1
-  for (int h = 0; h < 4; ++h) {
-    const uint32_t vw = chunk_visibility<kMasked>(vk, h);
-    uint32_t v[32];
-    tmem_ld32(s_addr + 32 * h, v);
-    tmem_wait_ld();
-#pragma unroll
-    for (int c = 0; c < 32; ++c) {
-      float x = __uint_as_float(v[c]);
-      if constexpr (kMasked) x = ((vw >> c) & 1u) ? x : -INFINITY;
-      m4[c & 3] = fmaxf(m4[c & 3], x);
-    }
-  }
-  return fmaxf(fmaxf(m4[0], m4[1]), fmaxf(m4[2], m4[3]));
+// Exponentials of score pairs on the FMA pipe, relieving the MUFU unit (16 results per
+// clock per SM) that otherwise bounds the softmax.  2^x = 2^j * 2^f with j = rint(x) taken
+// from the float rounding trick (x + 1.5 * 2^23) and 2^f, f in [-0.5, 0.5], from a cubic
+// fitted to minimise the relative error on that interval (Lawson / minimax fit; max
+// relative error 8.4e-5, far below the bf16 rounding of P).  j is added straight into the
+// exponent field; x is clamped at -125 so the result stays a normal number or zero.
+__device__ __forceinline__ float max3f(float a, float b, float c) {
+  float d;
+  asm("max.f32 %0, %1, %2, %3;\n" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
+}
+__device__ __forceinline__ float2 exp2_poly2(float2 x) {
+  x = make_float2(fmaxf(x.x, -125.f), fmaxf(x.y, -125.f));
+  const float2 t = __fadd2_rn(x, make_float2(12582912.f, 12582912.f));
+  const float2 j = __fadd2_rn(t, make_float2(-12582912.f, -12582912.f));
+  const float2 f = __fadd2_rn(x, make_float2(-j.x, -j.y));
+  float2 q = __ffma2_rn(make_float2(0.05521299f, 0.05521299f), f,
+                        make_float2(0.24271414f, 0.24271414f));
+  q = __ffma2_rn(q, f, make_float2(0.69326216f, 0.69326216f));
+  q = __ffma2_rn(q, f, make_float2(0.9999196f, 0.9999196f));
+  return make_float2(__int_as_float(__float_as_int(q.x) + (__float_as_int(t.x) << 23)),
+                     __int_as_float(__float_as_int(q.y) + (__float_as_int(t.y) << 23)));
 }
 
-// P = exp2(s * scale_log2 - m) rounded to the operand type, written over S (columns
-// 0..63; the fp32-probability low parts go to columns 64..127).  Returns the fp32 sum.
+// Pairs per 16 whose exponentials go to the FMA pipe in unmasked tiles (0, 1, 2, 4, 8).
+#ifndef JT_EXP2_POLY_PAIRS
+#define JT_EXP2_POLY_PAIRS 4
+#endif
+constexpr int kPolyPairs = JT_EXP2_POLY_PAIRS;
+__host__ __device__ constexpr bool poly_pair(int c) {
+  return kPolyPairs > 0 && (c % (16 / (kPolyPairs > 0 ? kPolyPairs : 1))) ==
+                               (16 / (kPolyPairs > 0 ? kPolyPairs : 1)) - 1;
+}
+
+// One pass over a 128-key score row: the four 32-column TMEM loads are issued back to
+// back and waited once, the row stays in registers for the max and the exponentials, and
+// P = exp2(s * scale_log2 - m) (rounded to the operand type) is written over S (columns
+// 0..63; the fp32-probability low parts go to columns 64..127).  Updates the lazy running
+// max (it moves only when the tile max exceeds it by more than 8 in log2 units) and
+// returns the fp32 row sum of P; `alpha` is the factor the older O and sum must take.
 template <typename Elem, bool FP32P, bool kMasked>
-__device__ __forceinline__ float write_probabilities(uint32_t s_addr, const TileKeys& vk,
-                                                     float scale_log2, float neg_m) {
+__device__ __forceinline__ float softmax_row(uint32_t s_addr, const TileKeys& vk,
+                                             float scale_log2, float& m_run, float& alpha) {
   using Mma = jt::MmaOp<Elem>;
-  float r4[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll 1
+  uint32_t v[128];
+#pragma unroll
+  for (int h = 0; h < 4; ++h)
+    tmem_ld32(s_addr + 32 * h, *reinterpret_cast<uint32_t(*)[32]>(v + 32 * h));
+  uint32_t vw[4];
+#pragma unroll
+  for (int h = 0; h < 4; ++h) vw[h] = chunk_visibility<kMasked>(vk, h);
+  tmem_wait_ld();
+  if constexpr (kMasked) {
+#pragma unroll
+    for (int c = 0; c < 128; ++c)
+      if (!((vw[c >> 5] >> (c & 31)) & 1u)) v[c] = __float_as_uint(-INFINITY);
+  }
+  float m8[8];
+#pragma unroll
+  for (int k = 0; k < 8; ++k) m8[k] = fmaxf(__uint_as_float(v[k]), __uint_as_float(v[k + 8]));
+#pragma unroll
+  for (int c = 16; c < 128; c += 16)
+#pragma unroll
+    for (int k = 0; k < 8; ++k)
+      m8[k] = max3f(m8[k], __uint_as_float(v[c + k]), __uint_as_float(v[c + k + 8]));
+  // Raw max; scale > 0 keeps the order.
+  const float mx = max3f(max3f(m8[0], m8[1], m8[2]), max3f(m8[3], m8[4], m8[5]),
+                         fmaxf(m8[6], m8[7])) * scale_log2;
+  alpha = 1.f;
+  if (mx > m_run + 8.f) {
+    if (m_run != -INFINITY) alpha = jt::fast_exp2(m_run - mx);
+    m_run = mx;
+  }
+  const float neg_m = m_run == -INFINITY ? 0.f : -m_run;
+  const float2 scale2 = make_float2(scale_log2, scale_log2);
+  const float2 neg2 = make_float2(neg_m, neg_m);
+  float2 r2[2] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
+#pragma unroll
   for (int h = 0; h < 4; ++h) {
-    const uint32_t vw = chunk_visibility<kMasked>(vk, h);
-    uint32_t v[32];
-    tmem_ld32(s_addr + 32 * h, v);
-    tmem_wait_ld();
     uint32_t ph[16];
     uint32_t pl[FP32P ? 16 : 1];
 #pragma unroll
     for (int c = 0; c < 16; ++c) {
-      float x0 = __uint_as_float(v[2 * c]), x1 = __uint_as_float(v[2 * c + 1]);
-      if constexpr (kMasked) {
-        x0 = ((vw >> (2 * c)) & 1u) ? x0 : -INFINITY;
-        x1 = ((vw >> (2 * c + 1)) & 1u) ? x1 : -INFINITY;
-      }
-      const float p0 = jt::fast_exp2(fmaf(x0, scale_log2, neg_m));
-      const float p1 = jt::fast_exp2(fmaf(x1, scale_log2, neg_m));
-      r4[c & 3] += p0 + p1;
-      ph[c] = Mma::pack(p0, p1);
+      const float2 x = __ffma2_rn(
+          make_float2(__uint_as_float(v[32 * h + 2 * c]), __uint_as_float(v[32 * h + 2 * c + 1])),
+          scale2, neg2);
+      float2 e;
+      if (!kMasked && !FP32P && poly_pair(c))
+        e = exp2_poly2(x);
+      else
+        e = make_float2(jt::fast_exp2(x.x), jt::fast_exp2(x.y));
+      r2[c & 1] = __fadd2_rn(r2[c & 1], e);
+      ph[c] = Mma::pack(e.x, e.y);
       if constexpr (FP32P) {
         const float2 r = Mma::unpack(ph[c]);
-        pl[c] = Mma::pack(p0 - r.x, p1 - r.y);
+        pl[c] = Mma::pack(e.x - r.x, e.y - r.y);
       }
     }
     tmem_st16(s_addr + 16 * h, ph);
     if constexpr (FP32P) tmem_st16(s_addr + 64 + 16 * h, pl);
   }
-  return (r4[0] + r4[1]) + (r4[2] + r4[3]);
+  return (r2[0].x + r2[1].x) + (r2[0].y + r2[1].y);
 }
 
 template <bool FP32P>
@@ -663,28 +711,15 @@ __global__ void __launch_bounds__(kThreads, 1)
         mbar_wait(JT_BAR(kBarSFull + i), sf_par, abort);
         sf_par ^= 1u;
         tc_fence_after();
-        // Pass 1: row max over the 128 scores (raw; scale > 0 keeps the order).
-        float mx = full ? row_max<false>(s_addr, vk) : row_max<true>(s_addr, vk);
-        mx *= scale_log2;
-        // Lazy max: move only when it grows by more than 8 (log2 units).
         float alpha = 1.f;
-        bool rescale = false;
-        if (mx > m_run + 8.f) {
-          if (m_run != -INFINITY) {
-            alpha = jt::fast_exp2(m_run - mx);
-            rescale = true;
-          }
-          m_run = mx;
-        }
-        const float neg_m = m_run == -INFINITY ? 0.f : -m_run;
-        // Pass 2: probabilities, 64 keys at a time; P overwrites the S columns already read.
         float rsum = 0.f;
         if (warp_live) {
-          rsum = full ? write_probabilities<Elem, FP32P, false>(s_addr, vk, scale_log2, neg_m)
-                      : write_probabilities<Elem, FP32P, true>(s_addr, vk, scale_log2, neg_m);
+          rsum = full ? softmax_row<Elem, FP32P, false>(s_addr, vk, scale_log2, m_run, alpha)
+                      : softmax_row<Elem, FP32P, true>(s_addr, vk, scale_log2, m_run, alpha);
         } else {
           write_zero_probabilities<FP32P>(s_addr);
         }
+        const bool rescale = alpha != 1.f;
         l_run = l_run * alpha + rsum;
         // S_i ready implies the previous PV into O_i completed: rescale O_i in place.
         if (t > 0 && __any_sync(0xffffffffu, rescale)) {
