@@ -43,7 +43,8 @@ constexpr int kOffK = kOffQ + 2 * kQTileBytes;
 constexpr int kOffV = kOffK + kStages * kKVBytes;
 constexpr int kOffBar = kOffV + kStages * kKVBytes;
 constexpr int kOffMisc = kOffBar + 8 * 32;
-constexpr int kSmemBytes = kOffMisc + 64 + 1024;        // + alignment slack
+constexpr int kOffXch = kOffMisc + 64;                  // [128] float2: paired-item merge
+constexpr int kSmemBytes = kOffXch + kM * 8 + 1024;      // + alignment slack
 constexpr long long kWaitLimit = 4000000000ll;          // cycles (~2 s) per wait
 
 // TMEM column map (512 columns x 128 lanes x 32 bit): O_i and S_i, 128 columns each.
@@ -57,11 +58,12 @@ constexpr int kBarKFull = 0;                   // [kStages]  loader warps (+ TMA
 constexpr int kBarKEmpty = 2;                  // [kStages]  MMA commit after the QKs
 constexpr int kBarVFull = 4;                   // [kStages]
 constexpr int kBarVEmpty = 6;                  // [kStages]  MMA commit after the PVs
-constexpr int kBarQFull = 8;                   // loader warps
+constexpr int kBarQFull = 8;                   // loader thread 0 (+ TMA bytes)
 constexpr int kBarQEmpty = 9;                  // MMA commit after an item's last QK
 constexpr int kBarSFull = 10;                  // [2 tiles]  MMA commit per QK
 constexpr int kBarPFull = 12;                  // [2 tiles]  128 softmax threads
-constexpr int kBarPvDone = 14;                 // [2 tiles]  (unused)
+constexpr int kBarXch = 14;                    // paired items: warpgroup 1's (m, l) published
+constexpr int kBarXchFree = 15;                // paired items: warpgroup 0 has read them
 constexpr int kBarOReady = 16;                 // [2 tiles]  MMA commit after an item's last PV
 constexpr int kBarOFree = 18;                  // [2 tiles]  128 threads after the epilogue
 constexpr int kBarDrain = 20;
@@ -186,6 +188,18 @@ __device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t (&v)[16
       "r"(v[8]), "r"(v[9]), "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]),
       "r"(v[15]));
 }
+__device__ __forceinline__ void tmem_ld8(uint32_t taddr, uint32_t (&v)[8]) {
+  asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];\n"
+               : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]),
+                 "=r"(v[6]), "=r"(v[7])
+               : "r"(taddr));
+}
+__device__ __forceinline__ void tmem_st8(uint32_t taddr, const uint32_t (&v)[8]) {
+  asm volatile("tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8};\n" ::"r"(
+                   taddr),
+               "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]),
+               "r"(v[7]));
+}
 __device__ __forceinline__ void tmem_wait_ld() {
   asm volatile("tcgen05.wait::ld.sync.aligned;\n" ::: "memory");
 }
@@ -199,6 +213,15 @@ __device__ __forceinline__ void tma_load_4d(uint32_t dst, const CUtensorMap* map
       "cp.async.bulk.tensor.4d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
       " [%0], [%1, {%2, %3, %4, %5}], [%6];\n" ::"r"(dst),
       "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(bar)
+      : "memory");
+}
+
+__device__ __forceinline__ void tma_load_3d(uint32_t dst, const CUtensorMap* map, int c0, int c1,
+                                            int c2, uint32_t bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%2, %3, %4}], [%5];\n" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(c2), "r"(bar)
       : "memory");
 }
 
@@ -266,6 +289,10 @@ __device__ __forceinline__ Item decode(const JtTreeAttnParams& p, const DevLayou
   it.n_tiles = (it.key_end - it.key_begin + kN - 1) / kN;
   return it;
 }
+
+// A paired item has one query tile and at least two key tiles: both softmax warpgroups
+// work on its rows, each over every other key tile, and their results are merged.
+__device__ __forceinline__ bool paired(const Item& it) { return it.nq == 1 && it.n_tiles >= 2; }
 
 // Loads one 128-key K or V tile into its ring stage: TMA when the keys are one page's
 // prefix run, else one cp.async row per loader thread (rows past key_end zero-filled).
@@ -451,6 +478,7 @@ __device__ __forceinline__ void write_zero_probabilities(uint32_t s_addr) {
 template <typename Elem, bool FP32P>
 __global__ void __launch_bounds__(kThreads, 1)
     tree_attn_tc_kernel(const JtTreeAttnParams p, const DevLayout w,
+                        const __grid_constant__ CUtensorMap qmap,
                         const __grid_constant__ CUtensorMap kmap,
                         const __grid_constant__ CUtensorMap vmap) {
   using Mma = jt::MmaOp<Elem>;
@@ -472,11 +500,11 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (tid == 0) {
     for (int i = 0; i < kNumBars; ++i) {
       uint32_t count = 1;
-      if (i == kBarPFull || i == kBarPFull + 1 || i == kBarOFree || i == kBarOFree + 1)
+      if (i == kBarPFull || i == kBarPFull + 1 || i == kBarOFree || i == kBarOFree + 1 ||
+          i == kBarXch || i == kBarXchFree)
         count = 128;
       if (i == kBarItemEmpty || i == kBarItemEmpty + 1) count = kItemConsumers;
-      if (i == kBarQFull || (i >= kBarKFull && i < kBarKFull + kStages) ||
-          (i >= kBarVFull && i < kBarVFull + kStages))
+      if ((i >= kBarKFull && i < kBarKFull + kStages) || (i >= kBarVFull && i < kBarVFull + kStages))
         count = kLoaderWarps;
       mbar_init(JT_BAR(i), count);
     }
@@ -515,11 +543,11 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   if (warp == 0) {
     // ------------------------------------------------------------------ MMA issuer
-    // Issue order per key tile t and query tile i: PV_i(t) then QK_i(t+1).  tcgen05.mma
-    // instructions of one thread execute in issue order, so PV_i(t) has read P out of S_i
-    // before QK_i(t+1) overwrites S_i, and the commit that signals S_i(t+1) also covers
-    // PV_i(t): the softmax may then rescale O_i.  While the softmax of one query tile
-    // runs, the tensor core works on the other tile.
+    // Issue order per key step and query-tile slot i: PV_i then the slot's next QK_i.
+    // tcgen05.mma instructions of one thread execute in issue order, so PV_i has read P
+    // out of S_i before the next QK_i overwrites S_i, and the commit that signals the new
+    // S_i also covers PV_i: the softmax may then rescale O_i.  While the softmax of one
+    // slot runs, the tensor core works on the other slot.
     uint32_t kc = 0, vc = 0, q_count = 0;
     uint32_t pf_par = 0, of_par = 0, of_seen = 0;
     for (uint32_t seq = 0;; ++seq) {
@@ -527,12 +555,22 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (index < 0) break;
       if (lane != 0) continue;
       const Item it = decode(p, w, index, split_keys);
-      const int nq = it.nq, n_tiles = it.n_tiles;
+      const int n = it.n_tiles;
+      const bool pair = paired(it);
+      const int slots = pair ? 2 : it.nq;
+      int qk_left = pair ? n : it.nq * n;  // QKs still to issue for this item
+      int pv_left = qk_left;
       mbar_wait(JT_BAR(kBarQFull), q_count & 1, abort);
       ++q_count;
       tc_fence_after();
+      auto wait_k = [&]() -> int {
+        const int stage = kc % kStages;
+        mbar_wait(JT_BAR(kBarKFull + stage), (kc / kStages) & 1, abort);
+        tc_fence_after();
+        return stage;
+      };
       auto issue_qk = [&](int i, int stage) {
-        const uint32_t qa = base + kOffQ + i * kQTileBytes;
+        const uint32_t qa = base + kOffQ + (pair ? 0 : i) * kQTileBytes;
         const uint32_t ka = base + kOffK + stage * kKVBytes;
 #pragma unroll
         for (int kk = 0; kk < kD / 16; ++kk) {
@@ -542,24 +580,36 @@ __global__ void __launch_bounds__(kThreads, 1)
                  kk > 0 ? 1u : 0u);
         }
         tc_commit(JT_BAR(kBarSFull + i));
+        if (--qk_left == 0) tc_commit(JT_BAR(kBarQEmpty));
       };
-      {
-        const int stage = kc % kStages;
-        mbar_wait(JT_BAR(kBarKFull + stage), (kc / kStages) & 1, abort);
-        tc_fence_after();
-        for (int i = 0; i < nq; ++i) issue_qk(i, stage);
+      // First S of every slot.  A paired item gives each slot its own K tile (tiles 0
+      // and 1); otherwise both query tiles share tile 0.
+      if (pair) {
+        for (int i = 0; i < 2; ++i) {
+          const int stage = wait_k();
+          issue_qk(i, stage);
+          tc_commit(JT_BAR(kBarKEmpty + stage));
+          ++kc;
+        }
+      } else {
+        const int stage = wait_k();
+        for (int i = 0; i < it.nq; ++i) issue_qk(i, stage);
         tc_commit(JT_BAR(kBarKEmpty + stage));
-        if (n_tiles == 1) tc_commit(JT_BAR(kBarQEmpty));
         ++kc;
       }
-      for (int t = 0; t < n_tiles; ++t) {
-        const int vstage = vc % kStages;
-        const int kstage = kc % kStages;
-        const bool more = t + 1 < n_tiles;
-        mbar_wait(JT_BAR(kBarVFull + vstage), (vc / kStages) & 1, abort);
-        const uint32_t va = base + kOffV + vstage * kKVBytes;
-        for (int i = 0; i < nq; ++i) {
-          if (t == 0 && ((of_seen >> i) & 1u)) {
+      const int steps = pair ? (n + 1) / 2 : n;
+      for (int s = 0; s < steps; ++s) {
+        int vstage = 0, kstage = 0;
+        auto wait_v = [&]() {
+          vstage = vc % kStages;
+          mbar_wait(JT_BAR(kBarVFull + vstage), (vc / kStages) & 1, abort);
+        };
+        if (!pair) wait_v();
+        for (int i = 0; i < slots; ++i) {
+          const int t = pair ? 2 * s + i : s;
+          if (t >= n) break;  // paired item with an odd tile count
+          if (pair) wait_v();
+          if (s == 0 && ((of_seen >> i) & 1u)) {
             mbar_wait(JT_BAR(kBarOFree + i), (of_par >> i) & 1u, abort);
             of_par ^= 1u << i;
           }
@@ -568,31 +618,46 @@ __global__ void __launch_bounds__(kThreads, 1)
           tc_fence_after();
           // O_i += P V (P over S_i in TMEM, V MN-major in shared memory).
           const uint32_t pa = tmem + col_s(i);
+          const uint32_t va = base + kOffV + vstage * kKVBytes;
 #pragma unroll
           for (int kk = 0; kk < kN / 16; ++kk) {
             const uint64_t b = smem_desc(va + kk * 2048, kKVHalfBytes, 1024);
-            mma_ts(tmem + col_o(i), pa + kk * 8, b, kIdescPV, (t > 0 || kk > 0) ? 1u : 0u);
+            mma_ts(tmem + col_o(i), pa + kk * 8, b, kIdescPV, (s > 0 || kk > 0) ? 1u : 0u);
             if constexpr (FP32P)
               mma_ts(tmem + col_o(i), pa + 64 + kk * 8, b, kIdescPV, 1u);
           }
-          if (!more) tc_commit(JT_BAR(kBarOReady + i));
-          if (more) {
-            if (i == 0) {
-              mbar_wait(JT_BAR(kBarKFull + kstage), (kc / kStages) & 1, abort);
-              tc_fence_after();
+          --pv_left;
+          if (pair) {
+            tc_commit(JT_BAR(kBarVEmpty + vstage));
+            ++vc;
+          }
+          if (t + (pair ? 2 : 1) < n) {
+            if (pair) {
+              const int stage = wait_k();
+              issue_qk(i, stage);
+              tc_commit(JT_BAR(kBarKEmpty + stage));
+              ++kc;
+            } else {
+              if (i == 0) kstage = wait_k();
+              issue_qk(i, kstage);
             }
-            issue_qk(i, kstage);
+          } else if (!pair) {
+            tc_commit(JT_BAR(kBarOReady + i));
+          }
+          // A paired item's two accumulators are merged by warpgroup 0 after both slots'
+          // last PVs: one commit after the item's final PV covers both.
+          if (pair && pv_left == 0) tc_commit(JT_BAR(kBarOReady));
+        }
+        if (!pair) {
+          tc_commit(JT_BAR(kBarVEmpty + vstage));
+          ++vc;
+          if (s + 1 < n) {
+            tc_commit(JT_BAR(kBarKEmpty + kstage));
+            ++kc;
           }
         }
-        tc_commit(JT_BAR(kBarVEmpty + vstage));
-        ++vc;
-        if (more) {
-          tc_commit(JT_BAR(kBarKEmpty + kstage));
-          if (t + 2 == n_tiles) tc_commit(JT_BAR(kBarQEmpty));
-          ++kc;
-        }
       }
-      for (int i = 0; i < nq; ++i) of_seen |= 1u << i;
+      for (int i = 0; i < slots; ++i) of_seen |= 1u << i;
     }
     if (lane == 0) {
       // Drain: every MMA this thread issued has completed before TMEM is released.
@@ -602,7 +667,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   } else if (warp < 4) {
     // ------------------------------------------------------------------ loaders
     const int ltid = tid - 32;
-    uint32_t kc = 0, vc = 0;
+    uint32_t kc = 0, vc = 0, q_fills = 0;
     uint32_t filled = 0;       // bit (2*stage + v): last fill of that ring slot was TMA
     uint32_t last_parity = 0;  // same bits: phase parity of that fill
     const int64_t pool_slots = p.num_blocks * static_cast<int64_t>(bs);
@@ -619,57 +684,60 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (index < 0) break;
       const Item it = decode(p, w, index, split_keys);
       const int32_t* table = p.block_tables + static_cast<int64_t>(it.r) * p.table_stride0;
-      // Query tiles (cp.async, swizzled).  Rows past the request's nodes are zero.  Each
-      // loader warp waits for its own copies, fences them for the tensor core (async
-      // proxy) and arrives once.
-      if (seq > 0) mbar_wait(JT_BAR(kBarQEmpty), (seq - 1) & 1, abort);
-      const int qrows = it.nq * kM;
-      for (int c = ltid; c < qrows * 16; c += 96) {
-        const int row = c >> 4, chunk = c & 15;
-        const int gm = it.tp * 2 * kM + row;
-        const int j = gm / G, g = gm - j * G;
-        const bool ok = j < it.T;
-        const char* src = static_cast<const char*>(p.q);
-        if (ok)
-          src += (static_cast<int64_t>(it.q_start + j) * p.q_stride0 +
-                  static_cast<int64_t>(it.h * G + g) * p.q_stride1 + chunk * 8) * 2;
-        const uint32_t dst = base + kOffQ + (row >> 7) * kQTileBytes + swz128(row & 127, chunk, kM);
-        jt::cp_async_16(dst, src, ok ? 16 : 0);
+      // Query tiles: one TMA box of 128/groups nodes x groups heads x 64 dims per half,
+      // once the previous item's last QK has read the buffer.  Rows past the request's
+      // nodes hold other requests' queries (or zeros past the end); their score rows are
+      // never written out.
+      if (ltid == 0) {
+        if (seq > 0) mbar_wait(JT_BAR(kBarQEmpty), (seq - 1) & 1, abort);
+        mbar_arrive_tx(JT_BAR(kBarQFull), it.nq * kQTileBytes);
+        const int node0 = it.q_start + it.tp * (2 * kM / G);
+        for (int i = 0; i < it.nq; ++i) {
+          const uint32_t dst = base + kOffQ + i * kQTileBytes;
+          const int node = node0 + i * (kM / G);
+          tma_load_3d(dst, &qmap, 0, it.h * G, node, JT_BAR(kBarQFull));
+          tma_load_3d(dst + kQHalfBytes, &qmap, 64, it.h * G, node, JT_BAR(kBarQFull));
+        }
+        ++q_fills;
       }
-      asm volatile("cp.async.wait_all;\n" ::: "memory");
-      fence_proxy_async();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(JT_BAR(kBarQFull));
-
-      for (int t = 0; t < it.n_tiles; ++t) {
+      auto load_k = [&](int t) {
         const int kb = it.key_begin + t * kN;
         const bool full = kb + kN <= min(it.P, it.key_end);
         const int page = (full && ltid == 0) ? __ldg(table + kb / bs) : 0;
         // Every loader thread waits for every refill, in order.
-        {
-          const int stage = kc % kStages;
-          const uint32_t parity = (kc / kStages) & 1;
-          if (kc >= kStages) mbar_wait(JT_BAR(kBarKEmpty + stage), parity ^ 1, abort);
-          load_kv_tile(p, it, table, kb, full, ltid, lane, base + kOffK + stage * kKVBytes, &kmap,
-                       static_cast<const char*>(p.k_pool), p.k_stride0, p.k_stride1, p.k_stride2,
-                       JT_BAR(kBarKFull + stage), pool_slots, page);
-          const uint32_t bit = 1u << (2 * stage);
-          if (full) { filled |= bit; last_parity = (last_parity & ~bit) | (parity ? bit : 0u); }
-          else filled &= ~bit;
-          ++kc;
-        }
-        {
-          const int stage = vc % kStages;
-          const uint32_t parity = (vc / kStages) & 1;
-          if (vc >= kStages) mbar_wait(JT_BAR(kBarVEmpty + stage), parity ^ 1, abort);
-          load_kv_tile(p, it, table, kb, full, ltid, lane, base + kOffV + stage * kKVBytes, &vmap,
-                       static_cast<const char*>(p.v_pool), p.v_stride0, p.v_stride1, p.v_stride2,
-                       JT_BAR(kBarVFull + stage), pool_slots, page);
-          const uint32_t bit = 2u << (2 * stage);
-          if (full) { filled |= bit; last_parity = (last_parity & ~bit) | (parity ? bit : 0u); }
-          else filled &= ~bit;
-          ++vc;
-        }
+        const int stage = kc % kStages;
+        const uint32_t parity = (kc / kStages) & 1;
+        if (kc >= kStages) mbar_wait(JT_BAR(kBarKEmpty + stage), parity ^ 1, abort);
+        load_kv_tile(p, it, table, kb, full, ltid, lane, base + kOffK + stage * kKVBytes, &kmap,
+                     static_cast<const char*>(p.k_pool), p.k_stride0, p.k_stride1, p.k_stride2,
+                     JT_BAR(kBarKFull + stage), pool_slots, page);
+        const uint32_t bit = 1u << (2 * stage);
+        if (full) { filled |= bit; last_parity = (last_parity & ~bit) | (parity ? bit : 0u); }
+        else filled &= ~bit;
+        ++kc;
+      };
+      auto load_v = [&](int t) {
+        const int kb = it.key_begin + t * kN;
+        const bool full = kb + kN <= min(it.P, it.key_end);
+        const int page = (full && ltid == 0) ? __ldg(table + kb / bs) : 0;
+        const int stage = vc % kStages;
+        const uint32_t parity = (vc / kStages) & 1;
+        if (vc >= kStages) mbar_wait(JT_BAR(kBarVEmpty + stage), parity ^ 1, abort);
+        load_kv_tile(p, it, table, kb, full, ltid, lane, base + kOffV + stage * kKVBytes, &vmap,
+                     static_cast<const char*>(p.v_pool), p.v_stride0, p.v_stride1, p.v_stride2,
+                     JT_BAR(kBarVFull + stage), pool_slots, page);
+        const uint32_t bit = 2u << (2 * stage);
+        if (full) { filled |= bit; last_parity = (last_parity & ~bit) | (parity ? bit : 0u); }
+        else filled &= ~bit;
+        ++vc;
+      };
+      // Fill order = the MMA's consumption order: K t, V t per tile; for a paired item
+      // K t, K t+1, V t, V t+1 per tile pair (the slots' next K tiles arrive early).
+      const int unit = paired(it) ? 2 : 1;
+      for (int t0 = 0; t0 < it.n_tiles; t0 += unit) {
+        const int t1 = min(t0 + unit, it.n_tiles);
+        for (int t = t0; t < t1; ++t) load_k(t);
+        for (int t = t0; t < t1; ++t) load_v(t);
       }
     }
     // Drain: the TMA copies this thread issued have landed before the CTA exits.
@@ -680,22 +748,30 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (filled & (2u << (2 * s)))
           mbar_wait(JT_BAR(kBarVFull + s), (last_parity >> (2 * s + 1)) & 1u, abort, false);
       }
+      if (q_fills > 0) mbar_wait(JT_BAR(kBarQFull), (q_fills - 1) & 1u, abort, false);
     }
   } else {
     // ------------------------------------------------------------------ softmax + epilogue
-    const int i = (warp - 4) >> 2;          // query tile of this warpgroup
+    const int i = (warp - 4) >> 2;          // query-tile slot of this warpgroup
     const int t128 = tid - 128 - i * 128;   // row within the query tile
     const uint32_t lane_base = static_cast<uint32_t>((t128 >> 5) * 32) << 16;
     const uint32_t s_addr = tmem + lane_base + col_s(i);
     const uint32_t o_addr = tmem + lane_base + col_o(i);
+    const uint32_t o1_addr = tmem + lane_base + col_o(1);
+    float2* xch = reinterpret_cast<float2*>(sbase + kOffXch);
     const float scale_log2 = p.scale * 1.4426950408889634f;
-    uint32_t sf_par = 0, or_par = 0;
+    uint32_t sf_par = 0, or_par = 0, xch_count = 0;  // xch_count: paired items so far
     for (uint32_t seq = 0;; ++seq) {
       const int index = next_item(seq);
       if (index < 0) break;
       const Item it = decode(p, w, index, split_keys);
-      if (i >= it.nq) continue;
-      const int gm = it.tp * 2 * kM + i * kM + t128;
+      const int n = it.n_tiles;
+      const bool pair = paired(it);
+      if (!pair && i >= it.nq) continue;
+      // A paired item (one query tile, two or more key tiles) gives both warpgroups the
+      // same rows: warpgroup i takes key tiles i, i + 2, ... into its own S_i / O_i.
+      const int qi = pair ? 0 : i;
+      const int gm = it.tp * 2 * kM + qi * kM + t128;
       const int j = gm / G, g = gm - j * G;
       const bool row_ok = j < it.T;
       const bool warp_live = __any_sync(0xffffffffu, row_ok);
@@ -703,7 +779,8 @@ __global__ void __launch_bounds__(kThreads, 1)
           w.masks + static_cast<int64_t>(it.q_start + (row_ok ? j : 0)) * w.mask_words;
       float m_run = -INFINITY;  // running max in log2 units (scaled scores)
       float l_run = 0.f;
-      for (int t = 0; t < it.n_tiles; ++t) {
+      const int t_first = pair ? i : 0, t_step = pair ? 2 : 1;
+      for (int t = t_first; t < n; t += t_step) {
         const int kb = it.key_begin + t * kN;
         const bool full = kb + kN <= min(it.P, it.key_end);
         // Keys of this tile; prefix-only tiles skip masking entirely.
@@ -719,10 +796,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         } else {
           write_zero_probabilities<FP32P>(s_addr);
         }
-        const bool rescale = alpha != 1.f;
         l_run = l_run * alpha + rsum;
         // S_i ready implies the previous PV into O_i completed: rescale O_i in place.
-        if (t > 0 && __any_sync(0xffffffffu, rescale)) {
+        if (t > t_first && __any_sync(0xffffffffu, alpha != 1.f)) {
 #pragma unroll 1
           for (int chunk = 0; chunk < 4; ++chunk) {
             uint32_t o[32];
@@ -737,20 +813,51 @@ __global__ void __launch_bounds__(kThreads, 1)
         tc_fence_before();
         mbar_arrive(JT_BAR(kBarPFull + i));
       }
-      // Epilogue: wait for the item's last PV into O_i.
+      if (pair && i == 1) {
+        // Hand this half's running max and sum to warpgroup 0, which merges O_1 into its
+        // own result, once warpgroup 0 has read the previous paired item's values.
+        if (xch_count > 0) mbar_wait(JT_BAR(kBarXchFree), (xch_count - 1) & 1u, abort);
+        xch[t128] = make_float2(m_run, l_run);
+        mbar_arrive(JT_BAR(kBarXch));
+        ++xch_count;
+        continue;
+      }
+      // Epilogue: wait for the item's last PV into O_i (both accumulators when paired).
       mbar_wait(JT_BAR(kBarOReady + i), or_par, abort);
       or_par ^= 1u;
       tc_fence_after();
+      float a0 = 1.f, a1 = 0.f;
+      if (pair) {
+        mbar_wait(JT_BAR(kBarXch), xch_count & 1u, abort);
+        const float2 ml1 = xch[t128];
+        mbar_arrive(JT_BAR(kBarXchFree));
+        ++xch_count;
+        const float m = fmaxf(m_run, ml1.x);
+        const float mref = m == -INFINITY ? 0.f : m;
+        a0 = jt::fast_exp2(m_run - mref);
+        a1 = jt::fast_exp2(ml1.x - mref);
+        l_run = a0 * l_run + a1 * ml1.y;
+        m_run = m;
+      }
       const bool split_item = it.n_split > 1;
       const int64_t slot = it.slot_base +
                            (static_cast<int64_t>(it.h) * it.mblocks + it.tp) * it.n_split + it.split;
-      const int item_row = i * kM + t128;
+      const int item_row = qi * kM + t128;
       const float inv = 1.f / l_run;
 #pragma unroll 1
       for (int chunk = 0; chunk < 4; ++chunk) {
         uint32_t o[32];
         tmem_ld32(o_addr + chunk * 32, o);
-        tmem_wait_ld();
+        if (pair) {
+          uint32_t o1[32];
+          tmem_ld32(o1_addr + chunk * 32, o1);
+          tmem_wait_ld();
+#pragma unroll
+          for (int c = 0; c < 32; ++c)
+            o[c] = __float_as_uint(a0 * __uint_as_float(o[c]) + a1 * __uint_as_float(o1[c]));
+        } else {
+          tmem_wait_ld();
+        }
         if (split_item) {
           float4* dst = reinterpret_cast<float4*>(w.part_o + (slot * (2 * kM) + item_row) * kD +
                                                   chunk * 32);
@@ -782,6 +889,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       tc_fence_before();
       mbar_arrive(JT_BAR(kBarOFree + i));
+      if (pair) mbar_arrive(JT_BAR(kBarOFree + 1));
       if (split_item) {
         // Per-row merge: each row publishes its partial (max in log2 units, sum), then bumps
         // its own counter; the split that completes a row merges that row.  Rows never

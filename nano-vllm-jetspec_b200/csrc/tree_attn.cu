@@ -756,12 +756,39 @@ bool encode_pool_map(CUtensorMap* map, const void* pool, int32_t dtype, int64_t 
   return rc == CUDA_SUCCESS;
 }
 
-// The tcgen05 core covers head_dim 128, pages that hold whole 64-key tiles and outputs
-// whose rows allow 16-byte stores; anything else runs on the portable core.
+// 3-D map over the packed queries [total_queries, heads, 128] (strides in elements): a box
+// is 128/groups nodes x the groups query heads of one KV head x 64 dims, i.e. 128 score
+// rows of a query tile in (node, group) order, with the MMA operand's 128-byte swizzle.
+bool encode_query_map(CUtensorMap* map, const JtTreeAttnParams& p) {
+  auto encode = tensor_map_encoder();
+  if (encode == nullptr) return false;
+  const int heads = p.num_kv_heads * p.groups;
+  const cuuint64_t dims[3] = {static_cast<cuuint64_t>(tc::kD), static_cast<cuuint64_t>(heads),
+                              static_cast<cuuint64_t>(p.total_queries)};
+  const cuuint64_t strides[2] = {static_cast<cuuint64_t>(p.q_stride1 * 2),
+                                 static_cast<cuuint64_t>(p.q_stride0 * 2)};
+  const cuuint32_t box[3] = {64, static_cast<cuuint32_t>(p.groups),
+                             static_cast<cuuint32_t>(tc::kM / p.groups)};
+  const cuuint32_t elem[3] = {1, 1, 1};
+  const CUresult rc = encode(map,
+                             p.dtype == JT_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
+                                                : CU_TENSOR_MAP_DATA_TYPE_FLOAT16,
+                             3, const_cast<void*>(p.q), dims, strides, box, elem,
+                             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                             CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return rc == CUDA_SUCCESS;
+}
+
+// The tcgen05 core covers head_dim 128, pages that hold whole 128-key tiles, group counts
+// that divide a 128-row query tile into whole nodes, 16-byte aligned query rows (TMA) and
+// outputs whose rows allow 16-byte stores; anything else runs on the portable core.
 bool tcgen05_eligible(const JtTreeAttnParams& p) {
   if (p.flags & JT_FLAG_PORTABLE_CORE) return false;
   if (p.head_dim != tc::kD || p.block_size % tc::kN != 0) return false;
+  if (p.groups > tc::kM || tc::kM % p.groups != 0) return false;
   if ((p.out_stride0 | p.out_stride1) % 8 != 0) return false;
+  if ((p.q_stride0 | p.q_stride1) % 8 != 0 || !al16(p.q)) return false;
   int dev = 0, major = 0;
   if (cudaGetDevice(&dev) != cudaSuccess) return false;
   if (cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev) != cudaSuccess)
@@ -771,7 +798,8 @@ bool tcgen05_eligible(const JtTreeAttnParams& p) {
 
 template <typename Elem, bool FP32P>
 int launch_tc(const JtTreeAttnParams& p, const Layout& L, const DevLayout& d,
-              const CUtensorMap& kmap, const CUtensorMap& vmap, cudaStream_t stream) {
+              const CUtensorMap& qmap, const CUtensorMap& kmap, const CUtensorMap& vmap,
+              cudaStream_t stream) {
   auto kernel = tc::tree_attn_tc_kernel<Elem, FP32P>;
   int rc = jt_cuda_check(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                               tc::kSmemBytes),
@@ -785,13 +813,15 @@ int launch_tc(const JtTreeAttnParams& p, const Layout& L, const DevLayout& d,
   rc = jt_cuda_check(cudaGetLastError(), "plan launch");
   if (rc != JT_OK) return rc;
   const int grid = std::min(sms, L.max_items);
-  kernel<<<grid, tc::kThreads, tc::kSmemBytes, stream>>>(p, d, kmap, vmap);
+  kernel<<<grid, tc::kThreads, tc::kSmemBytes, stream>>>(p, d, qmap, kmap, vmap);
   return jt_cuda_check(cudaGetLastError(), "tcgen05 attention launch");
 }
 
 int dispatch_tc(const JtTreeAttnParams& p, const Layout& L, const DevLayout& d,
                 cudaStream_t stream) {
-  CUtensorMap kmap, vmap;
+  CUtensorMap qmap, kmap, vmap;
+  if (!encode_query_map(&qmap, p))
+    return jt_fail(JT_ERR_CUDA, "tree_attn: cuTensorMapEncodeTiled rejected the query layout");
   if (!encode_pool_map(&kmap, p.k_pool, p.dtype, p.num_blocks, p.block_size, p.num_kv_heads,
                        p.k_stride0, p.k_stride1, p.k_stride2) ||
       !encode_pool_map(&vmap, p.v_pool, p.dtype, p.num_blocks, p.block_size, p.num_kv_heads,
@@ -799,10 +829,10 @@ int dispatch_tc(const JtTreeAttnParams& p, const Layout& L, const DevLayout& d,
     return jt_fail(JT_ERR_CUDA, "tree_attn: cuTensorMapEncodeTiled rejected the KV pool layout");
   const bool fp32p = (p.flags & JT_FLAG_FP32_PROBABILITY) != 0;
   if (p.dtype == JT_BF16)
-    return fp32p ? launch_tc<__nv_bfloat16, true>(p, L, d, kmap, vmap, stream)
-                 : launch_tc<__nv_bfloat16, false>(p, L, d, kmap, vmap, stream);
-  return fp32p ? launch_tc<__half, true>(p, L, d, kmap, vmap, stream)
-               : launch_tc<__half, false>(p, L, d, kmap, vmap, stream);
+    return fp32p ? launch_tc<__nv_bfloat16, true>(p, L, d, qmap, kmap, vmap, stream)
+                 : launch_tc<__nv_bfloat16, false>(p, L, d, qmap, kmap, vmap, stream);
+  return fp32p ? launch_tc<__half, true>(p, L, d, qmap, kmap, vmap, stream)
+               : launch_tc<__half, false>(p, L, d, qmap, kmap, vmap, stream);
 }
 
 }  // namespace
