@@ -43,8 +43,9 @@ constexpr int kOffK = kOffQ + 2 * kQTileBytes;
 constexpr int kOffV = kOffK + kStages * kKVBytes;
 constexpr int kOffBar = kOffV + kStages * kKVBytes;
 constexpr int kOffMisc = kOffBar + 8 * 32;
-constexpr int kOffXch = kOffMisc + 64;                  // [128] float2: paired-item merge
-constexpr int kSmemBytes = kOffXch + kM * 8 + 1024;      // + alignment slack
+constexpr int kOffXl = kOffMisc + 64;                   // [2 tiles][2 halves][128] row sums
+constexpr int kOffXm = kOffXl + 2 * 2 * kM * 4;         // [2 tiles][2 halves][128] half maxima
+constexpr int kSmemBytes = kOffXm + 2 * 2 * kM * 4 + 1024;  // + alignment slack
 constexpr long long kWaitLimit = 4000000000ll;          // cycles (~2 s) per wait
 
 // TMEM column map (512 columns x 128 lanes x 32 bit): O_i and S_i, 128 columns each.
@@ -52,6 +53,13 @@ constexpr long long kWaitLimit = 4000000000ll;          // cycles (~2 s) per wai
 // are written over S_i.
 __host__ __device__ constexpr uint32_t col_o(int i) { return 128u * i; }
 __host__ __device__ constexpr uint32_t col_s(int i) { return 256u + 128u * i; }
+// P of keys 16kk..16kk+15 (operand-type pairs, 8 columns) inside S_i: each softmax
+// warpgroup writes the probabilities of its 64 keys inside the S columns it owns (keys
+// 0..63 -> columns 0..31, keys 64..127 -> columns 64..95); fp32-probability low parts
+// follow 32 columns later.
+__host__ __device__ constexpr uint32_t col_p(int kk) {
+  return kk < 4 ? 8u * kk : 64u + 8u * (kk - 4);
+}
 
 // Barrier indices.
 constexpr int kBarKFull = 0;                   // [kStages]  loader warps (+ TMA bytes)
@@ -61,15 +69,15 @@ constexpr int kBarVEmpty = 6;                  // [kStages]  MMA commit after th
 constexpr int kBarQFull = 8;                   // loader thread 0 (+ TMA bytes)
 constexpr int kBarQEmpty = 9;                  // MMA commit after an item's last QK
 constexpr int kBarSFull = 10;                  // [2 tiles]  MMA commit per QK
-constexpr int kBarPFull = 12;                  // [2 tiles]  128 softmax threads
-constexpr int kBarXch = 14;                    // paired items: warpgroup 1's (m, l) published
-constexpr int kBarXchFree = 15;                // paired items: warpgroup 0 has read them
+constexpr int kBarPFull = 12;                  // [2 tiles]  256 softmax threads
+constexpr int kBarLx = 14;                     // [2 tiles]  256 softmax threads: row sums swapped
+constexpr int kBarMx = 25;                     // [2 tiles]  256 softmax threads: half maxima swapped
 constexpr int kBarOReady = 16;                 // [2 tiles]  MMA commit after an item's last PV
-constexpr int kBarOFree = 18;                  // [2 tiles]  128 threads after the epilogue
+constexpr int kBarOFree = 18;                  // [2 tiles]  256 threads after the epilogue
 constexpr int kBarDrain = 20;
 constexpr int kBarItemFull = 21;               // [2] work-item ring
 constexpr int kBarItemEmpty = 23;              // [2]
-constexpr int kNumBars = 25;
+constexpr int kNumBars = 27;
 constexpr int kItemConsumers = 12;             // every warp of the CTA reads each item
 constexpr int kLoaderWarps = 3;
 static_assert(kNumBars * 8 <= 8 * 32, "barrier area");
@@ -393,85 +401,115 @@ __host__ __device__ constexpr bool poly_pair(int c) {
                                (16 / (kPolyPairs > 0 ? kPolyPairs : 1)) - 1;
 }
 
-// One pass over a 128-key score row: the four 32-column TMEM loads are issued back to
-// back and waited once, the row stays in registers for the max and the exponentials, and
-// P = exp2(s * scale_log2 - m) (rounded to the operand type) is written over S (columns
-// 0..63; the fp32-probability low parts go to columns 64..127).  Updates the lazy running
-// max (it moves only when the tile max exceeds it by more than 8 in log2 units) and
-// returns the fp32 row sum of P; `alpha` is the factor the older O and sum must take.
+// Softmax of one score row for one key half.  The two softmax warpgroups share every
+// 128-key tile: warpgroup `c` owns keys 64c..64c+63, i.e. S columns 64c..64c+63, and only
+// ever reads or writes those.  Each thread loads its 64 scores (two 32-column TMEM loads,
+// one wait), publishes its half's max in `xm` and meets the other warpgroup on `mx_bar`
+// (a 256-thread rendezvous), so both derive the same running max.  The running max is
+// lazy: it moves only when the tile max exceeds it by more than 8 (log2 units); then this
+// half's O columns are rescaled in TMEM when `may_rescale` (O holds earlier tiles).  P =
+// exp2(s * scale_log2 - m), rounded to the operand type, goes to this half's columns
+// (col_p).  Returns the fp32 sum of this half's P; `alpha` is the factor the older partial
+// sum must take.
 template <typename Elem, bool FP32P, bool kMasked>
-__device__ __forceinline__ float softmax_row(uint32_t s_addr, const TileKeys& vk,
-                                             float scale_log2, float& m_run, float& alpha) {
+__device__ __forceinline__ float softmax_half(uint32_t s_addr, uint32_t o_addr, int c,
+                                              const TileKeys& vk, float scale_log2,
+                                              float& m_run, float& alpha, bool may_rescale,
+                                              float* xm_mine, const float* xm_other,
+                                              uint32_t mx_bar, uint32_t mx_parity,
+                                              volatile int* abort) {
   using Mma = jt::MmaOp<Elem>;
-  uint32_t v[128];
+  const int own = 64 * c;
+  uint32_t v[64];
 #pragma unroll
-  for (int h = 0; h < 4; ++h)
-    tmem_ld32(s_addr + 32 * h, *reinterpret_cast<uint32_t(*)[32]>(v + 32 * h));
-  uint32_t vw[4];
+  for (int h = 0; h < 2; ++h)
+    tmem_ld32(s_addr + own + 32 * h, *reinterpret_cast<uint32_t(*)[32]>(v + 32 * h));
+  uint32_t vw[2];
+  if constexpr (kMasked) {
 #pragma unroll
-  for (int h = 0; h < 4; ++h) vw[h] = chunk_visibility<kMasked>(vk, h);
+    for (int h = 0; h < 2; ++h) vw[h] = chunk_visibility<true>(vk, 2 * c + h);
+  }
   tmem_wait_ld();
   if constexpr (kMasked) {
 #pragma unroll
-    for (int c = 0; c < 128; ++c)
-      if (!((vw[c >> 5] >> (c & 31)) & 1u)) v[c] = __float_as_uint(-INFINITY);
+    for (int k = 0; k < 64; ++k)
+      if (!((vw[k >> 5] >> (k & 31)) & 1u)) v[k] = __float_as_uint(-INFINITY);
   }
   float m8[8];
 #pragma unroll
   for (int k = 0; k < 8; ++k) m8[k] = fmaxf(__uint_as_float(v[k]), __uint_as_float(v[k + 8]));
 #pragma unroll
-  for (int c = 16; c < 128; c += 16)
+  for (int k0 = 16; k0 < 64; k0 += 16)
 #pragma unroll
     for (int k = 0; k < 8; ++k)
-      m8[k] = max3f(m8[k], __uint_as_float(v[c + k]), __uint_as_float(v[c + k + 8]));
+      m8[k] = max3f(m8[k], __uint_as_float(v[k0 + k]), __uint_as_float(v[k0 + k + 8]));
+  const float half_max = max3f(max3f(m8[0], m8[1], m8[2]), max3f(m8[3], m8[4], m8[5]),
+                               fmaxf(m8[6], m8[7]));
+  *xm_mine = half_max;
+  mbar_arrive(mx_bar);
+  mbar_wait(mx_bar, mx_parity, abort);
   // Raw max; scale > 0 keeps the order.
-  const float mx = max3f(max3f(m8[0], m8[1], m8[2]), max3f(m8[3], m8[4], m8[5]),
-                         fmaxf(m8[6], m8[7])) * scale_log2;
+  const float mx = fmaxf(half_max, *xm_other) * scale_log2;
   alpha = 1.f;
   if (mx > m_run + 8.f) {
     if (m_run != -INFINITY) alpha = jt::fast_exp2(m_run - mx);
     m_run = mx;
   }
   const float neg_m = m_run == -INFINITY ? 0.f : -m_run;
+  // The previous PV into O completed before this S was produced: rescale in place.
+  if (may_rescale && __any_sync(0xffffffffu, alpha != 1.f)) {
+#pragma unroll 1
+    for (int chunk = 0; chunk < 2; ++chunk) {
+      uint32_t o[32];
+      tmem_ld32(o_addr + own + chunk * 32, o);
+      tmem_wait_ld();
+#pragma unroll
+      for (int k = 0; k < 32; ++k) o[k] = __float_as_uint(__uint_as_float(o[k]) * alpha);
+      tmem_st32(o_addr + own + chunk * 32, o);
+    }
+  }
   const float2 scale2 = make_float2(scale_log2, scale_log2);
   const float2 neg2 = make_float2(neg_m, neg_m);
   float2 r2[2] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
+  const uint32_t p_addr = s_addr + col_p(4 * c);
 #pragma unroll
-  for (int h = 0; h < 4; ++h) {
+  for (int h = 0; h < 2; ++h) {
     uint32_t ph[16];
     uint32_t pl[FP32P ? 16 : 1];
 #pragma unroll
-    for (int c = 0; c < 16; ++c) {
+    for (int k = 0; k < 16; ++k) {
       const float2 x = __ffma2_rn(
-          make_float2(__uint_as_float(v[32 * h + 2 * c]), __uint_as_float(v[32 * h + 2 * c + 1])),
+          make_float2(__uint_as_float(v[32 * h + 2 * k]), __uint_as_float(v[32 * h + 2 * k + 1])),
           scale2, neg2);
       float2 e;
-      if (!kMasked && !FP32P && poly_pair(c))
+      if (!kMasked && !FP32P && poly_pair(k))
         e = exp2_poly2(x);
       else
         e = make_float2(jt::fast_exp2(x.x), jt::fast_exp2(x.y));
-      r2[c & 1] = __fadd2_rn(r2[c & 1], e);
-      ph[c] = Mma::pack(e.x, e.y);
+      r2[k & 1] = __fadd2_rn(r2[k & 1], e);
+      ph[k] = Mma::pack(e.x, e.y);
       if constexpr (FP32P) {
-        const float2 r = Mma::unpack(ph[c]);
-        pl[c] = Mma::pack(e.x - r.x, e.y - r.y);
+        const float2 r = Mma::unpack(ph[k]);
+        pl[k] = Mma::pack(e.x - r.x, e.y - r.y);
       }
     }
-    tmem_st16(s_addr + 16 * h, ph);
-    if constexpr (FP32P) tmem_st16(s_addr + 64 + 16 * h, pl);
+    tmem_st16(p_addr + 16 * h, ph);
+    if constexpr (FP32P) tmem_st16(p_addr + 32 + 16 * h, pl);
   }
   return (r2[0].x + r2[1].x) + (r2[0].y + r2[1].y);
 }
 
+// Zero P for this warpgroup's 64 keys (rows of a warp with no live row).
 template <bool FP32P>
-__device__ __forceinline__ void write_zero_probabilities(uint32_t s_addr) {
+__device__ __forceinline__ void write_zero_half(uint32_t s_addr, int c) {
   uint32_t z[16];
 #pragma unroll
-  for (int c = 0; c < 16; ++c) z[c] = 0u;
+  for (int k = 0; k < 16; ++k) z[k] = 0u;
+  const uint32_t p_addr = s_addr + col_p(4 * c);
 #pragma unroll
-  for (int h = 0; h < 4; ++h) {
-    tmem_st16(s_addr + 16 * h, z);
-    if constexpr (FP32P) tmem_st16(s_addr + 64 + 16 * h, z);
+  for (int h = 0; h < 2; ++h) {
+    tmem_st16(p_addr + 16 * h, z);
+    if constexpr (FP32P) tmem_st16(p_addr + 32 + 16 * h, z);
   }
 }
 
@@ -501,8 +539,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int i = 0; i < kNumBars; ++i) {
       uint32_t count = 1;
       if (i == kBarPFull || i == kBarPFull + 1 || i == kBarOFree || i == kBarOFree + 1 ||
-          i == kBarXch || i == kBarXchFree)
-        count = 128;
+          i == kBarLx || i == kBarLx + 1 || i == kBarMx || i == kBarMx + 1)
+        count = 256;
       if (i == kBarItemEmpty || i == kBarItemEmpty + 1) count = kItemConsumers;
       if ((i >= kBarKFull && i < kBarKFull + kStages) || (i >= kBarVFull && i < kBarVFull + kStages))
         count = kLoaderWarps;
@@ -559,7 +597,6 @@ __global__ void __launch_bounds__(kThreads, 1)
       const bool pair = paired(it);
       const int slots = pair ? 2 : it.nq;
       int qk_left = pair ? n : it.nq * n;  // QKs still to issue for this item
-      int pv_left = qk_left;
       mbar_wait(JT_BAR(kBarQFull), q_count & 1, abort);
       ++q_count;
       tc_fence_after();
@@ -622,11 +659,10 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
           for (int kk = 0; kk < kN / 16; ++kk) {
             const uint64_t b = smem_desc(va + kk * 2048, kKVHalfBytes, 1024);
-            mma_ts(tmem + col_o(i), pa + kk * 8, b, kIdescPV, (s > 0 || kk > 0) ? 1u : 0u);
+            mma_ts(tmem + col_o(i), pa + col_p(kk), b, kIdescPV, (s > 0 || kk > 0) ? 1u : 0u);
             if constexpr (FP32P)
-              mma_ts(tmem + col_o(i), pa + 64 + kk * 8, b, kIdescPV, 1u);
+              mma_ts(tmem + col_o(i), pa + col_p(kk) + 32, b, kIdescPV, 1u);
           }
-          --pv_left;
           if (pair) {
             tc_commit(JT_BAR(kBarVEmpty + vstage));
             ++vc;
@@ -641,12 +677,9 @@ __global__ void __launch_bounds__(kThreads, 1)
               if (i == 0) kstage = wait_k();
               issue_qk(i, kstage);
             }
-          } else if (!pair) {
+          } else {
             tc_commit(JT_BAR(kBarOReady + i));
           }
-          // A paired item's two accumulators are merged by warpgroup 0 after both slots'
-          // last PVs: one commit after the item's final PV covers both.
-          if (pair && pv_left == 0) tc_commit(JT_BAR(kBarOReady));
         }
         if (!pair) {
           tc_commit(JT_BAR(kBarVEmpty + vstage));
@@ -752,195 +785,213 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else {
     // ------------------------------------------------------------------ softmax + epilogue
-    const int i = (warp - 4) >> 2;          // query-tile slot of this warpgroup
-    const int t128 = tid - 128 - i * 128;   // row within the query tile
+    // Both warpgroups work on every S tile: warpgroup c owns keys 64c..64c+63 of each tile
+    // and output columns 64c..64c+63; thread t128 owns score row t128 (its TMEM lane).
+    const int c = (warp - 4) >> 2;
+    const int t128 = tid - 128 - c * 128;
     const uint32_t lane_base = static_cast<uint32_t>((t128 >> 5) * 32) << 16;
-    const uint32_t s_addr = tmem + lane_base + col_s(i);
-    const uint32_t o_addr = tmem + lane_base + col_o(i);
-    const uint32_t o1_addr = tmem + lane_base + col_o(1);
-    float2* xch = reinterpret_cast<float2*>(sbase + kOffXch);
+    float* xl = reinterpret_cast<float*>(sbase + kOffXl);  // [tile][half][row] row sums
+    float* xm = reinterpret_cast<float*>(sbase + kOffXm);  // [tile][half][row] half maxima
     const float scale_log2 = p.scale * 1.4426950408889634f;
-    uint32_t sf_par = 0, or_par = 0, xch_count = 0;  // xch_count: paired items so far
+    // One parity bit per query-tile slot for each barrier this role waits on.
+    uint32_t sf_par = 0, or_par = 0, lx_par = 0, mx_par = 0;
     for (uint32_t seq = 0;; ++seq) {
       const int index = next_item(seq);
       if (index < 0) break;
       const Item it = decode(p, w, index, split_keys);
       const int n = it.n_tiles;
       const bool pair = paired(it);
-      if (!pair && i >= it.nq) continue;
-      // A paired item (one query tile, two or more key tiles) gives both warpgroups the
-      // same rows: warpgroup i takes key tiles i, i + 2, ... into its own S_i / O_i.
-      const int qi = pair ? 0 : i;
-      const int gm = it.tp * 2 * kM + qi * kM + t128;
-      const int j = gm / G, g = gm - j * G;
-      const bool row_ok = j < it.T;
-      const bool warp_live = __any_sync(0xffffffffu, row_ok);
-      const uint32_t* mask_row =
-          w.masks + static_cast<int64_t>(it.q_start + (row_ok ? j : 0)) * w.mask_words;
-      float m_run = -INFINITY;  // running max in log2 units (scaled scores)
-      float l_run = 0.f;
-      const int t_first = pair ? i : 0, t_step = pair ? 2 : 1;
-      for (int t = t_first; t < n; t += t_step) {
-        const int kb = it.key_begin + t * kN;
-        const bool full = kb + kN <= min(it.P, it.key_end);
-        // Keys of this tile; prefix-only tiles skip masking entirely.
-        const TileKeys vk{kb, it.P, it.key_end, it.T, mask_row, row_ok};
-        mbar_wait(JT_BAR(kBarSFull + i), sf_par, abort);
-        sf_par ^= 1u;
-        tc_fence_after();
-        float alpha = 1.f;
-        float rsum = 0.f;
-        if (warp_live) {
-          rsum = full ? softmax_row<Elem, FP32P, false>(s_addr, vk, scale_log2, m_run, alpha)
-                      : softmax_row<Elem, FP32P, true>(s_addr, vk, scale_log2, m_run, alpha);
-        } else {
-          write_zero_probabilities<FP32P>(s_addr);
+      const int slots = pair ? 2 : it.nq;
+      // Slot i holds query tile (pair ? 0 : i); a paired item's slots take alternate key
+      // tiles of the same rows and are merged at the end.
+      int j[2], g[2];
+      bool row_ok[2], warp_live[2];
+      const uint32_t* mask_row[2];
+#pragma unroll
+      for (int i = 0; i < 2; ++i) {
+        const int gm = it.tp * 2 * kM + (pair ? 0 : i) * kM + t128;
+        j[i] = gm / G;
+        g[i] = gm - j[i] * G;
+        row_ok[i] = j[i] < it.T;
+        warp_live[i] = __any_sync(0xffffffffu, row_ok[i]);
+        mask_row[i] = w.masks + static_cast<int64_t>(it.q_start + (row_ok[i] ? j[i] : 0)) * w.mask_words;
+      }
+      float m_run0 = -INFINITY, m_run1 = -INFINITY;  // running max, log2 units
+      float l_run0 = 0.f, l_run1 = 0.f;               // this half's partial row sums
+      const int steps = pair ? (n + 1) / 2 : n;
+      for (int s = 0; s < steps; ++s) {
+        for (int i = 0; i < slots; ++i) {
+          const int t = pair ? 2 * s + i : s;
+          if (t >= n) break;
+          const int kb = it.key_begin + t * kN;
+          const bool full = kb + kN <= min(it.P, it.key_end);
+          const bool ok = i ? row_ok[1] : row_ok[0];
+          const TileKeys vk{kb, it.P, it.key_end, it.T, i ? mask_row[1] : mask_row[0], ok};
+          const uint32_t s_addr = tmem + lane_base + col_s(i);
+          const uint32_t o_addr = tmem + lane_base + col_o(i);
+          mbar_wait(JT_BAR(kBarSFull + i), (sf_par >> i) & 1u, abort);
+          sf_par ^= 1u << i;
+          tc_fence_after();
+          float m = i ? m_run1 : m_run0;
+          float alpha = 1.f, rsum = 0.f;
+          float* xm_mine = xm + (i * 2 + c) * kM + t128;
+          const float* xm_other = xm + (i * 2 + (c ^ 1)) * kM + t128;
+          const uint32_t mx_parity = (mx_par >> i) & 1u;
+          mx_par ^= 1u << i;
+          if (i ? warp_live[1] : warp_live[0]) {
+            rsum = full ? softmax_half<Elem, FP32P, false>(s_addr, o_addr, c, vk, scale_log2, m,
+                                                           alpha, s > 0, xm_mine, xm_other,
+                                                           JT_BAR(kBarMx + i), mx_parity, abort)
+                        : softmax_half<Elem, FP32P, true>(s_addr, o_addr, c, vk, scale_log2, m,
+                                                          alpha, s > 0, xm_mine, xm_other,
+                                                          JT_BAR(kBarMx + i), mx_parity, abort);
+          } else {
+            // No live row in this warp: zero P, but still meet the other warpgroup.
+            mbar_arrive(JT_BAR(kBarMx + i));
+            mbar_wait(JT_BAR(kBarMx + i), mx_parity, abort);
+            write_zero_half<FP32P>(s_addr, c);
+          }
+          if (i) { m_run1 = m; l_run1 = l_run1 * alpha + rsum; }
+          else { m_run0 = m; l_run0 = l_run0 * alpha + rsum; }
+          tmem_wait_st();
+          tc_fence_before();
+          mbar_arrive(JT_BAR(kBarPFull + i));
         }
-        l_run = l_run * alpha + rsum;
-        // S_i ready implies the previous PV into O_i completed: rescale O_i in place.
-        if (t > t_first && __any_sync(0xffffffffu, alpha != 1.f)) {
+      }
+      // Epilogue: wait for each slot's last PV, swap the half row sums, then each
+      // warpgroup writes its 64 output columns (a paired item's two slots merged first).
+      float l_tot[2] = {0.f, 0.f};
+      for (int i = 0; i < slots; ++i) {
+        mbar_wait(JT_BAR(kBarOReady + i), (or_par >> i) & 1u, abort);
+        or_par ^= 1u << i;
+        const float mine = i ? l_run1 : l_run0;
+        xl[(i * 2 + c) * kM + t128] = mine;
+        mbar_arrive(JT_BAR(kBarLx + i));
+        mbar_wait(JT_BAR(kBarLx + i), (lx_par >> i) & 1u, abort);
+        lx_par ^= 1u << i;
+        l_tot[i] = mine + xl[(i * 2 + (c ^ 1)) * kM + t128];
+      }
+      tc_fence_after();
+      const int outs = pair ? 1 : slots;  // output tiles of this item
+      for (int i = 0; i < outs; ++i) {
+        float m_fin = i ? m_run1 : m_run0;
+        float l_fin = l_tot[i];
+        float a0 = 1.f, a1 = 0.f;
+        if (pair) {
+          const float mm = fmaxf(m_run0, m_run1);
+          const float mref = mm == -INFINITY ? 0.f : mm;
+          a0 = jt::fast_exp2(m_run0 - mref);
+          a1 = jt::fast_exp2(m_run1 - mref);
+          l_fin = a0 * l_tot[0] + a1 * l_tot[1];
+          m_fin = mm;
+        }
+        const int ji = i ? j[1] : j[0], gi = i ? g[1] : g[0];
+        const bool oki = i ? row_ok[1] : row_ok[0];
+        const bool split_item = it.n_split > 1;
+        const int64_t slot = it.slot_base +
+                             (static_cast<int64_t>(it.h) * it.mblocks + it.tp) * it.n_split + it.split;
+        const int item_row = (pair ? 0 : i) * kM + t128;
+        const float inv = 1.f / l_fin;
+        const uint32_t o_addr = tmem + lane_base + col_o(i) + 64 * c;
+        const uint32_t o1_addr = tmem + lane_base + col_o(1) + 64 * c;
 #pragma unroll 1
-          for (int chunk = 0; chunk < 4; ++chunk) {
-            uint32_t o[32];
-            tmem_ld32(o_addr + chunk * 32, o);
+        for (int chunk = 0; chunk < 2; ++chunk) {
+          uint32_t o[32];
+          tmem_ld32(o_addr + chunk * 32, o);
+          if (pair) {
+            uint32_t o1[32];
+            tmem_ld32(o1_addr + chunk * 32, o1);
             tmem_wait_ld();
 #pragma unroll
-            for (int c = 0; c < 32; ++c) o[c] = __float_as_uint(__uint_as_float(o[c]) * alpha);
-            tmem_st32(o_addr + chunk * 32, o);
+            for (int k = 0; k < 32; ++k)
+              o[k] = __float_as_uint(a0 * __uint_as_float(o[k]) + a1 * __uint_as_float(o1[k]));
+          } else {
+            tmem_wait_ld();
+          }
+          const int col = 64 * c + 32 * chunk;
+          if (split_item) {
+            float4* dst = reinterpret_cast<float4*>(w.part_o + (slot * (2 * kM) + item_row) * kD + col);
+#pragma unroll
+            for (int k = 0; k < 8; ++k)
+              dst[k] = make_float4(__uint_as_float(o[4 * k]), __uint_as_float(o[4 * k + 1]),
+                                   __uint_as_float(o[4 * k + 2]), __uint_as_float(o[4 * k + 3]));
+          } else if (oki) {
+            const int64_t off = static_cast<int64_t>(it.q_start + ji) * p.out_stride0 +
+                                static_cast<int64_t>(it.h * G + gi) * p.out_stride1 + col;
+            if (p.out_dtype == JT_F32) {
+              float4* dst = reinterpret_cast<float4*>(static_cast<float*>(p.out) + off);
+#pragma unroll
+              for (int k = 0; k < 8; ++k)
+                dst[k] = make_float4(__uint_as_float(o[4 * k]) * inv, __uint_as_float(o[4 * k + 1]) * inv,
+                                     __uint_as_float(o[4 * k + 2]) * inv,
+                                     __uint_as_float(o[4 * k + 3]) * inv);
+            } else {
+              uint4* dst = reinterpret_cast<uint4*>(static_cast<Elem*>(p.out) + off);
+#pragma unroll
+              for (int k = 0; k < 4; ++k)
+                dst[k] = make_uint4(
+                    Mma::pack(__uint_as_float(o[8 * k]) * inv, __uint_as_float(o[8 * k + 1]) * inv),
+                    Mma::pack(__uint_as_float(o[8 * k + 2]) * inv, __uint_as_float(o[8 * k + 3]) * inv),
+                    Mma::pack(__uint_as_float(o[8 * k + 4]) * inv, __uint_as_float(o[8 * k + 5]) * inv),
+                    Mma::pack(__uint_as_float(o[8 * k + 6]) * inv, __uint_as_float(o[8 * k + 7]) * inv));
+            }
           }
         }
-        tmem_wait_st();
-        tc_fence_before();
-        mbar_arrive(JT_BAR(kBarPFull + i));
-      }
-      if (pair && i == 1) {
-        // Hand this half's running max and sum to warpgroup 0, which merges O_1 into its
-        // own result, once warpgroup 0 has read the previous paired item's values.
-        if (xch_count > 0) mbar_wait(JT_BAR(kBarXchFree), (xch_count - 1) & 1u, abort);
-        xch[t128] = make_float2(m_run, l_run);
-        mbar_arrive(JT_BAR(kBarXch));
-        ++xch_count;
-        continue;
-      }
-      // Epilogue: wait for the item's last PV into O_i (both accumulators when paired).
-      mbar_wait(JT_BAR(kBarOReady + i), or_par, abort);
-      or_par ^= 1u;
-      tc_fence_after();
-      float a0 = 1.f, a1 = 0.f;
-      if (pair) {
-        mbar_wait(JT_BAR(kBarXch), xch_count & 1u, abort);
-        const float2 ml1 = xch[t128];
-        mbar_arrive(JT_BAR(kBarXchFree));
-        ++xch_count;
-        const float m = fmaxf(m_run, ml1.x);
-        const float mref = m == -INFINITY ? 0.f : m;
-        a0 = jt::fast_exp2(m_run - mref);
-        a1 = jt::fast_exp2(ml1.x - mref);
-        l_run = a0 * l_run + a1 * ml1.y;
-        m_run = m;
-      }
-      const bool split_item = it.n_split > 1;
-      const int64_t slot = it.slot_base +
-                           (static_cast<int64_t>(it.h) * it.mblocks + it.tp) * it.n_split + it.split;
-      const int item_row = qi * kM + t128;
-      const float inv = 1.f / l_run;
-#pragma unroll 1
-      for (int chunk = 0; chunk < 4; ++chunk) {
-        uint32_t o[32];
-        tmem_ld32(o_addr + chunk * 32, o);
-        if (pair) {
-          uint32_t o1[32];
-          tmem_ld32(o1_addr + chunk * 32, o1);
-          tmem_wait_ld();
-#pragma unroll
-          for (int c = 0; c < 32; ++c)
-            o[c] = __float_as_uint(a0 * __uint_as_float(o[c]) + a1 * __uint_as_float(o1[c]));
-        } else {
-          tmem_wait_ld();
-        }
         if (split_item) {
-          float4* dst = reinterpret_cast<float4*>(w.part_o + (slot * (2 * kM) + item_row) * kD +
-                                                  chunk * 32);
-#pragma unroll
-          for (int c = 0; c < 8; ++c)
-            dst[c] = make_float4(__uint_as_float(o[4 * c]), __uint_as_float(o[4 * c + 1]),
-                                 __uint_as_float(o[4 * c + 2]), __uint_as_float(o[4 * c + 3]));
-        } else if (row_ok) {
-          const int64_t off = static_cast<int64_t>(it.q_start + j) * p.out_stride0 +
-                              static_cast<int64_t>(it.h * G + g) * p.out_stride1 + chunk * 32;
-          if (p.out_dtype == JT_F32) {
-            float4* dst = reinterpret_cast<float4*>(static_cast<float*>(p.out) + off);
-#pragma unroll
-            for (int c = 0; c < 8; ++c)
-              dst[c] = make_float4(__uint_as_float(o[4 * c]) * inv, __uint_as_float(o[4 * c + 1]) * inv,
-                                   __uint_as_float(o[4 * c + 2]) * inv,
-                                   __uint_as_float(o[4 * c + 3]) * inv);
-          } else {
-            uint4* dst = reinterpret_cast<uint4*>(static_cast<Elem*>(p.out) + off);
-#pragma unroll
-            for (int c = 0; c < 4; ++c)
-              dst[c] = make_uint4(
-                  Mma::pack(__uint_as_float(o[8 * c]) * inv, __uint_as_float(o[8 * c + 1]) * inv),
-                  Mma::pack(__uint_as_float(o[8 * c + 2]) * inv, __uint_as_float(o[8 * c + 3]) * inv),
-                  Mma::pack(__uint_as_float(o[8 * c + 4]) * inv, __uint_as_float(o[8 * c + 5]) * inv),
-                  Mma::pack(__uint_as_float(o[8 * c + 6]) * inv, __uint_as_float(o[8 * c + 7]) * inv));
+          // Per-row merge: each half publishes its columns (warpgroup 0 also the row's max
+          // in log2 units and sum), then bumps the row's counter; the arrival that
+          // completes a row (both halves of every split) merges the whole row.  Rows never
+          // wait for one another.
+          if (c == 0) w.part_ml[slot * (2 * kM) + item_row] = make_float2(m_fin, l_fin);
+          __threadfence();
+          int* counter = w.counters +
+                         (static_cast<int64_t>(it.counter_base) + it.h * it.mblocks + it.tp) * (2 * kM) +
+                         item_row;
+          const int done = atomicAdd(counter, 1);
+          if (done == 2 * it.n_split - 1) {
+            *counter = 0;
+            __threadfence();
+            if (oki) {
+              const int64_t slot0 =
+                  it.slot_base + (static_cast<int64_t>(it.h) * it.mblocks + it.tp) * it.n_split;
+              float mmax = -INFINITY;
+              for (int s2 = 0; s2 < it.n_split; ++s2)
+                mmax = fmaxf(mmax, __ldcg(w.part_ml + (slot0 + s2) * (2 * kM) + item_row).x);
+              const float mref = mmax == -INFINITY ? 0.f : mmax;
+              float den = 0.f;
+              for (int s2 = 0; s2 < it.n_split; ++s2) {
+                const float2 ml = __ldcg(w.part_ml + (slot0 + s2) * (2 * kM) + item_row);
+                den += jt::fast_exp2(ml.x - mref) * ml.y;
+              }
+              const float dinv = 1.f / den;
+              const int64_t off = static_cast<int64_t>(it.q_start + ji) * p.out_stride0 +
+                                  static_cast<int64_t>(it.h * G + gi) * p.out_stride1;
+              for (int d = 0; d < kD; d += 4) {
+                float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+                for (int s2 = 0; s2 < it.n_split; ++s2) {
+                  const float wv =
+                      jt::fast_exp2(__ldcg(w.part_ml + (slot0 + s2) * (2 * kM) + item_row).x - mref);
+                  const float4 o = __ldcg(reinterpret_cast<const float4*>(
+                      w.part_o + ((slot0 + s2) * (2 * kM) + item_row) * kD + d));
+                  acc.x += wv * o.x;
+                  acc.y += wv * o.y;
+                  acc.z += wv * o.z;
+                  acc.w += wv * o.w;
+                }
+                if (p.out_dtype == JT_F32) {
+                  *reinterpret_cast<float4*>(static_cast<float*>(p.out) + off + d) =
+                      make_float4(acc.x * dinv, acc.y * dinv, acc.z * dinv, acc.w * dinv);
+                } else {
+                  *reinterpret_cast<uint2*>(static_cast<Elem*>(p.out) + off + d) = make_uint2(
+                      Mma::pack(acc.x * dinv, acc.y * dinv), Mma::pack(acc.z * dinv, acc.w * dinv));
+                }
+              }
+            }
           }
         }
       }
       tc_fence_before();
-      mbar_arrive(JT_BAR(kBarOFree + i));
-      if (pair) mbar_arrive(JT_BAR(kBarOFree + 1));
-      if (split_item) {
-        // Per-row merge: each row publishes its partial (max in log2 units, sum), then bumps
-        // its own counter; the split that completes a row merges that row.  Rows never
-        // wait for one another.
-        w.part_ml[slot * (2 * kM) + item_row] = make_float2(m_run, l_run);
-        __threadfence();
-        int* counter = w.counters +
-                       (static_cast<int64_t>(it.counter_base) + it.h * it.mblocks + it.tp) * (2 * kM) +
-                       item_row;
-        const int done = atomicAdd(counter, 1);
-        if (done == it.n_split - 1) {
-          *counter = 0;
-          __threadfence();
-          if (row_ok) {
-            const int64_t slot0 =
-                it.slot_base + (static_cast<int64_t>(it.h) * it.mblocks + it.tp) * it.n_split;
-            float mmax = -INFINITY;
-            for (int s2 = 0; s2 < it.n_split; ++s2)
-              mmax = fmaxf(mmax, __ldcg(w.part_ml + (slot0 + s2) * (2 * kM) + item_row).x);
-            const float mref = mmax == -INFINITY ? 0.f : mmax;
-            float den = 0.f;
-            for (int s2 = 0; s2 < it.n_split; ++s2) {
-              const float2 ml = __ldcg(w.part_ml + (slot0 + s2) * (2 * kM) + item_row);
-              den += jt::fast_exp2(ml.x - mref) * ml.y;
-            }
-            const float dinv = 1.f / den;
-            const int64_t off = static_cast<int64_t>(it.q_start + j) * p.out_stride0 +
-                                static_cast<int64_t>(it.h * G + g) * p.out_stride1;
-            for (int d = 0; d < kD; d += 4) {
-              float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-              for (int s2 = 0; s2 < it.n_split; ++s2) {
-                const float wv =
-                    jt::fast_exp2(__ldcg(w.part_ml + (slot0 + s2) * (2 * kM) + item_row).x - mref);
-                const float4 o = __ldcg(reinterpret_cast<const float4*>(
-                    w.part_o + ((slot0 + s2) * (2 * kM) + item_row) * kD + d));
-                acc.x += wv * o.x;
-                acc.y += wv * o.y;
-                acc.z += wv * o.z;
-                acc.w += wv * o.w;
-              }
-              if (p.out_dtype == JT_F32) {
-                *reinterpret_cast<float4*>(static_cast<float*>(p.out) + off + d) =
-                    make_float4(acc.x * dinv, acc.y * dinv, acc.z * dinv, acc.w * dinv);
-              } else {
-                *reinterpret_cast<uint2*>(static_cast<Elem*>(p.out) + off + d) = make_uint2(
-                    Mma::pack(acc.x * dinv, acc.y * dinv), Mma::pack(acc.z * dinv, acc.w * dinv));
-              }
-            }
-          }
-        }
-      }
+      for (int i = 0; i < slots; ++i) mbar_arrive(JT_BAR(kBarOFree + i));
     }
   }
 #undef JT_BAR
