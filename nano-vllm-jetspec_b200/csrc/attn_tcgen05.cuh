@@ -2,25 +2,30 @@
 //
 // Included by tree_attn.cu inside its anonymous namespace (uses DevLayout, the plan's
 // work items and g_attn_errors).  One persistent CTA per SM pulls work items from the
-// device plan's queue (longest first).  An item is up to two 128-row query tiles (256
-// score rows = 256/groups tree nodes x groups query heads) of one (request, KV head, key
-// split), streamed against 128-key K/V tiles.  Warp roles:
+// device plan's queue (longest first).  An item is one 128-row query tile (128/groups
+// tree nodes x groups query heads) of one (request, KV head, key split), streamed against
+// 128-key K/V tiles.  The query tiles of one request and KV head are adjacent in the
+// queue, so CTAs on neighbouring SMs stream the same K/V tiles at about the same time and
+// all but the first read them from L2.  Warp roles:
 //
 //   warp 0       MMA issuer (one thread) and TMEM owner (512 columns)
-//   warps 1-3    loaders: TMA for prefix tiles (128 keys inside one page, 128-byte
-//                swizzle), cp.async for query tiles and for tiles that touch the tree
+//   warps 1-3    loaders: TMA for the query tile and for prefix K/V tiles (128 keys inside
+//                one page, 128-byte swizzle), cp.async for tiles that touch the tree
 //                nodes (scattered scratch slots), written in the same swizzled layout
-//   warps 4-7    softmax + epilogue of query tile 0 (one thread per score row)
-//   warps 8-11   softmax + epilogue of query tile 1
+//   warps 4-11   softmax + epilogue: warpgroup c (warps 4+4c..7+4c) owns keys 64c..64c+63
+//                of every key tile and output columns 64c..64c+63; thread t owns score
+//                row t (its TMEM lane)
 //
-// Per key tile t and query tile i: S_i = Q_i K_t^T (tcgen05.mma M128 N128 K16, both
-// operands in shared memory, fp32 accumulator in TMEM); the softmax warps read S_i from
-// TMEM, apply the tree mask, update the fp32 online softmax and write P (rounded to the
-// operand type) back over S_i; O_i += P V_t (tcgen05.mma with A from TMEM and V MN-major
-// in shared memory).  The tensor core alternates between the two query tiles, so one
-// tile's softmax overlaps the other tile's MMAs.  The running max only moves (and O is
-// rescaled in TMEM) when it grows by more than 2^8, so P stays <= 256 and rescales are
-// rare.  K and V stages have separate barriers: K is released once both QKs read it.
+// TMEM holds O (128 columns) and three S buffers (128 columns each).  Per key tile t:
+// S = Q K_t^T (tcgen05.mma M128 N128 K16, both operands in shared memory) into buffer
+// t % 3; the softmax reads its half of S, swaps half-row maxima with the other warpgroup,
+// and writes P (rounded to the operand type) over the S columns it read; O += P V_t
+// (tcgen05.mma with A from TMEM, V MN-major in shared memory).  With three S buffers the
+// QKs run up to three tiles ahead of the softmax, which therefore never waits for the
+// tensor core; it only waits for the previous PV before it rescales O, and the running
+// max moves (O rescaled in TMEM) only when it grows by more than 2^8, so P stays <= 256
+// and rescales are rare.  K and V tiles share one five-slot ring filled in the MMA's
+// consumption order.
 //
 // Every mbarrier wait is bounded and every waiter consumes every phase of the barriers it
 // waits on, in order (parity waits are unambiguous only within one phase).  A wait that
@@ -32,28 +37,27 @@ namespace tc {
 constexpr int kN = 128;       // keys per KV tile
 constexpr int kD = 128;       // head dim
 constexpr int kM = 128;       // rows per query tile (MMA M)
-constexpr int kStages = 2;    // K and V ring depth
+constexpr int kRing = 5;      // K/V ring slots (32 KB each), filled in consumption order
+constexpr int kSBufs = 3;     // S buffers in TMEM
+constexpr int kAhead = 3;     // QKs issued ahead of the PVs (= kSBufs)
 constexpr int kThreads = 384;
 constexpr int kQTileBytes = kM * kD * 2;   // 32 KB: two 64-dim halves of [128 rows][128 B]
 constexpr int kQHalfBytes = kM * 128;
 constexpr int kKVBytes = kN * kD * 2;      // 32 KB: two 64-dim halves of [128 keys][128 B]
 constexpr int kKVHalfBytes = kN * 128;
 constexpr int kOffQ = 0;
-constexpr int kOffK = kOffQ + 2 * kQTileBytes;
-constexpr int kOffV = kOffK + kStages * kKVBytes;
-constexpr int kOffBar = kOffV + kStages * kKVBytes;
+constexpr int kOffRing = kOffQ + kQTileBytes;
+constexpr int kOffBar = kOffRing + kRing * kKVBytes;
 constexpr int kOffMisc = kOffBar + 8 * 32;
-constexpr int kOffXl = kOffMisc + 64;                   // [2 tiles][2 halves][128] row sums
-constexpr int kOffXm = kOffXl + 2 * 2 * kM * 4;         // [2 tiles][2 halves][128] half maxima
-constexpr int kSmemBytes = kOffXm + 2 * 2 * kM * 4 + 1024;  // + alignment slack
+constexpr int kOffXl = kOffMisc + 64;                   // [2 halves][128] row sums
+constexpr int kOffXm = kOffXl + 2 * kM * 4;             // [tile parity][2 halves][128] maxima
+constexpr int kSmemBytes = kOffXm + 4 * kM * 4 + 1024;  // + alignment slack
 constexpr long long kWaitLimit = 4000000000ll;          // cycles (~2 s) per wait
 
-// TMEM column map (512 columns x 128 lanes x 32 bit): O_i and S_i, 128 columns each.
-// P (operand-type pairs, 64 columns) and, for fp32 probabilities, its low part (64 more)
-// are written over S_i.
-__host__ __device__ constexpr uint32_t col_o(int i) { return 128u * i; }
-__host__ __device__ constexpr uint32_t col_s(int i) { return 256u + 128u * i; }
-// P of keys 16kk..16kk+15 (operand-type pairs, 8 columns) inside S_i: each softmax
+// TMEM column map (512 columns x 128 lanes x 32 bit): O, then the S buffers.
+__host__ __device__ constexpr uint32_t col_o() { return 0u; }
+__host__ __device__ constexpr uint32_t col_s(int b) { return 128u + 128u * b; }
+// P of keys 16kk..16kk+15 (operand-type pairs, 8 columns) inside an S buffer: each softmax
 // warpgroup writes the probabilities of its 64 keys inside the S columns it owns (keys
 // 0..63 -> columns 0..31, keys 64..127 -> columns 64..95); fp32-probability low parts
 // follow 32 columns later.
@@ -62,21 +66,20 @@ __host__ __device__ constexpr uint32_t col_p(int kk) {
 }
 
 // Barrier indices.
-constexpr int kBarKFull = 0;                   // [kStages]  loader warps (+ TMA bytes)
-constexpr int kBarKEmpty = 2;                  // [kStages]  MMA commit after the QKs
-constexpr int kBarVFull = 4;                   // [kStages]
-constexpr int kBarVEmpty = 6;                  // [kStages]  MMA commit after the PVs
-constexpr int kBarQFull = 8;                   // loader thread 0 (+ TMA bytes)
-constexpr int kBarQEmpty = 9;                  // MMA commit after an item's last QK
-constexpr int kBarSFull = 10;                  // [2 tiles]  MMA commit per QK
-constexpr int kBarPFull = 12;                  // [2 tiles]  256 softmax threads
-constexpr int kBarLx = 14;                     // [2 tiles]  256 softmax threads: row sums swapped
-constexpr int kBarMx = 25;                     // [2 tiles]  256 softmax threads: half maxima swapped
-constexpr int kBarOReady = 16;                 // [2 tiles]  MMA commit after an item's last PV
-constexpr int kBarOFree = 18;                  // [2 tiles]  256 threads after the epilogue
-constexpr int kBarDrain = 20;
-constexpr int kBarItemFull = 21;               // [2] work-item ring
-constexpr int kBarItemEmpty = 23;              // [2]
+constexpr int kBarFull = 0;                    // [kRing]  loader warps (+ TMA bytes)
+constexpr int kBarEmpty = 5;                   // [kRing]  MMA commit after the slot's MMAs
+constexpr int kBarQFull = 10;                  // loader thread 0 (+ TMA bytes)
+constexpr int kBarQEmpty = 11;                 // MMA commit after an item's last QK
+constexpr int kBarSFull = 12;                  // [kSBufs] MMA commit per QK
+constexpr int kBarPFull = 15;                  // [kSBufs] 8 softmax warps
+constexpr int kBarPvDone = 18;                 // MMA commit per PV
+constexpr int kBarOFree = 19;                  // 8 softmax warps after the epilogue
+constexpr int kBarMx = 20;                     // 8 softmax warps: half maxima swapped
+constexpr int kBarLx = 21;                     // 8 softmax warps: half row sums swapped
+constexpr int kSoftmaxWarps = 8;
+constexpr int kBarDrain = 22;
+constexpr int kBarItemFull = 23;               // [2] work-item ring
+constexpr int kBarItemEmpty = 25;              // [2]
 constexpr int kNumBars = 27;
 constexpr int kItemConsumers = 12;             // every warp of the CTA reads each item
 constexpr int kLoaderWarps = 3;
@@ -117,6 +120,18 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatil
       return false;
     }
   }
+}
+
+// Warp-wide arrival: the lanes synchronise (bar.warp.sync orders their earlier memory and
+// tcgen05-fenced operations before lane 0's arrival), then lane 0 arrives for the warp.
+__device__ __forceinline__ void warp_arrive(uint32_t bar) {
+  __syncwarp();
+  if ((threadIdx.x & 31) == 0) mbar_arrive(bar);
+}
+// Warp-wide wait: lane 0 waits for the phase, the other lanes synchronise behind it.
+__device__ __forceinline__ void warp_wait(uint32_t bar, uint32_t parity, volatile int* abort) {
+  if ((threadIdx.x & 31) == 0) mbar_wait(bar, parity, abort);
+  __syncwarp();
 }
 
 __device__ __forceinline__ void fence_proxy_async() {
@@ -265,7 +280,7 @@ __device__ __forceinline__ uint32_t visible_bits(int p0, int P, int key_end, int
 
 struct Item {
   int r, split, h, tp, n_split, mblocks, slot_base, counter_base;
-  int P, T, q_start, key_begin, key_end, n_tiles, nq;
+  int P, T, q_start, key_begin, key_end, n_tiles;
 };
 
 __device__ __forceinline__ Item decode(const JtTreeAttnParams& p, const DevLayout& w, int index,
@@ -284,23 +299,16 @@ __device__ __forceinline__ Item decode(const JtTreeAttnParams& p, const DevLayou
   it.P = p.prefix_lens[it.r];
   it.T = p.node_counts[it.r];
   it.q_start = p.cu_seqlens_q[it.r];
-  const int G = p.groups;
-  const int rows = it.T * G - it.tp * 2 * kM;
-  it.nq = rows > kM ? 2 : 1;
   it.key_begin = it.split * split_keys;
   if (it.split + 1 < it.n_split) {
     it.key_end = it.key_begin + split_keys;
   } else {
-    const int last_row = it.tp * 2 * kM + it.nq * kM - 1;
-    it.key_end = it.P + min(it.T, last_row / G + 1);
+    const int last_row = it.tp * kM + kM - 1;
+    it.key_end = it.P + min(it.T, last_row / p.groups + 1);
   }
   it.n_tiles = (it.key_end - it.key_begin + kN - 1) / kN;
   return it;
 }
-
-// A paired item has one query tile and at least two key tiles: both softmax warpgroups
-// work on its rows, each over every other key tile, and their results are merged.
-__device__ __forceinline__ bool paired(const Item& it) { return it.nq == 1 && it.n_tiles >= 2; }
 
 // Loads one 128-key K or V tile into its ring stage: TMA when the keys are one page's
 // prefix run, else one cp.async row per loader thread (rows past key_end zero-filled).
@@ -351,7 +359,6 @@ __device__ __forceinline__ void load_kv_tile(const JtTreeAttnParams& p, const It
   __syncwarp();
   if (lane == 0) mbar_arrive(full_bar);
 }
-
 // Softmax helpers for one score row (the calling thread's TMEM lane) of one 128-key tile.
 // `vk` describes the tile for masked tiles: keys kb..kb+127, prefix P, range end, nodes T
 // and the row's ancestor bitmask (row_ok false masks the whole row).
@@ -400,21 +407,18 @@ __host__ __device__ constexpr bool poly_pair(int c) {
   return kPolyPairs > 0 && (c % (16 / (kPolyPairs > 0 ? kPolyPairs : 1))) ==
                                (16 / (kPolyPairs > 0 ? kPolyPairs : 1)) - 1;
 }
-
 // Softmax of one score row for one key half.  The two softmax warpgroups share every
 // 128-key tile: warpgroup `c` owns keys 64c..64c+63, i.e. S columns 64c..64c+63, and only
 // ever reads or writes those.  Each thread loads its 64 scores (two 32-column TMEM loads,
 // one wait), publishes its half's max in `xm` and meets the other warpgroup on `mx_bar`
-// (a 256-thread rendezvous), so both derive the same running max.  The running max is
-// lazy: it moves only when the tile max exceeds it by more than 8 (log2 units); then this
-// half's O columns are rescaled in TMEM when `may_rescale` (O holds earlier tiles).  P =
+// (a rendezvous of the eight softmax warps), so both derive the same running max.  The running max is
+// lazy: it moves only when the tile max exceeds it by more than 8 (log2 units).  P =
 // exp2(s * scale_log2 - m), rounded to the operand type, goes to this half's columns
-// (col_p).  Returns the fp32 sum of this half's P; `alpha` is the factor the older partial
-// sum must take.
+// (col_p).  Returns the fp32 sum of this half's P; `alpha` is the factor the older O and
+// partial sum must take.
 template <typename Elem, bool FP32P, bool kMasked>
-__device__ __forceinline__ float softmax_half(uint32_t s_addr, uint32_t o_addr, int c,
-                                              const TileKeys& vk, float scale_log2,
-                                              float& m_run, float& alpha, bool may_rescale,
+__device__ __forceinline__ float softmax_half(uint32_t s_addr, int c, const TileKeys& vk,
+                                              float scale_log2, float& m_run, float& alpha,
                                               float* xm_mine, const float* xm_other,
                                               uint32_t mx_bar, uint32_t mx_parity,
                                               volatile int* abort) {
@@ -446,8 +450,8 @@ __device__ __forceinline__ float softmax_half(uint32_t s_addr, uint32_t o_addr, 
   const float half_max = max3f(max3f(m8[0], m8[1], m8[2]), max3f(m8[3], m8[4], m8[5]),
                                fmaxf(m8[6], m8[7]));
   *xm_mine = half_max;
-  mbar_arrive(mx_bar);
-  mbar_wait(mx_bar, mx_parity, abort);
+  warp_arrive(mx_bar);
+  warp_wait(mx_bar, mx_parity, abort);
   // Raw max; scale > 0 keeps the order.
   const float mx = fmaxf(half_max, *xm_other) * scale_log2;
   alpha = 1.f;
@@ -456,18 +460,6 @@ __device__ __forceinline__ float softmax_half(uint32_t s_addr, uint32_t o_addr, 
     m_run = mx;
   }
   const float neg_m = m_run == -INFINITY ? 0.f : -m_run;
-  // The previous PV into O completed before this S was produced: rescale in place.
-  if (may_rescale && __any_sync(0xffffffffu, alpha != 1.f)) {
-#pragma unroll 1
-    for (int chunk = 0; chunk < 2; ++chunk) {
-      uint32_t o[32];
-      tmem_ld32(o_addr + own + chunk * 32, o);
-      tmem_wait_ld();
-#pragma unroll
-      for (int k = 0; k < 32; ++k) o[k] = __float_as_uint(__uint_as_float(o[k]) * alpha);
-      tmem_st32(o_addr + own + chunk * 32, o);
-    }
-  }
   const float2 scale2 = make_float2(scale_log2, scale_log2);
   const float2 neg2 = make_float2(neg_m, neg_m);
   float2 r2[2] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
@@ -512,7 +504,6 @@ __device__ __forceinline__ void write_zero_half(uint32_t s_addr, int c) {
     if constexpr (FP32P) tmem_st16(p_addr + 32 + 16 * h, z);
   }
 }
-
 template <typename Elem, bool FP32P>
 __global__ void __launch_bounds__(kThreads, 1)
     tree_attn_tc_kernel(const JtTreeAttnParams p, const DevLayout w,
@@ -538,12 +529,11 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (tid == 0) {
     for (int i = 0; i < kNumBars; ++i) {
       uint32_t count = 1;
-      if (i == kBarPFull || i == kBarPFull + 1 || i == kBarOFree || i == kBarOFree + 1 ||
-          i == kBarLx || i == kBarLx + 1 || i == kBarMx || i == kBarMx + 1)
-        count = 256;
+      if ((i >= kBarPFull && i < kBarPFull + kSBufs) || i == kBarOFree || i == kBarMx ||
+          i == kBarLx)
+        count = kSoftmaxWarps;
       if (i == kBarItemEmpty || i == kBarItemEmpty + 1) count = kItemConsumers;
-      if ((i >= kBarKFull && i < kBarKFull + kStages) || (i >= kBarVFull && i < kBarVFull + kStages))
-        count = kLoaderWarps;
+      if (i >= kBarFull && i < kBarFull + kRing) count = kLoaderWarps;
       mbar_init(JT_BAR(i), count);
     }
     misc[1] = 0;
@@ -581,116 +571,75 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   if (warp == 0) {
     // ------------------------------------------------------------------ MMA issuer
-    // Issue order per key step and query-tile slot i: PV_i then the slot's next QK_i.
-    // tcgen05.mma instructions of one thread execute in issue order, so PV_i has read P
-    // out of S_i before the next QK_i overwrites S_i, and the commit that signals the new
-    // S_i also covers PV_i: the softmax may then rescale O_i.  While the softmax of one
-    // slot runs, the tensor core works on the other slot.
-    uint32_t kc = 0, vc = 0, q_count = 0;
-    uint32_t pf_par = 0, of_par = 0, of_seen = 0;
+    // Per item: QK 0..2 into S buffers g%3 (g counts tiles over all items), then per tile
+    // t: PV t (once the softmax published P t) and QK t+3.  tcgen05.mma instructions of
+    // one thread execute in issue order, so PV t has read P t out of its S buffer before
+    // QK t+3 overwrites that buffer.
+    uint32_t ring = 0, q_count = 0, g0 = 0;
+    bool o_used = false;
+    uint32_t of_par = 0;
     for (uint32_t seq = 0;; ++seq) {
       const int index = next_item(seq);
       if (index < 0) break;
       if (lane != 0) continue;
       const Item it = decode(p, w, index, split_keys);
       const int n = it.n_tiles;
-      const bool pair = paired(it);
-      const int slots = pair ? 2 : it.nq;
-      int qk_left = pair ? n : it.nq * n;  // QKs still to issue for this item
       mbar_wait(JT_BAR(kBarQFull), q_count & 1, abort);
       ++q_count;
       tc_fence_after();
-      auto wait_k = [&]() -> int {
-        const int stage = kc % kStages;
-        mbar_wait(JT_BAR(kBarKFull + stage), (kc / kStages) & 1, abort);
+      auto take = [&]() -> int {
+        const int slot = ring % kRing;
+        mbar_wait(JT_BAR(kBarFull + slot), (ring / kRing) & 1, abort);
         tc_fence_after();
-        return stage;
+        return slot;
       };
-      auto issue_qk = [&](int i, int stage) {
-        const uint32_t qa = base + kOffQ + (pair ? 0 : i) * kQTileBytes;
-        const uint32_t ka = base + kOffK + stage * kKVBytes;
+      auto release = [&](int slot) {
+        tc_commit(JT_BAR(kBarEmpty + slot));
+        ++ring;
+      };
+      auto issue_qk = [&](int t) {
+        const int slot = take();
+        const int b = (g0 + t) % kSBufs;
+        const uint32_t qa = base + kOffQ;
+        const uint32_t ka = base + kOffRing + slot * kKVBytes;
 #pragma unroll
         for (int kk = 0; kk < kD / 16; ++kk) {
           const uint32_t off = (kk & 3) * 32;
-          mma_ss(tmem + col_s(i), smem_desc(qa + (kk >> 2) * kQHalfBytes + off, 16, 1024),
+          mma_ss(tmem + col_s(b), smem_desc(qa + (kk >> 2) * kQHalfBytes + off, 16, 1024),
                  smem_desc(ka + (kk >> 2) * kKVHalfBytes + off, 16, 1024), kIdescQK,
                  kk > 0 ? 1u : 0u);
         }
-        tc_commit(JT_BAR(kBarSFull + i));
-        if (--qk_left == 0) tc_commit(JT_BAR(kBarQEmpty));
+        tc_commit(JT_BAR(kBarSFull + b));
+        release(slot);
+        if (t == n - 1) tc_commit(JT_BAR(kBarQEmpty));
       };
-      // First S of every slot.  A paired item gives each slot its own K tile (tiles 0
-      // and 1); otherwise both query tiles share tile 0.
-      if (pair) {
-        for (int i = 0; i < 2; ++i) {
-          const int stage = wait_k();
-          issue_qk(i, stage);
-          tc_commit(JT_BAR(kBarKEmpty + stage));
-          ++kc;
+      for (int t = 0; t < min(kAhead, n); ++t) issue_qk(t);
+      for (int t = 0; t < n; ++t) {
+        const int g = g0 + t;
+        const int b = g % kSBufs;
+        const int slot = take();
+        if (t == 0 && o_used) {
+          // O still holds the previous item until its epilogue has read it.
+          mbar_wait(JT_BAR(kBarOFree), of_par, abort);
+          of_par ^= 1u;
         }
-      } else {
-        const int stage = wait_k();
-        for (int i = 0; i < it.nq; ++i) issue_qk(i, stage);
-        tc_commit(JT_BAR(kBarKEmpty + stage));
-        ++kc;
-      }
-      const int steps = pair ? (n + 1) / 2 : n;
-      for (int s = 0; s < steps; ++s) {
-        int vstage = 0, kstage = 0;
-        auto wait_v = [&]() {
-          vstage = vc % kStages;
-          mbar_wait(JT_BAR(kBarVFull + vstage), (vc / kStages) & 1, abort);
-        };
-        if (!pair) wait_v();
-        for (int i = 0; i < slots; ++i) {
-          const int t = pair ? 2 * s + i : s;
-          if (t >= n) break;  // paired item with an odd tile count
-          if (pair) wait_v();
-          if (s == 0 && ((of_seen >> i) & 1u)) {
-            mbar_wait(JT_BAR(kBarOFree + i), (of_par >> i) & 1u, abort);
-            of_par ^= 1u << i;
-          }
-          mbar_wait(JT_BAR(kBarPFull + i), (pf_par >> i) & 1u, abort);
-          pf_par ^= 1u << i;
-          tc_fence_after();
-          // O_i += P V (P over S_i in TMEM, V MN-major in shared memory).
-          const uint32_t pa = tmem + col_s(i);
-          const uint32_t va = base + kOffV + vstage * kKVBytes;
+        mbar_wait(JT_BAR(kBarPFull + b), (g / kSBufs) & 1, abort);
+        tc_fence_after();
+        // O += P V (P inside S buffer b in TMEM, V MN-major in shared memory).
+        const uint32_t pa = tmem + col_s(b);
+        const uint32_t va = base + kOffRing + slot * kKVBytes;
 #pragma unroll
-          for (int kk = 0; kk < kN / 16; ++kk) {
-            const uint64_t b = smem_desc(va + kk * 2048, kKVHalfBytes, 1024);
-            mma_ts(tmem + col_o(i), pa + col_p(kk), b, kIdescPV, (s > 0 || kk > 0) ? 1u : 0u);
-            if constexpr (FP32P)
-              mma_ts(tmem + col_o(i), pa + col_p(kk) + 32, b, kIdescPV, 1u);
-          }
-          if (pair) {
-            tc_commit(JT_BAR(kBarVEmpty + vstage));
-            ++vc;
-          }
-          if (t + (pair ? 2 : 1) < n) {
-            if (pair) {
-              const int stage = wait_k();
-              issue_qk(i, stage);
-              tc_commit(JT_BAR(kBarKEmpty + stage));
-              ++kc;
-            } else {
-              if (i == 0) kstage = wait_k();
-              issue_qk(i, kstage);
-            }
-          } else {
-            tc_commit(JT_BAR(kBarOReady + i));
-          }
+        for (int kk = 0; kk < kN / 16; ++kk) {
+          const uint64_t bd = smem_desc(va + kk * 2048, kKVHalfBytes, 1024);
+          mma_ts(tmem + col_o(), pa + col_p(kk), bd, kIdescPV, (t > 0 || kk > 0) ? 1u : 0u);
+          if constexpr (FP32P) mma_ts(tmem + col_o(), pa + col_p(kk) + 32, bd, kIdescPV, 1u);
         }
-        if (!pair) {
-          tc_commit(JT_BAR(kBarVEmpty + vstage));
-          ++vc;
-          if (s + 1 < n) {
-            tc_commit(JT_BAR(kBarKEmpty + kstage));
-            ++kc;
-          }
-        }
+        tc_commit(JT_BAR(kBarPvDone));
+        release(slot);
+        if (t + kAhead < n) issue_qk(t + kAhead);
       }
-      for (int i = 0; i < slots; ++i) of_seen |= 1u << i;
+      g0 += n;
+      o_used = true;
     }
     if (lane == 0) {
       // Drain: every MMA this thread issued has completed before TMEM is released.
@@ -700,9 +649,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   } else if (warp < 4) {
     // ------------------------------------------------------------------ loaders
     const int ltid = tid - 32;
-    uint32_t kc = 0, vc = 0, q_fills = 0;
-    uint32_t filled = 0;       // bit (2*stage + v): last fill of that ring slot was TMA
-    uint32_t last_parity = 0;  // same bits: phase parity of that fill
+    uint32_t ring = 0, q_fills = 0;
+    uint32_t filled = 0;       // bit s: the last fill of ring slot s was TMA
+    uint32_t last_parity = 0;  // bit s: phase parity of that fill
     const int64_t pool_slots = p.num_blocks * static_cast<int64_t>(bs);
     for (uint32_t seq = 0;; ++seq) {
       if (ltid == 0) {
@@ -716,282 +665,231 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int index = next_item(seq);
       if (index < 0) break;
       const Item it = decode(p, w, index, split_keys);
+      const int n = it.n_tiles;
       const int32_t* table = p.block_tables + static_cast<int64_t>(it.r) * p.table_stride0;
-      // Query tiles: one TMA box of 128/groups nodes x groups heads x 64 dims per half,
-      // once the previous item's last QK has read the buffer.  Rows past the request's
-      // nodes hold other requests' queries (or zeros past the end); their score rows are
-      // never written out.
+      // Query tile: one TMA box of 128/groups nodes x groups heads x 64 dims per half, once
+      // the previous item's last QK has read the buffer.  Rows past the request's nodes
+      // hold other requests' queries (or zeros past the end); their score rows are never
+      // written out.
       if (ltid == 0) {
         if (seq > 0) mbar_wait(JT_BAR(kBarQEmpty), (seq - 1) & 1, abort);
-        mbar_arrive_tx(JT_BAR(kBarQFull), it.nq * kQTileBytes);
-        const int node0 = it.q_start + it.tp * (2 * kM / G);
-        for (int i = 0; i < it.nq; ++i) {
-          const uint32_t dst = base + kOffQ + i * kQTileBytes;
-          const int node = node0 + i * (kM / G);
-          tma_load_3d(dst, &qmap, 0, it.h * G, node, JT_BAR(kBarQFull));
-          tma_load_3d(dst + kQHalfBytes, &qmap, 64, it.h * G, node, JT_BAR(kBarQFull));
-        }
+        mbar_arrive_tx(JT_BAR(kBarQFull), kQTileBytes);
+        const int node = it.q_start + it.tp * (kM / G);
+        tma_load_3d(base + kOffQ, &qmap, 0, it.h * G, node, JT_BAR(kBarQFull));
+        tma_load_3d(base + kOffQ + kQHalfBytes, &qmap, 64, it.h * G, node, JT_BAR(kBarQFull));
         ++q_fills;
       }
-      auto load_k = [&](int t) {
+      // Fill order = the MMA's consumption order (K 0..2, then V t and K t+3 per tile).
+      auto fill = [&](bool is_v, int t) {
         const int kb = it.key_begin + t * kN;
         const bool full = kb + kN <= min(it.P, it.key_end);
         const int page = (full && ltid == 0) ? __ldg(table + kb / bs) : 0;
+        const int slot = ring % kRing;
+        const uint32_t parity = (ring / kRing) & 1;
         // Every loader thread waits for every refill, in order.
-        const int stage = kc % kStages;
-        const uint32_t parity = (kc / kStages) & 1;
-        if (kc >= kStages) mbar_wait(JT_BAR(kBarKEmpty + stage), parity ^ 1, abort);
-        load_kv_tile(p, it, table, kb, full, ltid, lane, base + kOffK + stage * kKVBytes, &kmap,
-                     static_cast<const char*>(p.k_pool), p.k_stride0, p.k_stride1, p.k_stride2,
-                     JT_BAR(kBarKFull + stage), pool_slots, page);
-        const uint32_t bit = 1u << (2 * stage);
+        if (ring >= kRing) mbar_wait(JT_BAR(kBarEmpty + slot), parity ^ 1, abort);
+        if (is_v)
+          load_kv_tile(p, it, table, kb, full, ltid, lane, base + kOffRing + slot * kKVBytes,
+                       &vmap, static_cast<const char*>(p.v_pool), p.v_stride0, p.v_stride1,
+                       p.v_stride2, JT_BAR(kBarFull + slot), pool_slots, page);
+        else
+          load_kv_tile(p, it, table, kb, full, ltid, lane, base + kOffRing + slot * kKVBytes,
+                       &kmap, static_cast<const char*>(p.k_pool), p.k_stride0, p.k_stride1,
+                       p.k_stride2, JT_BAR(kBarFull + slot), pool_slots, page);
+        const uint32_t bit = 1u << slot;
         if (full) { filled |= bit; last_parity = (last_parity & ~bit) | (parity ? bit : 0u); }
         else filled &= ~bit;
-        ++kc;
+        ++ring;
       };
-      auto load_v = [&](int t) {
-        const int kb = it.key_begin + t * kN;
-        const bool full = kb + kN <= min(it.P, it.key_end);
-        const int page = (full && ltid == 0) ? __ldg(table + kb / bs) : 0;
-        const int stage = vc % kStages;
-        const uint32_t parity = (vc / kStages) & 1;
-        if (vc >= kStages) mbar_wait(JT_BAR(kBarVEmpty + stage), parity ^ 1, abort);
-        load_kv_tile(p, it, table, kb, full, ltid, lane, base + kOffV + stage * kKVBytes, &vmap,
-                     static_cast<const char*>(p.v_pool), p.v_stride0, p.v_stride1, p.v_stride2,
-                     JT_BAR(kBarVFull + stage), pool_slots, page);
-        const uint32_t bit = 2u << (2 * stage);
-        if (full) { filled |= bit; last_parity = (last_parity & ~bit) | (parity ? bit : 0u); }
-        else filled &= ~bit;
-        ++vc;
-      };
-      // Fill order = the MMA's consumption order: K t, V t per tile; for a paired item
-      // K t, K t+1, V t, V t+1 per tile pair (the slots' next K tiles arrive early).
-      const int unit = paired(it) ? 2 : 1;
-      for (int t0 = 0; t0 < it.n_tiles; t0 += unit) {
-        const int t1 = min(t0 + unit, it.n_tiles);
-        for (int t = t0; t < t1; ++t) load_k(t);
-        for (int t = t0; t < t1; ++t) load_v(t);
+      for (int t = 0; t < min(kAhead, n); ++t) fill(false, t);
+      for (int t = 0; t < n; ++t) {
+        fill(true, t);
+        if (t + kAhead < n) fill(false, t + kAhead);
       }
     }
     // Drain: the TMA copies this thread issued have landed before the CTA exits.
     if (ltid == 0) {
-      for (int s = 0; s < kStages; ++s) {
-        if (filled & (1u << (2 * s)))
-          mbar_wait(JT_BAR(kBarKFull + s), (last_parity >> (2 * s)) & 1u, abort, false);
-        if (filled & (2u << (2 * s)))
-          mbar_wait(JT_BAR(kBarVFull + s), (last_parity >> (2 * s + 1)) & 1u, abort, false);
-      }
+      for (int s = 0; s < kRing; ++s)
+        if (filled & (1u << s))
+          mbar_wait(JT_BAR(kBarFull + s), (last_parity >> s) & 1u, abort, false);
       if (q_fills > 0) mbar_wait(JT_BAR(kBarQFull), (q_fills - 1) & 1u, abort, false);
     }
   } else {
     // ------------------------------------------------------------------ softmax + epilogue
-    // Both warpgroups work on every S tile: warpgroup c owns keys 64c..64c+63 of each tile
-    // and output columns 64c..64c+63; thread t128 owns score row t128 (its TMEM lane).
-    const int c = (warp - 4) >> 2;
-    const int t128 = tid - 128 - c * 128;
+    const int c = (warp - 4) >> 2;           // key / output column half of this warpgroup
+    const int t128 = tid - 128 - c * 128;    // score row (TMEM lane)
     const uint32_t lane_base = static_cast<uint32_t>((t128 >> 5) * 32) << 16;
-    float* xl = reinterpret_cast<float*>(sbase + kOffXl);  // [tile][half][row] row sums
-    float* xm = reinterpret_cast<float*>(sbase + kOffXm);  // [tile][half][row] half maxima
+    float* xl = reinterpret_cast<float*>(sbase + kOffXl);  // [half][row] row sums
+    // [tile parity][half][row] half maxima: alternating buffers, so a warpgroup that runs a
+    // tile ahead never overwrites a value the other warpgroup has yet to read.
+    float* xm = reinterpret_cast<float*>(sbase + kOffXm);
     const float scale_log2 = p.scale * 1.4426950408889634f;
-    // One parity bit per query-tile slot for each barrier this role waits on.
-    uint32_t sf_par = 0, or_par = 0, lx_par = 0, mx_par = 0;
+    uint32_t g0 = 0, pv_seen = 0, mx_par = 0, lx_par = 0;
     for (uint32_t seq = 0;; ++seq) {
       const int index = next_item(seq);
       if (index < 0) break;
       const Item it = decode(p, w, index, split_keys);
       const int n = it.n_tiles;
-      const bool pair = paired(it);
-      const int slots = pair ? 2 : it.nq;
-      // Slot i holds query tile (pair ? 0 : i); a paired item's slots take alternate key
-      // tiles of the same rows and are merged at the end.
-      int j[2], g[2];
-      bool row_ok[2], warp_live[2];
-      const uint32_t* mask_row[2];
-#pragma unroll
-      for (int i = 0; i < 2; ++i) {
-        const int gm = it.tp * 2 * kM + (pair ? 0 : i) * kM + t128;
-        j[i] = gm / G;
-        g[i] = gm - j[i] * G;
-        row_ok[i] = j[i] < it.T;
-        warp_live[i] = __any_sync(0xffffffffu, row_ok[i]);
-        mask_row[i] = w.masks + static_cast<int64_t>(it.q_start + (row_ok[i] ? j[i] : 0)) * w.mask_words;
-      }
-      float m_run0 = -INFINITY, m_run1 = -INFINITY;  // running max, log2 units
-      float l_run0 = 0.f, l_run1 = 0.f;               // this half's partial row sums
-      const int steps = pair ? (n + 1) / 2 : n;
-      for (int s = 0; s < steps; ++s) {
-        for (int i = 0; i < slots; ++i) {
-          const int t = pair ? 2 * s + i : s;
-          if (t >= n) break;
-          const int kb = it.key_begin + t * kN;
-          const bool full = kb + kN <= min(it.P, it.key_end);
-          const bool ok = i ? row_ok[1] : row_ok[0];
-          const TileKeys vk{kb, it.P, it.key_end, it.T, i ? mask_row[1] : mask_row[0], ok};
-          const uint32_t s_addr = tmem + lane_base + col_s(i);
-          const uint32_t o_addr = tmem + lane_base + col_o(i);
-          mbar_wait(JT_BAR(kBarSFull + i), (sf_par >> i) & 1u, abort);
-          sf_par ^= 1u << i;
+      const int gm = it.tp * kM + t128;
+      const int j = gm / G, g = gm - j * G;
+      const bool row_ok = j < it.T;
+      const bool warp_live = __any_sync(0xffffffffu, row_ok);
+      const uint32_t* mask_row =
+          w.masks + static_cast<int64_t>(it.q_start + (row_ok ? j : 0)) * w.mask_words;
+      float m_run = -INFINITY;  // running max in log2 units (scaled scores)
+      float l_run = 0.f;        // this half's partial row sum
+      const uint32_t o_addr = tmem + lane_base + col_o();
+      for (int t = 0; t < n; ++t) {
+        const int gt = g0 + t;
+        const int b = gt % kSBufs;
+        const int kb = it.key_begin + t * kN;
+        const bool full = kb + kN <= min(it.P, it.key_end);
+        const TileKeys vk{kb, it.P, it.key_end, it.T, mask_row, row_ok};
+        const uint32_t s_addr = tmem + lane_base + col_s(b);
+        warp_wait(JT_BAR(kBarSFull + b), (gt / kSBufs) & 1, abort);
+        tc_fence_after();
+        float alpha = 1.f, rsum = 0.f;
+        float* xm_mine = xm + ((gt & 1) * 2 + c) * kM + t128;
+        const float* xm_other = xm + ((gt & 1) * 2 + (c ^ 1)) * kM + t128;
+        if (warp_live) {
+          rsum = full ? softmax_half<Elem, FP32P, false>(s_addr, c, vk, scale_log2, m_run,
+                                                         alpha, xm_mine, xm_other,
+                                                         JT_BAR(kBarMx), mx_par, abort)
+                      : softmax_half<Elem, FP32P, true>(s_addr, c, vk, scale_log2, m_run,
+                                                        alpha, xm_mine, xm_other,
+                                                        JT_BAR(kBarMx), mx_par, abort);
+        } else {
+          // No live row in this warp: zero P, but still meet the other warpgroup.
+          warp_arrive(JT_BAR(kBarMx));
+          warp_wait(JT_BAR(kBarMx), mx_par, abort);
+          write_zero_half<FP32P>(s_addr, c);
+        }
+        mx_par ^= 1u;
+        l_run = l_run * alpha + rsum;
+        if (t > 0) {
+          // PV t-1 has completed: O is stable and may be rescaled in place.
+          warp_wait(JT_BAR(kBarPvDone), pv_seen & 1u, abort);
+          ++pv_seen;
           tc_fence_after();
-          float m = i ? m_run1 : m_run0;
-          float alpha = 1.f, rsum = 0.f;
-          float* xm_mine = xm + (i * 2 + c) * kM + t128;
-          const float* xm_other = xm + (i * 2 + (c ^ 1)) * kM + t128;
-          const uint32_t mx_parity = (mx_par >> i) & 1u;
-          mx_par ^= 1u << i;
-          if (i ? warp_live[1] : warp_live[0]) {
-            rsum = full ? softmax_half<Elem, FP32P, false>(s_addr, o_addr, c, vk, scale_log2, m,
-                                                           alpha, s > 0, xm_mine, xm_other,
-                                                           JT_BAR(kBarMx + i), mx_parity, abort)
-                        : softmax_half<Elem, FP32P, true>(s_addr, o_addr, c, vk, scale_log2, m,
-                                                          alpha, s > 0, xm_mine, xm_other,
-                                                          JT_BAR(kBarMx + i), mx_parity, abort);
-          } else {
-            // No live row in this warp: zero P, but still meet the other warpgroup.
-            mbar_arrive(JT_BAR(kBarMx + i));
-            mbar_wait(JT_BAR(kBarMx + i), mx_parity, abort);
-            write_zero_half<FP32P>(s_addr, c);
-          }
-          if (i) { m_run1 = m; l_run1 = l_run1 * alpha + rsum; }
-          else { m_run0 = m; l_run0 = l_run0 * alpha + rsum; }
-          tmem_wait_st();
-          tc_fence_before();
-          mbar_arrive(JT_BAR(kBarPFull + i));
-        }
-      }
-      // Epilogue: wait for each slot's last PV, swap the half row sums, then each
-      // warpgroup writes its 64 output columns (a paired item's two slots merged first).
-      float l_tot[2] = {0.f, 0.f};
-      for (int i = 0; i < slots; ++i) {
-        mbar_wait(JT_BAR(kBarOReady + i), (or_par >> i) & 1u, abort);
-        or_par ^= 1u << i;
-        const float mine = i ? l_run1 : l_run0;
-        xl[(i * 2 + c) * kM + t128] = mine;
-        mbar_arrive(JT_BAR(kBarLx + i));
-        mbar_wait(JT_BAR(kBarLx + i), (lx_par >> i) & 1u, abort);
-        lx_par ^= 1u << i;
-        l_tot[i] = mine + xl[(i * 2 + (c ^ 1)) * kM + t128];
-      }
-      tc_fence_after();
-      const int outs = pair ? 1 : slots;  // output tiles of this item
-      for (int i = 0; i < outs; ++i) {
-        float m_fin = i ? m_run1 : m_run0;
-        float l_fin = l_tot[i];
-        float a0 = 1.f, a1 = 0.f;
-        if (pair) {
-          const float mm = fmaxf(m_run0, m_run1);
-          const float mref = mm == -INFINITY ? 0.f : mm;
-          a0 = jt::fast_exp2(m_run0 - mref);
-          a1 = jt::fast_exp2(m_run1 - mref);
-          l_fin = a0 * l_tot[0] + a1 * l_tot[1];
-          m_fin = mm;
-        }
-        const int ji = i ? j[1] : j[0], gi = i ? g[1] : g[0];
-        const bool oki = i ? row_ok[1] : row_ok[0];
-        const bool split_item = it.n_split > 1;
-        const int64_t slot = it.slot_base +
-                             (static_cast<int64_t>(it.h) * it.mblocks + it.tp) * it.n_split + it.split;
-        const int item_row = (pair ? 0 : i) * kM + t128;
-        const float inv = 1.f / l_fin;
-        const uint32_t o_addr = tmem + lane_base + col_o(i) + 64 * c;
-        const uint32_t o1_addr = tmem + lane_base + col_o(1) + 64 * c;
+          if (__any_sync(0xffffffffu, alpha != 1.f)) {
 #pragma unroll 1
-        for (int chunk = 0; chunk < 2; ++chunk) {
-          uint32_t o[32];
-          tmem_ld32(o_addr + chunk * 32, o);
-          if (pair) {
-            uint32_t o1[32];
-            tmem_ld32(o1_addr + chunk * 32, o1);
-            tmem_wait_ld();
+            for (int chunk = 0; chunk < 2; ++chunk) {
+              uint32_t o[32];
+              tmem_ld32(o_addr + 64 * c + chunk * 32, o);
+              tmem_wait_ld();
 #pragma unroll
-            for (int k = 0; k < 32; ++k)
-              o[k] = __float_as_uint(a0 * __uint_as_float(o[k]) + a1 * __uint_as_float(o1[k]));
-          } else {
-            tmem_wait_ld();
+              for (int k = 0; k < 32; ++k) o[k] = __float_as_uint(__uint_as_float(o[k]) * alpha);
+              tmem_st32(o_addr + 64 * c + chunk * 32, o);
+            }
           }
-          const int col = 64 * c + 32 * chunk;
-          if (split_item) {
-            float4* dst = reinterpret_cast<float4*>(w.part_o + (slot * (2 * kM) + item_row) * kD + col);
+        }
+        tmem_wait_st();
+        tc_fence_before();
+        warp_arrive(JT_BAR(kBarPFull + b));
+      }
+      // Epilogue: wait for the item's last PV, swap the half row sums, then each
+      // warpgroup writes its 64 output columns.
+      warp_wait(JT_BAR(kBarPvDone), pv_seen & 1u, abort);
+      ++pv_seen;
+      xl[c * kM + t128] = l_run;
+      warp_arrive(JT_BAR(kBarLx));
+      warp_wait(JT_BAR(kBarLx), lx_par, abort);
+      lx_par ^= 1u;
+      const float l_fin = l_run + xl[(c ^ 1) * kM + t128];
+      tc_fence_after();
+      const bool split_item = it.n_split > 1;
+      const int64_t slot = it.slot_base +
+                           (static_cast<int64_t>(it.h) * it.mblocks + it.tp) * it.n_split + it.split;
+      const float inv = 1.f / l_fin;
+#pragma unroll 1
+      for (int chunk = 0; chunk < 2; ++chunk) {
+        uint32_t o[32];
+        tmem_ld32(o_addr + 64 * c + chunk * 32, o);
+        tmem_wait_ld();
+        const int col = 64 * c + 32 * chunk;
+        if (split_item) {
+          float4* dst = reinterpret_cast<float4*>(w.part_o + (slot * kM + t128) * kD + col);
+#pragma unroll
+          for (int k = 0; k < 8; ++k)
+            dst[k] = make_float4(__uint_as_float(o[4 * k]), __uint_as_float(o[4 * k + 1]),
+                                 __uint_as_float(o[4 * k + 2]), __uint_as_float(o[4 * k + 3]));
+        } else if (row_ok) {
+          const int64_t off = static_cast<int64_t>(it.q_start + j) * p.out_stride0 +
+                              static_cast<int64_t>(it.h * G + g) * p.out_stride1 + col;
+          if (p.out_dtype == JT_F32) {
+            float4* dst = reinterpret_cast<float4*>(static_cast<float*>(p.out) + off);
 #pragma unroll
             for (int k = 0; k < 8; ++k)
-              dst[k] = make_float4(__uint_as_float(o[4 * k]), __uint_as_float(o[4 * k + 1]),
-                                   __uint_as_float(o[4 * k + 2]), __uint_as_float(o[4 * k + 3]));
-          } else if (oki) {
-            const int64_t off = static_cast<int64_t>(it.q_start + ji) * p.out_stride0 +
-                                static_cast<int64_t>(it.h * G + gi) * p.out_stride1 + col;
-            if (p.out_dtype == JT_F32) {
-              float4* dst = reinterpret_cast<float4*>(static_cast<float*>(p.out) + off);
+              dst[k] = make_float4(__uint_as_float(o[4 * k]) * inv, __uint_as_float(o[4 * k + 1]) * inv,
+                                   __uint_as_float(o[4 * k + 2]) * inv,
+                                   __uint_as_float(o[4 * k + 3]) * inv);
+          } else {
+            uint4* dst = reinterpret_cast<uint4*>(static_cast<Elem*>(p.out) + off);
 #pragma unroll
-              for (int k = 0; k < 8; ++k)
-                dst[k] = make_float4(__uint_as_float(o[4 * k]) * inv, __uint_as_float(o[4 * k + 1]) * inv,
-                                     __uint_as_float(o[4 * k + 2]) * inv,
-                                     __uint_as_float(o[4 * k + 3]) * inv);
-            } else {
-              uint4* dst = reinterpret_cast<uint4*>(static_cast<Elem*>(p.out) + off);
-#pragma unroll
-              for (int k = 0; k < 4; ++k)
-                dst[k] = make_uint4(
-                    Mma::pack(__uint_as_float(o[8 * k]) * inv, __uint_as_float(o[8 * k + 1]) * inv),
-                    Mma::pack(__uint_as_float(o[8 * k + 2]) * inv, __uint_as_float(o[8 * k + 3]) * inv),
-                    Mma::pack(__uint_as_float(o[8 * k + 4]) * inv, __uint_as_float(o[8 * k + 5]) * inv),
-                    Mma::pack(__uint_as_float(o[8 * k + 6]) * inv, __uint_as_float(o[8 * k + 7]) * inv));
-            }
-          }
-        }
-        if (split_item) {
-          // Per-row merge: each half publishes its columns (warpgroup 0 also the row's max
-          // in log2 units and sum), then bumps the row's counter; the arrival that
-          // completes a row (both halves of every split) merges the whole row.  Rows never
-          // wait for one another.
-          if (c == 0) w.part_ml[slot * (2 * kM) + item_row] = make_float2(m_fin, l_fin);
-          __threadfence();
-          int* counter = w.counters +
-                         (static_cast<int64_t>(it.counter_base) + it.h * it.mblocks + it.tp) * (2 * kM) +
-                         item_row;
-          const int done = atomicAdd(counter, 1);
-          if (done == 2 * it.n_split - 1) {
-            *counter = 0;
-            __threadfence();
-            if (oki) {
-              const int64_t slot0 =
-                  it.slot_base + (static_cast<int64_t>(it.h) * it.mblocks + it.tp) * it.n_split;
-              float mmax = -INFINITY;
-              for (int s2 = 0; s2 < it.n_split; ++s2)
-                mmax = fmaxf(mmax, __ldcg(w.part_ml + (slot0 + s2) * (2 * kM) + item_row).x);
-              const float mref = mmax == -INFINITY ? 0.f : mmax;
-              float den = 0.f;
-              for (int s2 = 0; s2 < it.n_split; ++s2) {
-                const float2 ml = __ldcg(w.part_ml + (slot0 + s2) * (2 * kM) + item_row);
-                den += jt::fast_exp2(ml.x - mref) * ml.y;
-              }
-              const float dinv = 1.f / den;
-              const int64_t off = static_cast<int64_t>(it.q_start + ji) * p.out_stride0 +
-                                  static_cast<int64_t>(it.h * G + gi) * p.out_stride1;
-              for (int d = 0; d < kD; d += 4) {
-                float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-                for (int s2 = 0; s2 < it.n_split; ++s2) {
-                  const float wv =
-                      jt::fast_exp2(__ldcg(w.part_ml + (slot0 + s2) * (2 * kM) + item_row).x - mref);
-                  const float4 o = __ldcg(reinterpret_cast<const float4*>(
-                      w.part_o + ((slot0 + s2) * (2 * kM) + item_row) * kD + d));
-                  acc.x += wv * o.x;
-                  acc.y += wv * o.y;
-                  acc.z += wv * o.z;
-                  acc.w += wv * o.w;
-                }
-                if (p.out_dtype == JT_F32) {
-                  *reinterpret_cast<float4*>(static_cast<float*>(p.out) + off + d) =
-                      make_float4(acc.x * dinv, acc.y * dinv, acc.z * dinv, acc.w * dinv);
-                } else {
-                  *reinterpret_cast<uint2*>(static_cast<Elem*>(p.out) + off + d) = make_uint2(
-                      Mma::pack(acc.x * dinv, acc.y * dinv), Mma::pack(acc.z * dinv, acc.w * dinv));
-                }
-              }
-            }
+            for (int k = 0; k < 4; ++k)
+              dst[k] = make_uint4(
+                  Mma::pack(__uint_as_float(o[8 * k]) * inv, __uint_as_float(o[8 * k + 1]) * inv),
+                  Mma::pack(__uint_as_float(o[8 * k + 2]) * inv, __uint_as_float(o[8 * k + 3]) * inv),
+                  Mma::pack(__uint_as_float(o[8 * k + 4]) * inv, __uint_as_float(o[8 * k + 5]) * inv),
+                  Mma::pack(__uint_as_float(o[8 * k + 6]) * inv, __uint_as_float(o[8 * k + 7]) * inv));
           }
         }
       }
       tc_fence_before();
-      for (int i = 0; i < slots; ++i) mbar_arrive(JT_BAR(kBarOFree + i));
+      warp_arrive(JT_BAR(kBarOFree));
+      if (split_item) {
+        // Per-row merge: each half publishes its columns (warpgroup 0 also the row's max
+        // in log2 units and sum), then bumps the row's counter; the arrival that
+        // completes a row (both halves of every split) merges the whole row.  Rows never
+        // wait for one another.
+        if (c == 0) w.part_ml[slot * kM + t128] = make_float2(m_run, l_fin);
+        __threadfence();
+        int* counter = w.counters +
+                       (static_cast<int64_t>(it.counter_base) + it.h * it.mblocks + it.tp) * kM +
+                       t128;
+        const int done = atomicAdd(counter, 1);
+        if (done == 2 * it.n_split - 1) {
+          *counter = 0;
+          __threadfence();
+          if (row_ok) {
+            const int64_t slot0 =
+                it.slot_base + (static_cast<int64_t>(it.h) * it.mblocks + it.tp) * it.n_split;
+            float mmax = -INFINITY;
+            for (int s2 = 0; s2 < it.n_split; ++s2)
+              mmax = fmaxf(mmax, __ldcg(w.part_ml + (slot0 + s2) * kM + t128).x);
+            const float mref = mmax == -INFINITY ? 0.f : mmax;
+            float den = 0.f;
+            for (int s2 = 0; s2 < it.n_split; ++s2) {
+              const float2 ml = __ldcg(w.part_ml + (slot0 + s2) * kM + t128);
+              den += jt::fast_exp2(ml.x - mref) * ml.y;
+            }
+            const float dinv = 1.f / den;
+            const int64_t off = static_cast<int64_t>(it.q_start + j) * p.out_stride0 +
+                                static_cast<int64_t>(it.h * G + g) * p.out_stride1;
+            for (int d = 0; d < kD; d += 4) {
+              float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+              for (int s2 = 0; s2 < it.n_split; ++s2) {
+                const float wv =
+                    jt::fast_exp2(__ldcg(w.part_ml + (slot0 + s2) * kM + t128).x - mref);
+                const float4 o = __ldcg(reinterpret_cast<const float4*>(
+                    w.part_o + ((slot0 + s2) * kM + t128) * kD + d));
+                acc.x += wv * o.x;
+                acc.y += wv * o.y;
+                acc.z += wv * o.z;
+                acc.w += wv * o.w;
+              }
+              if (p.out_dtype == JT_F32) {
+                *reinterpret_cast<float4*>(static_cast<float*>(p.out) + off + d) =
+                    make_float4(acc.x * dinv, acc.y * dinv, acc.z * dinv, acc.w * dinv);
+              } else {
+                *reinterpret_cast<uint2*>(static_cast<Elem*>(p.out) + off + d) = make_uint2(
+                    Mma::pack(acc.x * dinv, acc.y * dinv), Mma::pack(acc.z * dinv, acc.w * dinv));
+              }
+            }
+          }
+        }
+      }
+      g0 += n;
     }
   }
 #undef JT_BAR

@@ -43,6 +43,7 @@ constexpr int64_t kPartialBudgetBytes = 256ll << 20;
 // ---- workspace layout ---------------------------------------------------------------
 struct Layout {
   int bm;           // score rows per item (64 or 128)
+  int counter_stride;  // split counters per (request, kv head, m-block): 1, or one per row
   int mask_words;   // 32-bit words of ancestor bitmask per tree node
   int max_items;
   int max_slots;    // partial-result slots (split items)
@@ -59,7 +60,8 @@ int choose_bm(int32_t num_requests, int32_t total_queries, int32_t groups) {
 }
 
 Layout make_layout(int32_t R, int32_t Q, int32_t H, int32_t G, int32_t D,
-                   int64_t partial_budget = kPartialBudgetBytes, int bm = 0) {
+                   int64_t partial_budget = kPartialBudgetBytes, int bm = 0,
+                   bool row_counters = false) {
   Layout L{};
   L.bm = bm > 0 ? bm : choose_bm(R, Q, G);
   L.mask_words = static_cast<int>(std::min<int64_t>((std::max<int32_t>(Q, 1) + 31) / 32,
@@ -76,7 +78,8 @@ Layout make_layout(int32_t R, int32_t Q, int32_t H, int32_t G, int32_t D,
   L.off_items = o;    o = align_up(o + sizeof(int4) * static_cast<size_t>(L.max_items), 256);
   // Split counters: one per (request, kv head, m-block) for the portable core, one per
   // score row for the tcgen05 core (whose rows finish independently).
-  const size_t counter_stride = L.bm > 128 ? static_cast<size_t>(L.bm) : 1;
+  const size_t counter_stride = row_counters ? static_cast<size_t>(L.bm) : 1;
+  L.counter_stride = static_cast<int>(counter_stride);
   L.off_counters = o;
   o = align_up(o + sizeof(int) * static_cast<size_t>(L.max_slots) * counter_stride, 256);
   L.off_masks = o;
@@ -114,7 +117,7 @@ DevLayout device_layout(const Layout& L, void* ws) {
   d.mask_words = L.mask_words;
   d.max_items = L.max_items;
   d.max_slots = L.max_slots;
-  d.counter_stride = L.bm > 128 ? L.bm : 1;
+  d.counter_stride = L.counter_stride;
   return d;
 }
 
@@ -718,7 +721,7 @@ int dispatch_bm(const JtTreeAttnParams& p, const Layout& L, const DevLayout& d,
 bool al16(const void* ptr) { return (reinterpret_cast<uintptr_t>(ptr) & 15u) == 0; }
 
 // ---- tcgen05 path -------------------------------------------------------------------
-constexpr int kTcItemRows = 2 * tc::kM;  // score rows per tcgen05 work item
+constexpr int kTcItemRows = tc::kM;  // score rows per tcgen05 work item (one query tile)
 
 PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
   static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
@@ -856,7 +859,7 @@ extern "C" int jt_tree_attn_workspace_size(int32_t num_requests, int32_t total_q
   size_t total = make_layout(num_requests, total_queries, num_kv_heads, groups, head_dim).total;
   if (head_dim == tc::kD)
     total = std::max(total, make_layout(num_requests, total_queries, num_kv_heads, groups,
-                                        head_dim, kPartialBudgetBytes, kTcItemRows)
+                                        head_dim, kPartialBudgetBytes, kTcItemRows, true)
                                 .total);
   *bytes = total;
   return JT_OK;
@@ -899,7 +902,7 @@ int validate_params(const JtTreeAttnParams& p) {
 int run_tree_attn(const JtTreeAttnParams& p, int64_t partial_budget, cudaStream_t stream) {
   const bool tc_core = tcgen05_eligible(p);
   const Layout L = make_layout(p.num_requests, p.total_queries, p.num_kv_heads, p.groups,
-                               p.head_dim, partial_budget, tc_core ? kTcItemRows : 0);
+                               p.head_dim, partial_budget, tc_core ? kTcItemRows : 0, tc_core);
   if (p.workspace == nullptr || p.workspace_bytes < L.total || !al16(p.workspace))
     return jt_fail(JT_ERR_WORKSPACE, "tree_attn: workspace of %zu bytes required (got %zu)",
                    L.total, p.workspace_bytes);
@@ -962,9 +965,10 @@ extern "C" int jt_tree_attn_launch_noalloc(const JtTreeAttnParams* pp, cudaStrea
   if (pp == nullptr) return jt_fail(JT_ERR_INVALID, "tree_attn_noalloc: null params");
   int rc = validate_params(*pp);
   if (rc != JT_OK) return rc;
+  const bool tc_core = tcgen05_eligible(*pp);
   const Layout L = make_layout(pp->num_requests, pp->total_queries, pp->num_kv_heads,
                                pp->groups, pp->head_dim, kStaticPartialBudget,
-                               tcgen05_eligible(*pp) ? kTcItemRows : 0);
+                               tc_core ? kTcItemRows : 0, tc_core);
   if (L.total > kStaticWorkspaceBytes)
     return jt_fail(JT_ERR_WORKSPACE,
                    "tree_attn_noalloc: this geometry needs %zu bytes of scratch, above the "
