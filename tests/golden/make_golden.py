@@ -1,0 +1,214 @@
+"""Generate the golden fixtures under tests/golden/ from the reference implementation.
+
+Run from the repository root in a container where the reference checkout is present:
+
+    python tests/golden/make_golden.py --reference <path to the reference checkout>
+
+Everything here executes the reference's own code on the CPU:
+
+  * packed_metadata.py PackedTreeMetadata.build  -> metadata_ragged3.npz
+  * paged_backend.py _packed_paged_tree_fp32 (the reference's fp32 tree-attention
+    kernel, run by the Triton interpreter, TRITON_INTERPRET=1)  -> attn_*.npz
+  * benchmarks/jetspec_numeric_oracles.py parent_chain + fp64_attention
+    (the reference's fp64 per-node oracle)                       -> attn_*.npz ("fp64_*")
+  * layers/attention.py store_kvcache (Triton kernel, interpreter) -> kv_store.npz
+  * speculative/jetspec/state.py copy_accepted_kv (torch on CPU)   -> kv_commit.npz
+
+The fixtures hold only live K/V rows (bf16 bit patterns) plus seeds and shapes, so they
+stay small; the tests rebuild the NaN-poisoned pools from them.  The GPU box never runs
+this script (the reference is not there); it only reads the .npz files.
+"""
+from __future__ import annotations
+
+import argparse
+import os
+from pathlib import Path
+import sys
+
+os.environ.setdefault("TRITON_INTERPRET", "1")  # must precede the first triton import
+
+import numpy as np
+import torch
+
+HERE = Path(__file__).resolve().parent
+
+
+def bf16_bits(t: torch.Tensor) -> np.ndarray:
+    return t.contiguous().to(torch.bfloat16).view(torch.int16).numpy().view(np.uint16)
+
+
+def random_parents(rng: np.random.Generator, nodes: int, window: int = 8) -> list[int]:
+    parents = [-1]
+    for node in range(1, nodes):
+        parents.append(int(rng.integers(max(0, node - window), node)))
+    return parents
+
+
+def ancestors(parents: list[int]) -> torch.Tensor:
+    n = len(parents)
+    mask = torch.zeros((n, n), dtype=torch.bool)
+    for node in range(n):
+        cur = node
+        while cur != -1:
+            mask[node, cur] = True
+            cur = parents[cur]
+    return mask
+
+
+def attention_case(name, prefixes, tables, parents, slot_base, num_blocks, kv_heads, groups,
+                   head_dim, seed, fp64_rows):
+    from nanovllm.speculative.jetspec.packed_metadata import PackedTreeMetadata
+    from nanovllm.speculative.jetspec.paged_backend import _packed_paged_tree_fp32
+    from benchmarks.jetspec_numeric_oracles import fp64_attention, parent_chain
+
+    bs = 256
+    counts = [len(p) for p in parents]
+    starts = np.concatenate(([0], np.cumsum(counts))).astype(int)
+    slots = [torch.arange(slot_base + starts[i], slot_base + starts[i + 1], dtype=torch.int64)
+             for i in range(len(counts))]
+    masks = [ancestors(p) for p in parents]
+    meta = PackedTreeMetadata.build(prefixes, tables, slots, masks, bs)
+    gen = torch.Generator().manual_seed(seed)
+    Q, Hq = meta.total_queries, kv_heads * groups
+    q = (torch.randn((Q, Hq, head_dim), generator=gen) * head_dim ** -0.5).to(torch.bfloat16)
+    live = []
+    for r, prefix in enumerate(prefixes):
+        pos = torch.arange(prefix, dtype=torch.int64)
+        page = torch.tensor(list(tables[r]) or [0], dtype=torch.int64)
+        if prefix:
+            live.append(page[pos // bs] * bs + pos % bs)
+        live.append(slots[r])
+    live = torch.cat(live)
+    k_rows = (torch.randn((live.numel(), kv_heads, head_dim), generator=gen)
+              * head_dim ** -0.5).to(torch.bfloat16)
+    v_rows = (torch.randn((live.numel(), kv_heads, head_dim), generator=gen)
+              * head_dim ** -0.5).to(torch.bfloat16)
+    # fp32 pools holding bf16-exact values; unleased rows NaN (never read by the kernel)
+    k = torch.full((num_blocks, bs, kv_heads, head_dim), float("nan"))
+    v = torch.full_like(k, float("nan"))
+    k.view(-1, kv_heads, head_dim)[live] = k_rows.float()
+    v.view(-1, kv_heads, head_dim)[live] = v_rows.float()
+    qf = q.float()
+    out = torch.empty((Q, Hq, head_dim), dtype=torch.float32)
+    scale = head_dim ** -0.5
+    _packed_paged_tree_fp32[(Q, Hq)](
+        out, qf, k, v,
+        meta.query_to_request, meta.query_local_row, meta.prefix_lens, meta.node_counts,
+        meta.cu_seqlens_q, meta.block_tables, meta.tree_slots, meta.qq_bias, meta.qq_bias_offsets,
+        scale,
+        q_stride_0=qf.stride(0), q_stride_1=qf.stride(1),
+        out_stride_0=out.stride(0), out_stride_1=out.stride(1),
+        table_stride_0=meta.block_tables.stride(0),
+        k_stride_0=k.stride(0), k_stride_1=k.stride(1), k_stride_2=k.stride(2), k_stride_3=k.stride(3),
+        v_stride_0=v.stride(0), v_stride_1=v.stride(1), v_stride_2=v.stride(2), v_stride_3=v.stride(3),
+        num_queries_per_kv=groups, block_size=bs, head_size=head_dim,
+        BLOCK_D=max(16, 1 << (head_dim - 1).bit_length()), TILE=64,
+    )
+    # fp64 oracle rows: prefix keys followed by the node's root-to-node chain
+    fp64_idx, fp64_out = [], []
+    for r, node in fp64_rows:
+        chain = parent_chain(parents[r], node)
+        prefix = prefixes[r]
+        pos = torch.arange(prefix, dtype=torch.int64)
+        page = torch.tensor(list(tables[r]) or [0], dtype=torch.int64)
+        keys_slots = torch.cat(((page[pos // bs] * bs + pos % bs) if prefix else
+                                torch.empty(0, dtype=torch.int64), slots[r][chain]))
+        kk = k.view(-1, kv_heads, head_dim)[keys_slots]
+        vv = v.view(-1, kv_heads, head_dim)[keys_slots]
+        row = int(starts[r] + node)
+        fp64_idx.append(row)
+        fp64_out.append(fp64_attention(qf[row], kk, vv, scale, groups).numpy())
+    np.savez_compressed(
+        HERE / f"attn_{name}.npz",
+        prefixes=np.asarray(prefixes, dtype=np.int64),
+        tables=np.asarray([list(t) + [-1] * (4 - len(t)) for t in tables], dtype=np.int64),
+        parents=np.asarray([p + [-2] * (max(counts) - len(p)) for p in parents], dtype=np.int64),
+        counts=np.asarray(counts, dtype=np.int64),
+        slot_base=np.int64(slot_base), num_blocks=np.int64(num_blocks),
+        kv_heads=np.int64(kv_heads), groups=np.int64(groups), head_dim=np.int64(head_dim),
+        scale=np.float64(scale),
+        q_bits=bf16_bits(q), live_slots=live.numpy(), k_bits=bf16_bits(k_rows),
+        v_bits=bf16_bits(v_rows), ref_out=out.numpy(),
+        fp64_rows=np.asarray(fp64_idx, dtype=np.int64), fp64_out=np.stack(fp64_out),
+    )
+    print(f"attn_{name}: Q={Q} Hq={Hq} D={head_dim} live={live.numel()} finite={torch.isfinite(out).all().item()}")
+
+
+def metadata_case():
+    """The reference's own CPU metadata fixture (tests/test_jetspec_packed_attention.py:23-44)."""
+    from nanovllm.speculative.jetspec.packed_metadata import PackedTreeMetadata
+
+    def heap_ancestors(nodes):
+        result = torch.zeros((nodes, nodes), dtype=torch.bool)
+        for node in range(nodes):
+            cur = node
+            while cur >= 0:
+                result[node, cur] = True
+                cur = (cur - 1) // 2
+        return result
+
+    counts = (63, 31, 47)
+    starts = np.concatenate(([0], np.cumsum(counts))).astype(int)
+    slots = [torch.arange(6 * 256 + starts[i], 6 * 256 + starts[i + 1], dtype=torch.int64)
+             for i in range(3)]
+    meta = PackedTreeMetadata.build((65, 0, 257), ((2,), (), (4, 0)), slots,
+                                    [heap_ancestors(c) for c in counts], 256)
+    np.savez_compressed(
+        HERE / "metadata_ragged3.npz",
+        cu_seqlens_q=meta.cu_seqlens_q.numpy(), query_to_request=meta.query_to_request.numpy(),
+        query_local_row=meta.query_local_row.numpy(), prefix_lens=meta.prefix_lens.numpy(),
+        block_tables=meta.block_tables.numpy(), tree_slots=meta.tree_slots.numpy(),
+        qq_bias=meta.qq_bias.numpy(), qq_bias_offsets=meta.qq_bias_offsets.numpy(),
+        node_counts=meta.node_counts.numpy(), counts=np.asarray(counts),
+    )
+    print("metadata_ragged3: Q =", meta.total_queries)
+
+
+def kv_cases():
+    from nanovllm.layers.attention import store_kvcache
+    from nanovllm.speculative.jetspec.state import copy_accepted_kv
+
+    gen = torch.Generator().manual_seed(2024)
+    # store_kvcache: 6 tokens, 2 heads x 8 dims, 3 pages of 16, one skipped slot (-1)
+    key = torch.randn((6, 2, 8), generator=gen)
+    value = torch.randn((6, 2, 8), generator=gen)
+    k_cache = torch.randn((3, 16, 2, 8), generator=gen)
+    v_cache = torch.randn((3, 16, 2, 8), generator=gen)
+    slots = torch.tensor([5, 17, -1, 40, 0, 33], dtype=torch.int64)
+    k_before, v_before = k_cache.clone(), v_cache.clone()
+    store_kvcache(key, value, k_cache, v_cache, slots)
+    np.savez_compressed(HERE / "kv_store.npz", key=key.numpy(), value=value.numpy(),
+                        k_before=k_before.numpy(), v_before=v_before.numpy(),
+                        slots=slots.numpy(), k_after=k_cache.numpy(), v_after=v_cache.numpy())
+    # copy_accepted_kv: pool [2, L=3, 4 pages, 16, 2 heads, 8], overlapping src/dst
+    pool = torch.randn((2, 3, 4, 16, 2, 8), generator=gen)
+    before = pool.clone()
+    src = torch.tensor([3, 4, 5, 6, 20, 33], dtype=torch.int64)
+    dst = torch.tensor([4, 5, 6, 7, 48, 34], dtype=torch.int64)
+    nbytes = copy_accepted_kv(pool, src, dst, 16)
+    np.savez_compressed(HERE / "kv_commit.npz", before=before.numpy(), after=pool.numpy(),
+                        src=src.numpy(), dst=dst.numpy(), nbytes=np.int64(nbytes))
+    print("kv_store / kv_commit: payload bytes", nbytes)
+
+
+def main():
+    parser = argparse.ArgumentParser()
+    parser.add_argument("--reference", required=True, help="path of the reference checkout")
+    args = parser.parse_args()
+    sys.path.insert(0, str(Path(args.reference).resolve()))
+    metadata_case()
+    kv_cases()
+    rng = np.random.default_rng(7)
+    parents = [random_parents(rng, n) for n in (7, 5, 9)]
+    attention_case("ragged3", (65, 0, 257), ((2,), (), (4, 0)), parents, 6 * 256, 8,
+                   kv_heads=2, groups=2, head_dim=16, seed=317,
+                   fp64_rows=[(0, 0), (0, 6), (1, 4), (2, 8), (2, 3)])
+    rng = np.random.default_rng(1001)
+    parents1 = [random_parents(rng, 16, window=16)]
+    attention_case("config1", (512,), ((3, 0),), parents1, 4 * 256, 5,
+                   kv_heads=1, groups=4, head_dim=128, seed=1001,
+                   fp64_rows=[(0, 0), (0, 7), (0, 15)])
+
+
+if __name__ == "__main__":
+    main()
