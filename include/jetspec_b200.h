@@ -179,6 +179,46 @@ typedef struct JtKvCommitParams {
 int jt_kv_commit_launch(const JtKvCommitParams* params, cudaStream_t stream);
 int32_t jt_kv_commit_max_slots(void);
 
+/*
+ * HF-order RoPE of Q and K with the tree-node K/V scatter, in one launch:
+ *   out[r, h]                    = rope(q[r, h], positions[r])      every query head h
+ *   k_pool[s / bs, s % bs, kh]   = rope(k[r, kh], positions[r])     s = node_slots[r]
+ *   v_pool[s / bs, s % bs, kh]   = v[r, kh]
+ * rope(x) = [x1*cos - x2*sin, x2*cos + x1*sin] over the two halves of the head dim, with
+ * cos/sin = cache[positions[r], :dim/2] and [dim/2:] converted to the operand type, and
+ * every product rounded to the operand type before the add / subtract (eager PyTorch
+ * order; no fused multiply-add).  Bit-exact with rope_scatter_prevalidated
+ * (nanovllm/speculative/jetspec/tree_fusion.py:181-199, kernel :31-83).  The caller
+ * guarantees in-range positions, unique in-range slots and non-aliasing buffers (the
+ * prevalidated contract); out-of-range slots are skipped and flagged in the device error
+ * word.  All strides in elements.
+ */
+typedef struct JtRopeScatterParams {
+  const void* q;             /* [rows, q_heads, dim]  bf16 or fp32 */
+  const void* k;             /* [rows, kv_heads, dim] */
+  const void* v;             /* [rows, kv_heads, dim] */
+  const void* positions;     /* [rows] int32 or int64 */
+  const void* cos_sin_cache; /* [max_position, dim] (cos | sin), bf16 or fp32 */
+  const void* node_slots;    /* [rows] int32 or int64 */
+  void* out;                 /* [rows, q_heads, dim] rotated Q */
+  void* k_pool;              /* [pages, page_size, kv_heads, dim] */
+  void* v_pool;
+  int32_t dtype;             /* JT_BF16 or JT_F32 (q, k, v, out, pools) */
+  int32_t cache_dtype;       /* JT_BF16 or JT_F32 */
+  int32_t positions_is_int64, slots_is_int64;
+  int32_t rows, q_heads, kv_heads, head_dim, page_size;
+  int64_t num_pages;
+  int64_t q_stride0, q_stride1, q_stride2;
+  int64_t k_stride0, k_stride1, k_stride2;
+  int64_t v_stride0, v_stride1, v_stride2;
+  int64_t positions_stride, slots_stride, cache_stride0, cache_stride_last;
+  int64_t out_stride0, out_stride1, out_stride2;
+  int64_t kp_stride0, kp_stride1, kp_stride2, kp_stride3;
+  int64_t vp_stride0, vp_stride1, vp_stride2, vp_stride3;
+} JtRopeScatterParams;
+
+int jt_rope_scatter_launch(const JtRopeScatterParams* params, cudaStream_t stream);
+
 /* Library information / diagnostics. */
 int32_t jt_abi_version(void);
 const char* jt_last_error(void);

@@ -8,6 +8,7 @@ verifier, scratch arena and block tables work unchanged:
 * store_kvcache              - nanovllm/layers/attention.py:38
 * copy_accepted_kv           - nanovllm/speculative/jetspec/state.py:64
 * PackedTreeMetadata         - nanovllm/speculative/jetspec/packed_metadata.py:16
+* rope_scatter(_prevalidated) - nanovllm/speculative/jetspec/tree_fusion.py:172-199
 
 All compute runs in libjetspec_b200.so (hand-written CUDA for sm_100a) through a C ABI
 (include/jetspec_b200.h).  There is no CPU or library fallback: without the built
@@ -19,12 +20,13 @@ from .packed_metadata import PackedTreeMetadata, ancestor_mask_from_parents
 from .paged_backend import packed_tree_attention, packed_tree_attention_reference
 from .sharding import KvHeadShard, shard_for_rank
 from .state import _slots_for_blocks, copy_accepted_kv
-from .tree_fusion import scatter_tree_kv
+from .tree_fusion import rope_scatter, rope_scatter_prevalidated, scatter_tree_kv
 from .tree_gqa import packed_tree_attention_gqa
 
 __all__ = [
     "KernelLaunchError", "LibraryMissingError", "load_library", "read_device_errors",
     "store_kvcache", "PackedTreeMetadata", "ancestor_mask_from_parents",
     "packed_tree_attention", "packed_tree_attention_reference", "KvHeadShard",
-    "shard_for_rank", "copy_accepted_kv", "scatter_tree_kv", "packed_tree_attention_gqa",
+    "shard_for_rank", "copy_accepted_kv", "scatter_tree_kv", "rope_scatter",
+    "rope_scatter_prevalidated", "packed_tree_attention_gqa",
 ]

@@ -28,6 +28,7 @@ EXPORTED_SYMBOLS = (
     "jt_tree_attn_launch_noalloc",
     "jt_kv_store_launch",
     "jt_kv_commit_launch",
+    "jt_rope_scatter_launch",
     "jt_kv_commit_max_slots",
     "jt_abi_version",
     "jt_last_error",
@@ -93,6 +94,25 @@ class JtKvCommitParams(ctypes.Structure):
     ]
 
 
+class JtRopeScatterParams(ctypes.Structure):
+    _fields_ = [
+        ("q", c_void_p), ("k", c_void_p), ("v", c_void_p), ("positions", c_void_p),
+        ("cos_sin_cache", c_void_p), ("node_slots", c_void_p), ("out", c_void_p),
+        ("k_pool", c_void_p), ("v_pool", c_void_p),
+        ("dtype", c_i32), ("cache_dtype", c_i32), ("positions_is_int64", c_i32),
+        ("slots_is_int64", c_i32), ("rows", c_i32), ("q_heads", c_i32), ("kv_heads", c_i32),
+        ("head_dim", c_i32), ("page_size", c_i32), ("num_pages", c_i64),
+        ("q_stride0", c_i64), ("q_stride1", c_i64), ("q_stride2", c_i64),
+        ("k_stride0", c_i64), ("k_stride1", c_i64), ("k_stride2", c_i64),
+        ("v_stride0", c_i64), ("v_stride1", c_i64), ("v_stride2", c_i64),
+        ("positions_stride", c_i64), ("slots_stride", c_i64), ("cache_stride0", c_i64),
+        ("cache_stride_last", c_i64),
+        ("out_stride0", c_i64), ("out_stride1", c_i64), ("out_stride2", c_i64),
+        ("kp_stride0", c_i64), ("kp_stride1", c_i64), ("kp_stride2", c_i64), ("kp_stride3", c_i64),
+        ("vp_stride0", c_i64), ("vp_stride1", c_i64), ("vp_stride2", c_i64), ("vp_stride3", c_i64),
+    ]
+
+
 _lock = threading.Lock()
 _lib = None
 
@@ -110,6 +130,8 @@ def _declare(lib):
     lib.jt_kv_store_launch.restype = ctypes.c_int
     lib.jt_kv_commit_launch.argtypes = [P(JtKvCommitParams), c_void_p]
     lib.jt_kv_commit_launch.restype = ctypes.c_int
+    lib.jt_rope_scatter_launch.argtypes = [P(JtRopeScatterParams), c_void_p]
+    lib.jt_rope_scatter_launch.restype = ctypes.c_int
     lib.jt_kv_commit_max_slots.argtypes = []
     lib.jt_kv_commit_max_slots.restype = c_i32
     lib.jt_abi_version.argtypes = []

@@ -27,11 +27,13 @@ extern "C" const char* jt_last_error(void) { return g_last_error; }
 
 extern "C" int jt_read_device_errors(uint32_t* errors) {
   if (errors == nullptr) return jt_fail(JT_ERR_INVALID, "jt_read_device_errors: null output");
-  uint32_t a = 0, b = 0;
+  uint32_t a = 0, b = 0, c = 0;
   int rc = jt_read_errors_kv(&a);
   if (rc != JT_OK) return rc;
   rc = jt_read_errors_attn(&b);
   if (rc != JT_OK) return rc;
-  *errors = a | b;
+  rc = jt_read_errors_rope(&c);
+  if (rc != JT_OK) return rc;
+  *errors = a | b | c;
   return JT_OK;
 }

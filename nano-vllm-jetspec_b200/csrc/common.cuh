@@ -18,6 +18,7 @@ int jt_cuda_check(cudaError_t err, const char* what);
 // Per-translation-unit device error word readers (each TU owns its own word).
 int jt_read_errors_kv(uint32_t* bits);
 int jt_read_errors_attn(uint32_t* bits);
+int jt_read_errors_rope(uint32_t* bits);
 
 #define JT_DEVERR_OUT_OF_RANGE 1u
 #define JT_DEVERR_TREE_TOO_LARGE 2u

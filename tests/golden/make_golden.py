@@ -13,6 +13,8 @@ Everything here executes the reference's own code on the CPU:
     (the reference's fp64 per-node oracle)                       -> attn_*.npz ("fp64_*")
   * layers/attention.py store_kvcache (Triton kernel, interpreter) -> kv_store.npz
   * speculative/jetspec/state.py copy_accepted_kv (torch on CPU)   -> kv_commit.npz
+  * speculative/jetspec/tree_fusion.py _rope_scatter_hf_order (interpreter; fp32) and the
+    eager RoPE definition of its byte-exact test (bf16)           -> rope_scatter.npz
 
 The fixtures hold only live K/V rows (bf16 bit patterns) plus seeds and shapes, so they
 stay small; the tests rebuild the NaN-poisoned pools from them.  The GPU box never runs
@@ -31,6 +33,7 @@ import numpy as np
 import torch
 
 HERE = Path(__file__).resolve().parent
+REFERENCE = None  # the reference checkout (set from --reference)
 
 
 def bf16_bits(t: torch.Tensor) -> np.ndarray:
@@ -191,13 +194,73 @@ def kv_cases():
     print("kv_store / kv_commit: payload bytes", nbytes)
 
 
+def rope_cases():
+    """The reference's fused RoPE + scatter kernel (tree_fusion.py:31-83) on its own CPU
+    fixture shapes (tests/test_jetspec_tree_fusion.py:35-68), run by the interpreter."""
+    from nanovllm.speculative.jetspec.tree_fusion import _rope_scatter_hf_order
+
+    out_arrays = {}
+    for dtype_name, dtype in (("bf16", torch.bfloat16), ("f32", torch.float32)):
+        gen = torch.Generator().manual_seed(740319)
+        rows, q_heads, kv_heads, dim = 7, 8, 2, 128
+        q = torch.randn(rows, q_heads, dim, generator=gen).to(dtype)
+        k = torch.randn(rows, kv_heads, dim, generator=gen).to(dtype)
+        v = torch.randn(rows, kv_heads, dim, generator=gen).to(dtype)
+        positions = torch.tensor([0, 1, 127, 255, 513, 1023, 2047])
+        slots = torch.tensor([257, 1, 767, 256, 0, 513, 511])
+        angles = torch.arange(2048, dtype=torch.float32)[:, None] * (
+            torch.arange(dim // 2, dtype=torch.float32)[None, :] + 1) * .00317
+        cache = torch.cat((angles.cos(), angles.sin()), -1).unsqueeze(1)
+        pools = torch.randn(2, 4, 256, kv_heads, dim, generator=gen).to(dtype)
+        before = pools.clone()
+        k_pool, v_pool = pools[0], pools[1]
+        out = torch.empty_like(q)
+        _rope_scatter_hf_order[(rows, q_heads)](
+            q, k, v, positions, cache, slots, out, k_pool, v_pool,
+            *q.stride(), *k.stride(), *v.stride(), positions.stride(0), slots.stride(0),
+            cache.stride(0), cache.stride(-1), *out.stride(), *k_pool.stride(), *v_pool.stride(),
+            KV_HEADS=kv_heads, HEAD_DIM=dim, PAGE_SIZE=256, HALF_BLOCK=64,
+            num_warps=4, enable_fp_fusion=False)
+        # The reference's byte-exact gate (tests/test_jetspec_tree_fusion.py) holds its
+        # kernel equal to its eager definition on the GPU.  The Triton interpreter does not
+        # emulate bf16 rounding faithfully, so the bf16 golden is the reference's eager
+        # definition itself; for fp32 the interpreted kernel and the eager form agree bit
+        # for bit and the kernel output is kept.
+        sys.path.insert(0, str(REFERENCE / "tests"))
+        from test_jetspec_tree_fusion import eager_rope
+        rq, rk = eager_rope(q, k, positions, cache)
+        if dtype == torch.bfloat16:
+            out = rq
+            pools = before.clone()
+            pools[0][slots // 256, slots % 256] = rk
+            pools[1][slots // 256, slots % 256] = v
+        else:
+            assert torch.equal(out.view(torch.uint8), rq.view(torch.uint8))
+        enc = (lambda t: t.contiguous().view(torch.int16).numpy().view(np.uint16)) \
+            if dtype == torch.bfloat16 else (lambda t: t.contiguous().numpy().view(np.uint32))
+        touched = pools[:, slots // 256, slots % 256]          # [2, rows, kv_heads, dim]
+        untouched = before.clone()
+        untouched[:, slots // 256, slots % 256] = pools[:, slots // 256, slots % 256]
+        assert torch.equal(untouched.view(torch.uint8), pools.view(torch.uint8))
+        out_arrays.update({f"{dtype_name}_q": enc(q), f"{dtype_name}_k": enc(k),
+                           f"{dtype_name}_v": enc(v), f"{dtype_name}_out": enc(out),
+                           f"{dtype_name}_kv_rows_after": enc(touched)})
+        out_arrays["positions"], out_arrays["slots"] = positions.numpy(), slots.numpy()
+        out_arrays["cache_rows"] = cache[positions].numpy()   # [rows, 1, dim] fp32
+    np.savez_compressed(HERE / "rope_scatter.npz", **out_arrays)
+    print("rope_scatter: bf16 and f32 cases")
+
+
 def main():
     parser = argparse.ArgumentParser()
     parser.add_argument("--reference", required=True, help="path of the reference checkout")
     args = parser.parse_args()
-    sys.path.insert(0, str(Path(args.reference).resolve()))
+    global REFERENCE
+    REFERENCE = Path(args.reference).resolve()
+    sys.path.insert(0, str(REFERENCE))
     metadata_case()
     kv_cases()
+    rope_cases()
     rng = np.random.default_rng(7)
     parents = [random_parents(rng, n) for n in (7, 5, 9)]
     attention_case("ragged3", (65, 0, 257), ((2,), (), (4, 0)), parents, 6 * 256, 8,
