@@ -163,6 +163,19 @@ def cpu_oracle_rate(batch, budget_s: float, seed: int = 5):
     return tokens / elapsed, sample, threads
 
 
+def workload_config(batch, world: int) -> dict:
+    """The `config` object of both arms' JSON lines (same workload, same keys)."""
+    keys = sum(p + t for p, t in zip(batch.prefix_lens, batch.node_counts))
+    return {
+        "workload": (f"config3 serving mix x{world}: {batch.num_requests} requests, "
+                     f"ctx log-uniform[512,16384], trees {{16,32,64,128}}, "
+                     f"GQA 32/8 D128 bf16, KV heads {KV_HEADS // world} per GPU"),
+        "requests": batch.num_requests, "tree_tokens": batch.total_queries,
+        "kv_bytes_per_step_all_gpus": keys * KV_HEADS * HEAD_DIM * 2 * 2,
+        "parallelism": f"kv-head shard x{world}",
+        "l2": "inputs larger than L2 (KV per GPU per step > 126 MB)"}
+
+
 def run_reference(args, rank: int, world: int):
     if rank != 0:
         return
@@ -180,8 +193,7 @@ def run_reference(args, rank: int, world: int):
             "warmup": warmup, "ms_per_step": None, "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "f32 (bf16 operands)", "data": "synthetic",
             "impl": "reference",
-            "config": {"workload": f"config3 serving mix, {batch.num_requests} requests",
-                       "kv_heads_per_gpu": KV_HEADS // world},
+            "config": workload_config(batch, world),
             "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": "port",
                              "sample": f"per step: {sample}"},
             "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
@@ -365,14 +377,7 @@ def main():
                 "metric": METRIC, "value": tokens / (ms * 1e-3), "unit": UNIT, "n_gpus": world,
                 "steps": steps, "warmup": warmup, "ms_per_step": ms, "higher_is_better": True,
                 "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-                "config": {
-                    "workload": (f"config3 serving mix x{world}: {batch.num_requests} requests, "
-                                 f"ctx log-uniform[512,16384], trees {{16,32,64,128}}, "
-                                 f"GQA 32/8 D128 bf16, KV heads {KV_HEADS // world} per GPU"),
-                    "requests": batch.num_requests, "tree_tokens": tokens,
-                    "kv_bytes_per_step_all_gpus": kv_total,
-                    "parallelism": f"kv-head shard x{world}",
-                    "l2": "inputs larger than L2 (KV per GPU per step > 126 MB)"},
+                "config": workload_config(batch, world),
                 "effective_kv_gbs": kv_total / (attn_ms * 1e-3) / 1e9,
                 "attention_ms": attn_ms,
                 "roofline": {"bound": "hbm", "achieved": achieved, "peak": pk["hbm_gbs"],
