@@ -7,7 +7,7 @@ commit.  At N GPUs the global batch has N x 64 requests and every GPU owns 8/N o
 8 KV heads of every request (KV-head sharding: per-GPU work is fixed, scaling "weak";
 there is no collective on the data path, only the timing max-reduction).
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference|reference-triton]
 
 Rank 0 prints one JSON line.  ``--impl reference`` times the reference's CPU path (the
 oracle port of its masked-SDPA attention) on the host cores for the same workload.
@@ -47,7 +47,10 @@ def parse():
     parser.add_argument("--gpus", type=int, default=1)
     parser.add_argument("--steps", type=int, default=200)
     parser.add_argument("--warmup", type=int, default=10)
-    parser.add_argument("--impl", choices=("ours", "reference"), default="ours")
+    parser.add_argument("--impl", choices=("ours", "reference", "reference-triton"),
+                        default="ours",
+                        help="reference-triton: the reference's own Triton kernels (installed "
+                             "under baseline/_ref) beside ours on configs 1-4, one GPU")
     parser.add_argument("--requests-per-gpu", type=int, default=64)
     parser.add_argument("--no-cpu-baseline", action="store_true")
     parser.add_argument("--cpu-seconds", type=float, default=12.0,
@@ -200,6 +203,78 @@ def run_reference(args, rank: int, world: int):
     print(json.dumps(line), flush=True)
 
 
+# ---- the reference's own GPU kernels on this GPU ---------------------------------------
+def run_reference_triton(args, rank: int):
+    """Reference Triton kernels and ours on the same inputs (attention launch only).
+
+    Times ``packed_tree_attention_gqa`` (tree_gqa.py:114-140, the reference's fastest
+    path) and ``packed_tree_attention(backend="auto")`` (paged_backend.py:240-306, the
+    scalar fp32 kernel on devices other than sm_120) from the reference package installed
+    under ``baseline/_ref``, beside this package's ``packed_tree_attention_gqa``, with CUDA
+    events per call and a 256 MB L2 flush before each call.  Prints one JSON line per
+    configuration with medians and the max-abs output differences.
+    """
+    if rank != 0:
+        return
+    ref_root = ROOT / "baseline" / "_ref"
+    if not (ref_root / "nanovllm").is_dir():
+        print(json.dumps({"impl": "reference-triton",
+                          "unavailable": "reference package not installed under baseline/_ref"}))
+        return
+    sys.path.insert(0, str(ref_root))
+    from nanovllm.speculative.jetspec.paged_backend import packed_tree_attention as ref_dispatch
+    from nanovllm.speculative.jetspec.tree_gqa import packed_tree_attention_gqa as ref_gqa
+
+    device = torch.device("cuda", 0)
+    torch.cuda.set_device(device)
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=device)
+    scale = HEAD_DIM ** -0.5
+    steps, warmup = max(args.steps, 1), max(args.warmup, 3)
+    for name in ("config1", "config2", "config3", "config4"):
+        batch = workloads.CONFIGS[name]()
+        q, k, v = workloads.make_tensors(batch, device, poison=False, generator_device="cuda")
+        meta = batch.metadata(device)
+        arms = {
+            "ours": lambda: jb.packed_tree_attention_gqa(q, k, v, meta, scale, GROUPS),
+            "reference_gqa": lambda: ref_gqa(q, k, v, meta, scale, GROUPS),
+            "reference_auto": lambda: ref_dispatch(q, k, v, meta, scale, GROUPS),
+        }
+        outs, ms = {}, {}
+        for arm, fn in arms.items():
+            outs[arm] = fn().float()
+            torch.cuda.synchronize(device)
+            # The scalar fp32 kernel takes tens of ms at the larger configurations.
+            reps = steps if arm != "reference_auto" else max(3, min(steps, 10))
+            times = []
+            for i in range(warmup + reps):
+                flush.zero_()
+                start = torch.cuda.Event(enable_timing=True)
+                end = torch.cuda.Event(enable_timing=True)
+                start.record()
+                fn()
+                end.record()
+                torch.cuda.synchronize(device)
+                if i >= warmup:
+                    times.append(start.elapsed_time(end))
+            ms[arm] = statistics.median(times)
+        kv_bytes = batch.kv_bytes()
+        line = {
+            "impl": "reference-triton", "workload": name, "requests": batch.num_requests,
+            "tree_tokens": batch.total_queries, "kv_bytes": kv_bytes, "steps": steps,
+            "warmup": warmup, "l2": "256 MB flush before every call",
+            "ms": ms,
+            "tree_tokens_per_s": {a: batch.total_queries / (t * 1e-3) for a, t in ms.items()},
+            "effective_kv_gbs": {a: kv_bytes / (t * 1e-3) / 1e9 for a, t in ms.items()},
+            "speedup_of_ours": {a: ms[a] / ms["ours"] for a in ms if a != "ours"},
+            "max_abs_diff_vs_ours": {a: (outs[a] - outs["ours"]).abs().max().item()
+                                     for a in outs if a != "ours"},
+            "finite": {a: bool(torch.isfinite(o).all()) for a, o in outs.items()},
+        }
+        print(json.dumps(line), flush=True)
+        del q, k, v, meta, outs
+        torch.cuda.empty_cache()
+
+
 # ---- GPU side -------------------------------------------------------------------------
 class Step:
     """Device-resident inputs of one verify step on this rank's KV-head shard."""
@@ -343,6 +418,8 @@ def main():
     local_rank = int(os.environ.get("LOCAL_RANK", 0))
     if args.impl == "reference":
         return run_reference(args, rank, world)
+    if args.impl == "reference-triton":
+        return run_reference_triton(args, rank)
     if world != args.gpus and "WORLD_SIZE" in os.environ:
         args.gpus = world
     device = torch.device("cuda", local_rank)
