@@ -149,6 +149,31 @@ __device__ __forceinline__ void tc_commit(uint32_t bar) {
       : "memory");
 }
 
+// Warp-wide forms: every lane of the warp executes them with identical operands and
+// elect.sync picks one lane (always the same one for a fully active warp) to issue, so the
+// operands stay warp-uniform and the issuing lane is the one whose MMAs each commit tracks.
+__device__ __forceinline__ void tc_commit_warp(uint32_t bar) {
+  asm volatile(
+      "{\n .reg .pred e;\n elect.sync _|e, 0xffffffff;\n"
+      " @e tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];\n}\n" ::"r"(
+          bar)
+      : "memory");
+}
+__device__ __forceinline__ void mma_ss_warp(uint32_t d, uint64_t a, uint64_t b, uint32_t idesc,
+                                            uint32_t acc) {
+  asm volatile(
+      "{\n .reg .pred p, e;\n setp.ne.b32 p, %4, 0;\n elect.sync _|e, 0xffffffff;\n"
+      " @e tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}\n" ::"r"(d),
+      "l"(a), "l"(b), "r"(idesc), "r"(acc));
+}
+__device__ __forceinline__ void mma_ts_warp(uint32_t d, uint32_t a_tmem, uint64_t b,
+                                            uint32_t idesc, uint32_t acc) {
+  asm volatile(
+      "{\n .reg .pred p, e;\n setp.ne.b32 p, %4, 0;\n elect.sync _|e, 0xffffffff;\n"
+      " @e tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n}\n" ::"r"(d),
+      "r"(a_tmem), "l"(b), "r"(idesc), "r"(acc));
+}
+
 // Shared-memory matrix descriptor, 128-byte swizzle (sm_100 descriptor version 1).
 __device__ __forceinline__ uint64_t smem_desc(uint32_t addr, uint32_t lbo, uint32_t sbo) {
   uint64_t d = static_cast<uint64_t>((addr & 0x3FFFFu) >> 4);
@@ -575,13 +600,19 @@ __global__ void __launch_bounds__(kThreads, 1)
     // t: PV t (once the softmax published P t) and QK t+3.  tcgen05.mma instructions of
     // one thread execute in issue order, so PV t has read P t out of its S buffer before
     // QK t+3 overwrites that buffer.
+    // The whole warp runs this loop with warp-uniform values; elect.sync inside the MMA
+    // and commit wrappers picks the issuing lane.  Descriptors are built once: within a
+    // tile they differ only in the start-address field (16-byte units), so each MMA adds
+    // a compile-time constant.
     uint32_t ring = 0, q_count = 0, g0 = 0;
     bool o_used = false;
     uint32_t of_par = 0;
+    const uint64_t q_desc = smem_desc(base + kOffQ, 16, 1024);
+    const uint64_t ring_k_desc = smem_desc(base + kOffRing, 16, 1024);
+    const uint64_t ring_v_desc = smem_desc(base + kOffRing, kKVHalfBytes, 1024);
     for (uint32_t seq = 0;; ++seq) {
       const int index = next_item(seq);
       if (index < 0) break;
-      if (lane != 0) continue;
       const Item it = decode(p, w, index, split_keys);
       const int n = it.n_tiles;
       mbar_wait(JT_BAR(kBarQFull), q_count & 1, abort);
@@ -594,24 +625,22 @@ __global__ void __launch_bounds__(kThreads, 1)
         return slot;
       };
       auto release = [&](int slot) {
-        tc_commit(JT_BAR(kBarEmpty + slot));
+        tc_commit_warp(JT_BAR(kBarEmpty + slot));
         ++ring;
       };
       auto issue_qk = [&](int t) {
         const int slot = take();
         const int b = (g0 + t) % kSBufs;
-        const uint32_t qa = base + kOffQ;
-        const uint32_t ka = base + kOffRing + slot * kKVBytes;
+        const uint64_t kd = ring_k_desc + static_cast<uint64_t>(slot * (kKVBytes >> 4));
 #pragma unroll
         for (int kk = 0; kk < kD / 16; ++kk) {
           const uint32_t off = (kk & 3) * 32;
-          mma_ss(tmem + col_s(b), smem_desc(qa + (kk >> 2) * kQHalfBytes + off, 16, 1024),
-                 smem_desc(ka + (kk >> 2) * kKVHalfBytes + off, 16, 1024), kIdescQK,
-                 kk > 0 ? 1u : 0u);
+          mma_ss_warp(tmem + col_s(b), q_desc + ((kk >> 2) * kQHalfBytes + off) / 16,
+                      kd + ((kk >> 2) * kKVHalfBytes + off) / 16, kIdescQK, kk > 0 ? 1u : 0u);
         }
-        tc_commit(JT_BAR(kBarSFull + b));
+        tc_commit_warp(JT_BAR(kBarSFull + b));
         release(slot);
-        if (t == n - 1) tc_commit(JT_BAR(kBarQEmpty));
+        if (t == n - 1) tc_commit_warp(JT_BAR(kBarQEmpty));
       };
       for (int t = 0; t < min(kAhead, n); ++t) issue_qk(t);
       for (int t = 0; t < n; ++t) {
@@ -627,25 +656,24 @@ __global__ void __launch_bounds__(kThreads, 1)
         tc_fence_after();
         // O += P V (P inside S buffer b in TMEM, V MN-major in shared memory).
         const uint32_t pa = tmem + col_s(b);
-        const uint32_t va = base + kOffRing + slot * kKVBytes;
+        const uint64_t vd = ring_v_desc + static_cast<uint64_t>(slot * (kKVBytes >> 4));
 #pragma unroll
         for (int kk = 0; kk < kN / 16; ++kk) {
-          const uint64_t bd = smem_desc(va + kk * 2048, kKVHalfBytes, 1024);
-          mma_ts(tmem + col_o(), pa + col_p(kk), bd, kIdescPV, (t > 0 || kk > 0) ? 1u : 0u);
-          if constexpr (FP32P) mma_ts(tmem + col_o(), pa + col_p(kk) + 32, bd, kIdescPV, 1u);
+          mma_ts_warp(tmem + col_o(), pa + col_p(kk), vd + kk * (2048 / 16), kIdescPV,
+                      (t > 0 || kk > 0) ? 1u : 0u);
+          if constexpr (FP32P)
+            mma_ts_warp(tmem + col_o(), pa + col_p(kk) + 32, vd + kk * (2048 / 16), kIdescPV, 1u);
         }
-        tc_commit(JT_BAR(kBarPvDone));
+        tc_commit_warp(JT_BAR(kBarPvDone));
         release(slot);
         if (t + kAhead < n) issue_qk(t + kAhead);
       }
       g0 += n;
       o_used = true;
     }
-    if (lane == 0) {
-      // Drain: every MMA this thread issued has completed before TMEM is released.
-      tc_commit(JT_BAR(kBarDrain));
-      mbar_wait(JT_BAR(kBarDrain), 0, abort, false);
-    }
+    // Drain: every MMA the issuing lane started has completed before TMEM is released.
+    tc_commit_warp(JT_BAR(kBarDrain));
+    mbar_wait(JT_BAR(kBarDrain), 0, abort, false);
   } else if (warp < 4) {
     // ------------------------------------------------------------------ loaders
     const int ltid = tid - 32;
