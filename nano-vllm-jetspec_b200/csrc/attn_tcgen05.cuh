@@ -51,7 +51,8 @@ constexpr int kOffBar = kOffRing + kRing * kKVBytes;
 constexpr int kOffMisc = kOffBar + 8 * 32;
 constexpr int kOffXl = kOffMisc + 64;                   // [2 halves][128] row sums
 constexpr int kOffXm = kOffXl + 2 * kM * 4;             // [tile parity][2 halves][128] maxima
-constexpr int kSmemBytes = kOffXm + 4 * kM * 4 + 1024;  // + alignment slack
+constexpr int kOffItem = kOffXm + 4 * kM * 4;           // [2] decoded work items (16 ints)
+constexpr int kSmemBytes = kOffItem + 2 * 64 + 1024;    // + alignment slack
 constexpr long long kWaitLimit = 4000000000ll;          // cycles (~2 s) per wait
 
 // TMEM column map (512 columns x 128 lanes x 32 bit): O, then the S buffers.
@@ -82,7 +83,9 @@ constexpr int kBarItemFull = 23;               // [2] work-item ring
 constexpr int kBarItemEmpty = 25;              // [2]
 constexpr int kNumBars = 27;
 constexpr int kItemConsumers = 12;             // every warp of the CTA reads each item
-constexpr int kLoaderWarps = 3;
+constexpr int kGatherThreads = 64;             // warps 2-3: cp.async tree tiles
+constexpr int kFullArrivals = 2;               // per ring fill: TMA (arrive_tx + arrive) or
+                                               // one arrival per gather warp
 static_assert(kNumBars * 8 <= 8 * 32, "barrier area");
 
 // ---- PTX wrappers ------------------------------------------------------------------
@@ -132,6 +135,32 @@ __device__ __forceinline__ void warp_arrive(uint32_t bar) {
 __device__ __forceinline__ void warp_wait(uint32_t bar, uint32_t parity, volatile int* abort) {
   if ((threadIdx.x & 31) == 0) mbar_wait(bar, parity, abort);
   __syncwarp();
+}
+
+// Release store / bounded acquire wait on a shared-memory position counter.
+__device__ __forceinline__ void st_release_shared(uint32_t addr, uint32_t v) {
+  asm volatile("st.release.cta.shared::cta.u32 [%0], %1;\n" ::"r"(addr), "r"(v) : "memory");
+}
+__device__ __forceinline__ uint32_t ld_acquire_shared(uint32_t addr) {
+  uint32_t v;
+  asm volatile("ld.acquire.cta.shared::cta.u32 %0, [%1];\n" : "=r"(v) : "r"(addr) : "memory");
+  return v;
+}
+// Waits until the counter reaches `target` (counters only grow; a difference of less than
+// 2^31 counts as reached).  Bounded like the mbarrier waits.
+__device__ __forceinline__ bool wait_shared_at_least(uint32_t addr, uint32_t target,
+                                                     volatile int* abort) {
+  if (static_cast<int>(ld_acquire_shared(addr) - target) >= 0) return true;
+  const long long start = clock64();
+  for (;;) {
+    if (static_cast<int>(ld_acquire_shared(addr) - target) >= 0) return true;
+    if (*abort) return false;
+    if (clock64() - start > kWaitLimit) {
+      *abort = 1;
+      atomicOr(&g_attn_errors, JT_DEVERR_TIMEOUT);
+      return false;
+    }
+  }
 }
 
 __device__ __forceinline__ void fence_proxy_async() {
@@ -335,27 +364,16 @@ __device__ __forceinline__ Item decode(const JtTreeAttnParams& p, const DevLayou
   return it;
 }
 
-// Loads one 128-key K or V tile into its ring stage: TMA when the keys are one page's
-// prefix run, else one cp.async row per loader thread (rows past key_end zero-filled).
-__device__ __forceinline__ void load_kv_tile(const JtTreeAttnParams& p, const Item& it,
-                                             const int32_t* table, int kb, bool full, int ltid,
-                                             int lane, uint32_t dst, const CUtensorMap* map,
-                                             const char* pool, int64_t s0, int64_t s1,
-                                             int64_t s2, uint32_t full_bar, int64_t pool_slots,
-                                             int page) {
+// Gathers one 128-key K or V tile that touches tree nodes (scattered scratch slots) into
+// its ring stage, one cp.async row per gather thread and step (rows past key_end are
+// zero-filled), and waits for the rows to land; the caller then arrives on the stage's
+// full barrier.
+__device__ __forceinline__ void gather_kv_tile(const JtTreeAttnParams& p, const Item& it,
+                                               const int32_t* table, int kb, int gtid,
+                                               uint32_t dst, const char* pool, int64_t s0,
+                                               int64_t s1, int64_t s2, int64_t pool_slots) {
   const int bs = p.block_size;
-  if (full) {
-    if (ltid == 0) {
-      const int off = kb % bs;
-      mbar_arrive_tx(full_bar, kKVBytes);
-      tma_load_4d(dst, map, 0, it.h, off, page, full_bar);
-      tma_load_4d(dst + kKVHalfBytes, map, 64, it.h, off, page, full_bar);
-    } else if (lane == 0) {
-      mbar_arrive(full_bar);
-    }
-    return;
-  }
-  for (int row = ltid; row < kN; row += 96) {
+  for (int row = gtid; row < kN; row += kGatherThreads) {
     const int pos = kb + row;
     int64_t off = -1;
     if (pos < it.key_end) {
@@ -381,8 +399,6 @@ __device__ __forceinline__ void load_kv_tile(const JtTreeAttnParams& p, const It
   }
   asm volatile("cp.async.wait_all;\n" ::: "memory");
   fence_proxy_async();
-  __syncwarp();
-  if (lane == 0) mbar_arrive(full_bar);
 }
 // Softmax helpers for one score row (the calling thread's TMEM lane) of one 128-key tile.
 // `vk` describes the tile for masked tiles: keys kb..kb+127, prefix P, range end, nodes T
@@ -547,7 +563,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   const uint32_t bar0 = base + kOffBar;
 #define JT_BAR(i) (bar0 + 8u * static_cast<uint32_t>(i))
   volatile int* misc = reinterpret_cast<volatile int*>(sbase + kOffMisc);
-  // misc[0]: TMEM base, misc[1]: abort, misc[4..5]: item ring
+  // misc[0]: TMEM base, misc[1]: abort, misc[2]: ring positions free to gather into
   volatile int* abort = misc + 1;
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -558,11 +574,11 @@ __global__ void __launch_bounds__(kThreads, 1)
           i == kBarLx)
         count = kSoftmaxWarps;
       if (i == kBarItemEmpty || i == kBarItemEmpty + 1) count = kItemConsumers;
-      if (i >= kBarFull && i < kBarFull + kRing) count = kLoaderWarps;
+      if (i >= kBarFull && i < kBarFull + kRing) count = kFullArrivals;
       mbar_init(JT_BAR(i), count);
     }
     misc[1] = 0;
-    misc[4] = misc[5] = -1;
+    misc[2] = 0;  // ring_free
     asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
   }
   if (warp == 0) {
@@ -580,18 +596,50 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int split_keys = w.header[2];
   const int G = p.groups, bs = p.block_size;
 
-  // Work items: loader thread 0 takes the next one from the device queue and publishes it
-  // through a two-entry ring.  Lane 0 of every warp reads each entry and broadcasts it
-  // (a warp always agrees with itself); after an abort every reader sees -1.
-  auto next_item = [&](uint32_t seq) -> int {
+  // Work items: lane 0 of the TMA warp takes the next one from the device queue, decodes
+  // it and publishes the decoded item through a two-entry ring in shared memory, one item
+  // ahead of its own loads, so no role waits on the decode's global-memory chain at an
+  // item boundary.  Lane 0 of every warp reads each entry and broadcasts it (a warp always
+  // agrees with itself); the end of the queue, or an abort, reads as no item.
+  volatile int* item_ring = reinterpret_cast<volatile int*>(sbase + kOffItem);
+  auto publish = [&](uint32_t seq) {
     const int slot = seq & 1;
-    int index = -1;
+    if (seq >= 2) mbar_wait(JT_BAR(kBarItemEmpty + slot), ((seq >> 1) - 1) & 1, abort);
+    volatile int* e = item_ring + 16 * slot;
+    const int index = *abort ? num_items : atomicAdd(&w.header[0], 1);
+    if (index < num_items) {
+      const Item it = decode(p, w, index, split_keys);
+      const int f[14] = {it.r, it.split, it.h, it.tp, it.n_split, it.mblocks, it.slot_base,
+                         it.counter_base, it.P, it.T, it.q_start, it.key_begin, it.key_end,
+                         it.n_tiles};
+#pragma unroll
+      for (int k = 0; k < 14; ++k) e[k] = f[k];
+      e[15] = 1;
+    } else {
+      e[15] = 0;
+    }
+    mbar_arrive(JT_BAR(kBarItemFull + slot));
+  };
+  auto next_item = [&](uint32_t seq, Item& it) -> bool {
+    const int slot = seq & 1;
+    int f[15];
+#pragma unroll
+    for (int k = 0; k < 15; ++k) f[k] = 0;
     if (lane == 0) {
-      if (mbar_wait(JT_BAR(kBarItemFull + slot), (seq >> 1) & 1, abort) && !*abort)
-        index = misc[4 + slot];
+      if (mbar_wait(JT_BAR(kBarItemFull + slot), (seq >> 1) & 1, abort) && !*abort) {
+        volatile int* e = item_ring + 16 * slot;
+        f[14] = e[15];
+#pragma unroll
+        for (int k = 0; k < 14; ++k) f[k] = e[k];
+      }
       mbar_arrive(JT_BAR(kBarItemEmpty + slot));
     }
-    return __shfl_sync(0xffffffffu, index, 0);
+#pragma unroll
+    for (int k = 0; k < 15; ++k) f[k] = __shfl_sync(0xffffffffu, f[k], 0);
+    it.r = f[0]; it.split = f[1]; it.h = f[2]; it.tp = f[3]; it.n_split = f[4];
+    it.mblocks = f[5]; it.slot_base = f[6]; it.counter_base = f[7]; it.P = f[8]; it.T = f[9];
+    it.q_start = f[10]; it.key_begin = f[11]; it.key_end = f[12]; it.n_tiles = f[13];
+    return f[14] != 0;
   };
 
   if (warp == 0) {
@@ -611,9 +659,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     const uint64_t ring_k_desc = smem_desc(base + kOffRing, 16, 1024);
     const uint64_t ring_v_desc = smem_desc(base + kOffRing, kKVHalfBytes, 1024);
     for (uint32_t seq = 0;; ++seq) {
-      const int index = next_item(seq);
-      if (index < 0) break;
-      const Item it = decode(p, w, index, split_keys);
+      Item it;
+      if (!next_item(seq, it)) break;
       const int n = it.n_tiles;
       mbar_wait(JT_BAR(kBarQFull), q_count & 1, abort);
       ++q_count;
@@ -676,30 +723,31 @@ __global__ void __launch_bounds__(kThreads, 1)
     mbar_wait(JT_BAR(kBarDrain), 0, abort, false);
   } else if (warp < 4) {
     // ------------------------------------------------------------------ loaders
-    const int ltid = tid - 32;
+    // Warp 1 publishes the work items, issues every TMA load (query tiles, prefix K/V
+    // tiles) and is the only waiter on the ring's empty barriers: it waits for every ring
+    // position in order (so it is never a phase behind or ahead on any slot) and then
+    // publishes the position as free in `ring_free`.  Warps 2-3 gather the tiles that touch
+    // tree nodes with cp.async, each once `ring_free` has reached its position, so a gather
+    // waiting for its rows never holds back the TMA loads behind it.  Both walk the same
+    // fill sequence: the MMA's consumption order, K 0..2, then V t and K t+3 per tile.
+    const bool tma_warp = warp == 1;
+    const int gtid = tid - 64;  // gather thread index (warps 2-3)
     uint32_t ring = 0, q_fills = 0;
     uint32_t filled = 0;       // bit s: the last fill of ring slot s was TMA
     uint32_t last_parity = 0;  // bit s: phase parity of that fill
     const int64_t pool_slots = p.num_blocks * static_cast<int64_t>(bs);
+    const uint32_t ring_free = base + kOffMisc + 8;  // misc[2]: last free ring position + 1
+    if (tma_warp && lane == 0) publish(0);
     for (uint32_t seq = 0;; ++seq) {
-      if (ltid == 0) {
-        // Publish the next work item (or -1 when the queue is exhausted).
-        const int slot = seq & 1;
-        if (seq >= 2) mbar_wait(JT_BAR(kBarItemEmpty + slot), ((seq >> 1) - 1) & 1, abort);
-        const int index = atomicAdd(&w.header[0], 1);
-        misc[4 + slot] = index < num_items ? index : -1;
-        mbar_arrive(JT_BAR(kBarItemFull + slot));
-      }
-      const int index = next_item(seq);
-      if (index < 0) break;
-      const Item it = decode(p, w, index, split_keys);
+      Item it;
+      if (!next_item(seq, it)) break;
       const int n = it.n_tiles;
       const int32_t* table = p.block_tables + static_cast<int64_t>(it.r) * p.table_stride0;
       // Query tile: one TMA box of 128/groups nodes x groups heads x 64 dims per half, once
       // the previous item's last QK has read the buffer.  Rows past the request's nodes
       // hold other requests' queries (or zeros past the end); their score rows are never
       // written out.
-      if (ltid == 0) {
+      if (tma_warp && lane == 0) {
         if (seq > 0) mbar_wait(JT_BAR(kBarQEmpty), (seq - 1) & 1, abort);
         mbar_arrive_tx(JT_BAR(kBarQFull), kQTileBytes);
         const int node = it.q_start + it.tp * (kM / G);
@@ -707,23 +755,39 @@ __global__ void __launch_bounds__(kThreads, 1)
         tma_load_3d(base + kOffQ + kQHalfBytes, &qmap, 64, it.h * G, node, JT_BAR(kBarQFull));
         ++q_fills;
       }
-      // Fill order = the MMA's consumption order (K 0..2, then V t and K t+3 per tile).
       auto fill = [&](bool is_v, int t) {
         const int kb = it.key_begin + t * kN;
+        // A prefix tile inside one page (tiles never straddle pages: block_size is a
+        // multiple of 128 and every key range starts on a tile boundary) goes by TMA.
         const bool full = kb + kN <= min(it.P, it.key_end);
-        const int page = (full && ltid == 0) ? __ldg(table + kb / bs) : 0;
         const int slot = ring % kRing;
         const uint32_t parity = (ring / kRing) & 1;
-        // Every loader thread waits for every refill, in order.
-        if (ring >= kRing) mbar_wait(JT_BAR(kBarEmpty + slot), parity ^ 1, abort);
-        if (is_v)
-          load_kv_tile(p, it, table, kb, full, ltid, lane, base + kOffRing + slot * kKVBytes,
-                       &vmap, static_cast<const char*>(p.v_pool), p.v_stride0, p.v_stride1,
-                       p.v_stride2, JT_BAR(kBarFull + slot), pool_slots, page);
-        else
-          load_kv_tile(p, it, table, kb, full, ltid, lane, base + kOffRing + slot * kKVBytes,
-                       &kmap, static_cast<const char*>(p.k_pool), p.k_stride0, p.k_stride1,
-                       p.k_stride2, JT_BAR(kBarFull + slot), pool_slots, page);
+        const uint32_t dst = base + kOffRing + slot * kKVBytes;
+        const uint32_t full_bar = JT_BAR(kBarFull + slot);
+        if (tma_warp) {
+          if (lane == 0) {
+            if (ring >= kRing) mbar_wait(JT_BAR(kBarEmpty + slot), parity ^ 1, abort);
+            if (full) {
+              const int page = __ldg(table + kb / bs);
+              const CUtensorMap* map = is_v ? &vmap : &kmap;
+              mbar_arrive_tx(full_bar, kKVBytes);
+              tma_load_4d(dst, map, 0, it.h, kb % bs, page, full_bar);
+              tma_load_4d(dst + kKVHalfBytes, map, 64, it.h, kb % bs, page, full_bar);
+              mbar_arrive(full_bar);
+            } else {
+              st_release_shared(ring_free, ring + 1);
+            }
+          }
+        } else if (!full) {
+          wait_shared_at_least(ring_free, ring + 1, abort);
+          const char* pool = static_cast<const char*>(is_v ? p.v_pool : p.k_pool);
+          const int64_t s0 = is_v ? p.v_stride0 : p.k_stride0;
+          const int64_t s1 = is_v ? p.v_stride1 : p.k_stride1;
+          const int64_t s2 = is_v ? p.v_stride2 : p.k_stride2;
+          gather_kv_tile(p, it, table, kb, gtid, dst, pool, s0, s1, s2, pool_slots);
+          __syncwarp();
+          if (lane == 0) mbar_arrive(full_bar);
+        }
         const uint32_t bit = 1u << slot;
         if (full) { filled |= bit; last_parity = (last_parity & ~bit) | (parity ? bit : 0u); }
         else filled &= ~bit;
@@ -731,12 +795,16 @@ __global__ void __launch_bounds__(kThreads, 1)
       };
       for (int t = 0; t < min(kAhead, n); ++t) fill(false, t);
       for (int t = 0; t < n; ++t) {
+        // The next item is claimed and published while this one still has about four
+        // tiles to go: early enough for its query tile and first K tiles to be loaded
+        // before the MMA reaches them, late enough not to hold work another CTA could take.
+        if (tma_warp && lane == 0 && t == max(0, n - 4)) publish(seq + 1);
         fill(true, t);
         if (t + kAhead < n) fill(false, t + kAhead);
       }
     }
-    // Drain: the TMA copies this thread issued have landed before the CTA exits.
-    if (ltid == 0) {
+    // Drain: the TMA copies this warp issued have landed before the CTA exits.
+    if (tma_warp && lane == 0) {
       for (int s = 0; s < kRing; ++s)
         if (filled & (1u << s))
           mbar_wait(JT_BAR(kBarFull + s), (last_parity >> s) & 1u, abort, false);
@@ -754,9 +822,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     const float scale_log2 = p.scale * 1.4426950408889634f;
     uint32_t g0 = 0, pv_seen = 0, mx_par = 0, lx_par = 0;
     for (uint32_t seq = 0;; ++seq) {
-      const int index = next_item(seq);
-      if (index < 0) break;
-      const Item it = decode(p, w, index, split_keys);
+      Item it;
+      if (!next_item(seq, it)) break;
       const int n = it.n_tiles;
       const int gm = it.tp * kM + t128;
       const int j = gm / G, g = gm - j * G;
