@@ -28,7 +28,10 @@
 // consumption order.
 //
 // Every mbarrier wait is bounded and every waiter consumes every phase of the barriers it
-// waits on, in order (parity waits are unambiguous only within one phase).  A wait that
+// waits on, in order (parity waits are unambiguous only within one phase), except the
+// softmax's waits on the per-buffer PV barriers, which it takes only before a rescale and
+// at the epilogue; the argument that each of those waits is exactly one phase behind sits
+// beside it.  A wait that
 // runs out sets JT_DEVERR_TIMEOUT and an abort flag; all roles then leave their loops,
 // drain their own asynchronous copies and MMAs, and the CTA frees its TMEM and exits.
 
@@ -73,15 +76,15 @@ constexpr int kBarQFull = 10;                  // loader thread 0 (+ TMA bytes)
 constexpr int kBarQEmpty = 11;                 // MMA commit after an item's last QK
 constexpr int kBarSFull = 12;                  // [kSBufs] MMA commit per QK
 constexpr int kBarPFull = 15;                  // [kSBufs] 8 softmax warps
-constexpr int kBarPvDone = 18;                 // MMA commit per PV
-constexpr int kBarOFree = 19;                  // 8 softmax warps after the epilogue
-constexpr int kBarMx = 20;                     // 8 softmax warps: half maxima swapped
-constexpr int kBarLx = 21;                     // 8 softmax warps: half row sums swapped
+constexpr int kBarPvDone = 18;                 // [kSBufs] MMA commit per PV (by P's S buffer)
+constexpr int kBarOFree = 21;                  // 8 softmax warps after the epilogue
+constexpr int kBarMx = 22;                     // 8 softmax warps: half maxima swapped
+constexpr int kBarLx = 23;                     // 8 softmax warps: half row sums swapped
 constexpr int kSoftmaxWarps = 8;
-constexpr int kBarDrain = 22;
-constexpr int kBarItemFull = 23;               // [2] work-item ring
-constexpr int kBarItemEmpty = 25;              // [2]
-constexpr int kNumBars = 27;
+constexpr int kBarDrain = 24;
+constexpr int kBarItemFull = 25;               // [2] work-item ring
+constexpr int kBarItemEmpty = 27;              // [2]
+constexpr int kNumBars = 29;
 constexpr int kItemConsumers = 12;             // every warp of the CTA reads each item
 constexpr int kGatherThreads = 64;             // warps 2-3: cp.async tree tiles
 constexpr int kFullArrivals = 2;               // per ring fill: TMA (arrive_tx + arrive) or
@@ -131,9 +134,9 @@ __device__ __forceinline__ void warp_arrive(uint32_t bar) {
   __syncwarp();
   if ((threadIdx.x & 31) == 0) mbar_arrive(bar);
 }
-// Warp-wide wait: lane 0 waits for the phase, the other lanes synchronise behind it.
+// Warp-wide wait: every lane polls the phase itself (no divergent branch to reconverge).
 __device__ __forceinline__ void warp_wait(uint32_t bar, uint32_t parity, volatile int* abort) {
-  if ((threadIdx.x & 31) == 0) mbar_wait(bar, parity, abort);
+  mbar_wait(bar, parity, abort);
   __syncwarp();
 }
 
@@ -599,8 +602,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   // Work items: lane 0 of the TMA warp takes the next one from the device queue, decodes
   // it and publishes the decoded item through a two-entry ring in shared memory, one item
   // ahead of its own loads, so no role waits on the decode's global-memory chain at an
-  // item boundary.  Lane 0 of every warp reads each entry and broadcasts it (a warp always
-  // agrees with itself); the end of the queue, or an abort, reads as no item.
+  // item boundary.  Every lane reads each entry; the warp takes it as an item only when
+  // every lane did, so the end of the queue, or an abort, reads as no item for all lanes.
   volatile int* item_ring = reinterpret_cast<volatile int*>(sbase + kOffItem);
   auto publish = [&](uint32_t seq) {
     const int slot = seq & 1;
@@ -625,17 +628,16 @@ __global__ void __launch_bounds__(kThreads, 1)
     int f[15];
 #pragma unroll
     for (int k = 0; k < 15; ++k) f[k] = 0;
-    if (lane == 0) {
-      if (mbar_wait(JT_BAR(kBarItemFull + slot), (seq >> 1) & 1, abort) && !*abort) {
-        volatile int* e = item_ring + 16 * slot;
-        f[14] = e[15];
+    // Every lane waits for the entry and reads it; lane 0 releases it once all have.
+    if (mbar_wait(JT_BAR(kBarItemFull + slot), (seq >> 1) & 1, abort) && !*abort) {
+      volatile int* e = item_ring + 16 * slot;
+      f[14] = e[15];
 #pragma unroll
-        for (int k = 0; k < 14; ++k) f[k] = e[k];
-      }
-      mbar_arrive(JT_BAR(kBarItemEmpty + slot));
+      for (int k = 0; k < 14; ++k) f[k] = e[k];
     }
-#pragma unroll
-    for (int k = 0; k < 15; ++k) f[k] = __shfl_sync(0xffffffffu, f[k], 0);
+    // One verdict per warp: an item only when every lane read it.
+    f[14] = __all_sync(0xffffffffu, f[14] != 0) ? 1 : 0;
+    if (lane == 0) mbar_arrive(JT_BAR(kBarItemEmpty + slot));
     it.r = f[0]; it.split = f[1]; it.h = f[2]; it.tp = f[3]; it.n_split = f[4];
     it.mblocks = f[5]; it.slot_base = f[6]; it.counter_base = f[7]; it.P = f[8]; it.T = f[9];
     it.q_start = f[10]; it.key_begin = f[11]; it.key_end = f[12]; it.n_tiles = f[13];
@@ -711,7 +713,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           if constexpr (FP32P)
             mma_ts_warp(tmem + col_o(), pa + col_p(kk) + 32, vd + kk * (2048 / 16), kIdescPV, 1u);
         }
-        tc_commit_warp(JT_BAR(kBarPvDone));
+        tc_commit_warp(JT_BAR(kBarPvDone + b));
         release(slot);
         if (t + kAhead < n) issue_qk(t + kAhead);
       }
@@ -820,7 +822,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     // tile ahead never overwrites a value the other warpgroup has yet to read.
     float* xm = reinterpret_cast<float*>(sbase + kOffXm);
     const float scale_log2 = p.scale * 1.4426950408889634f;
-    uint32_t g0 = 0, pv_seen = 0, mx_par = 0, lx_par = 0;
+    uint32_t g0 = 0, mx_par = 0, lx_par = 0;
     for (uint32_t seq = 0;; ++seq) {
       Item it;
       if (!next_item(seq, it)) break;
@@ -861,21 +863,23 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         mx_par ^= 1u;
         l_run = l_run * alpha + rsum;
-        if (t > 0) {
-          // PV t-1 has completed: O is stable and may be rescaled in place.
-          warp_wait(JT_BAR(kBarPvDone), pv_seen & 1u, abort);
-          ++pv_seen;
+        if (t > 0 && __any_sync(0xffffffffu, alpha != 1.f)) {
+          // Rescale this warp's O rows once PV t-1 has completed.  A warp that needs no
+          // rescale publishes P t at once, so PV t never waits for PV t-1 in the common
+          // case.  The wait is for exactly one phase of PvDone[(gt-1) % 3]: its previous
+          // phase (PV gt-4) completed before QK gt, whose S this warp has read, and its next
+          // one (PV gt+2) needs this warp's P gt+2.
+          const int gp = gt - 1;
+          warp_wait(JT_BAR(kBarPvDone + gp % kSBufs), (gp / kSBufs) & 1, abort);
           tc_fence_after();
-          if (__any_sync(0xffffffffu, alpha != 1.f)) {
 #pragma unroll 1
-            for (int chunk = 0; chunk < 2; ++chunk) {
-              uint32_t o[32];
-              tmem_ld32(o_addr + 64 * c + chunk * 32, o);
-              tmem_wait_ld();
+          for (int chunk = 0; chunk < 2; ++chunk) {
+            uint32_t o[32];
+            tmem_ld32(o_addr + 64 * c + chunk * 32, o);
+            tmem_wait_ld();
 #pragma unroll
-              for (int k = 0; k < 32; ++k) o[k] = __float_as_uint(__uint_as_float(o[k]) * alpha);
-              tmem_st32(o_addr + 64 * c + chunk * 32, o);
-            }
+            for (int k = 0; k < 32; ++k) o[k] = __float_as_uint(__uint_as_float(o[k]) * alpha);
+            tmem_st32(o_addr + 64 * c + chunk * 32, o);
           }
         }
         tmem_wait_st();
@@ -884,8 +888,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       // Epilogue: wait for the item's last PV, swap the half row sums, then each
       // warpgroup writes its 64 output columns.
-      warp_wait(JT_BAR(kBarPvDone), pv_seen & 1u, abort);
-      ++pv_seen;
+      {
+        const int gl = g0 + n - 1;  // same one-phase argument as the rescale wait
+        warp_wait(JT_BAR(kBarPvDone + gl % kSBufs), (gl / kSBufs) & 1, abort);
+      }
       xl[c * kM + t128] = l_run;
       warp_arrive(JT_BAR(kBarLx));
       warp_wait(JT_BAR(kBarLx), lx_par, abort);
