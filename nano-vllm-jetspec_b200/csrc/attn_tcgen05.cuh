@@ -595,6 +595,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   tc_fence_after();
   const uint32_t tmem = static_cast<uint32_t>(misc[0]);
 
+  // Launched as a programmatic dependent of the plan kernel: everything above overlapped
+  // the plan; from here on the plan's output (and, through it, every earlier launch on the
+  // stream) is complete and visible.
+  asm volatile("griddepcontrol.wait;\n" ::: "memory");
   const int num_items = w.header[1];
   const int split_keys = w.header[2];
   const int G = p.groups, bs = p.block_size;
@@ -939,17 +943,18 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc_fence_before();
       warp_arrive(JT_BAR(kBarOFree));
       if (split_item) {
-        // Per-row merge: each half publishes its columns (warpgroup 0 also the row's max
-        // in log2 units and sum), then bumps the row's counter; the arrival that
-        // completes a row (both halves of every split) merges the whole row.  Rows never
-        // wait for one another.
-        if (c == 0) w.part_ml[slot * kM + t128] = make_float2(m_run, l_fin);
+        // Per-(row, half) merge: each half publishes its 64 columns and its own copy of the
+        // row's max (log2 units) and sum, then bumps the (row, half) counter; the arrival
+        // that completes it (this half of every split) merges those 64 columns.  Nothing
+        // waits: rows and halves finish independently.  The merge issues each split's
+        // loads together (one load round per split, not one per 4 columns).
+        w.part_ml[(slot * 2 + c) * kM + t128] = make_float2(m_run, l_fin);
         __threadfence();
         int* counter = w.counters +
-                       (static_cast<int64_t>(it.counter_base) + it.h * it.mblocks + it.tp) * kM +
-                       t128;
+                       (static_cast<int64_t>(it.counter_base) + it.h * it.mblocks + it.tp) * 2 * kM +
+                       c * kM + t128;
         const int done = atomicAdd(counter, 1);
-        if (done == 2 * it.n_split - 1) {
+        if (done == it.n_split - 1) {
           *counter = 0;
           __threadfence();
           if (row_ok) {
@@ -957,34 +962,49 @@ __global__ void __launch_bounds__(kThreads, 1)
                 it.slot_base + (static_cast<int64_t>(it.h) * it.mblocks + it.tp) * it.n_split;
             float mmax = -INFINITY;
             for (int s2 = 0; s2 < it.n_split; ++s2)
-              mmax = fmaxf(mmax, __ldcg(w.part_ml + (slot0 + s2) * kM + t128).x);
+              mmax = fmaxf(mmax, __ldcg(w.part_ml + ((slot0 + s2) * 2 + c) * kM + t128).x);
             const float mref = mmax == -INFINITY ? 0.f : mmax;
-            float den = 0.f;
-            for (int s2 = 0; s2 < it.n_split; ++s2) {
-              const float2 ml = __ldcg(w.part_ml + (slot0 + s2) * kM + t128);
-              den += jt::fast_exp2(ml.x - mref) * ml.y;
-            }
-            const float dinv = 1.f / den;
             const int64_t off = static_cast<int64_t>(it.q_start + j) * p.out_stride0 +
-                                static_cast<int64_t>(it.h * G + g) * p.out_stride1;
-            for (int d = 0; d < kD; d += 4) {
-              float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+                                static_cast<int64_t>(it.h * G + g) * p.out_stride1 + 64 * c;
+#pragma unroll 1
+            for (int part = 0; part < 2; ++part) {
+              float acc[32];
+#pragma unroll
+              for (int k = 0; k < 32; ++k) acc[k] = 0.f;
+              float den = 0.f;
+#pragma unroll 1
               for (int s2 = 0; s2 < it.n_split; ++s2) {
-                const float wv =
-                    jt::fast_exp2(__ldcg(w.part_ml + (slot0 + s2) * kM + t128).x - mref);
-                const float4 o = __ldcg(reinterpret_cast<const float4*>(
-                    w.part_o + ((slot0 + s2) * kM + t128) * kD + d));
-                acc.x += wv * o.x;
-                acc.y += wv * o.y;
-                acc.z += wv * o.z;
-                acc.w += wv * o.w;
+                const float2 ml = __ldcg(w.part_ml + ((slot0 + s2) * 2 + c) * kM + t128);
+                const float4* src = reinterpret_cast<const float4*>(
+                    w.part_o + ((slot0 + s2) * kM + t128) * kD + 64 * c + 32 * part);
+                float4 v[8];
+#pragma unroll
+                for (int k = 0; k < 8; ++k) v[k] = __ldcg(src + k);
+                const float wv = jt::fast_exp2(ml.x - mref);
+                den += wv * ml.y;
+#pragma unroll
+                for (int k = 0; k < 8; ++k) {
+                  acc[4 * k] += wv * v[k].x;
+                  acc[4 * k + 1] += wv * v[k].y;
+                  acc[4 * k + 2] += wv * v[k].z;
+                  acc[4 * k + 3] += wv * v[k].w;
+                }
               }
+              const float dinv = 1.f / den;
               if (p.out_dtype == JT_F32) {
-                *reinterpret_cast<float4*>(static_cast<float*>(p.out) + off + d) =
-                    make_float4(acc.x * dinv, acc.y * dinv, acc.z * dinv, acc.w * dinv);
+                float4* dst = reinterpret_cast<float4*>(static_cast<float*>(p.out) + off + 32 * part);
+#pragma unroll
+                for (int k = 0; k < 8; ++k)
+                  dst[k] = make_float4(acc[4 * k] * dinv, acc[4 * k + 1] * dinv,
+                                       acc[4 * k + 2] * dinv, acc[4 * k + 3] * dinv);
               } else {
-                *reinterpret_cast<uint2*>(static_cast<Elem*>(p.out) + off + d) = make_uint2(
-                    Mma::pack(acc.x * dinv, acc.y * dinv), Mma::pack(acc.z * dinv, acc.w * dinv));
+                uint4* dst = reinterpret_cast<uint4*>(static_cast<Elem*>(p.out) + off + 32 * part);
+#pragma unroll
+                for (int k = 0; k < 4; ++k)
+                  dst[k] = make_uint4(Mma::pack(acc[8 * k] * dinv, acc[8 * k + 1] * dinv),
+                                      Mma::pack(acc[8 * k + 2] * dinv, acc[8 * k + 3] * dinv),
+                                      Mma::pack(acc[8 * k + 4] * dinv, acc[8 * k + 5] * dinv),
+                                      Mma::pack(acc[8 * k + 6] * dinv, acc[8 * k + 7] * dinv));
               }
             }
           }

@@ -38,12 +38,18 @@ constexpr int kMaxMaskWords = 32; // tree nodes per request <= 1024
 constexpr int kPlanThreads = 256;
 constexpr int kBuckets = 32;
 constexpr int kSplitCandidates = 16;  // split lengths 1024 << c
+constexpr int kSplitBase = 1024;
+// Planning costs in 128-key tile times, measured: the fixed cost of one work item (query
+// tile load, pipeline fill, epilogue) and the extra cost of a split plan (fp32 partials,
+// the release fence and counter of every split item, the merging loads).
+constexpr int kItemCostTiles = 2;
+constexpr int kMergeCostTiles = 16;
 constexpr int64_t kPartialBudgetBytes = 256ll << 20;
 
 // ---- workspace layout ---------------------------------------------------------------
 struct Layout {
   int bm;           // score rows per item (64 or 128)
-  int counter_stride;  // split counters per (request, kv head, m-block): 1, or one per row
+  int counter_stride;  // split counters per (request, kv head, m-block): 1, or 2 per row
   int mask_words;   // 32-bit words of ancestor bitmask per tree node
   int max_items;
   int max_slots;    // partial-result slots (split items)
@@ -77,16 +83,18 @@ Layout make_layout(int32_t R, int32_t Q, int32_t H, int32_t G, int32_t D,
   L.off_req = o;      o = align_up(o + sizeof(int4) * static_cast<size_t>(R), 256);
   L.off_items = o;    o = align_up(o + sizeof(int4) * static_cast<size_t>(L.max_items), 256);
   // Split counters: one per (request, kv head, m-block) for the portable core, one per
-  // score row for the tcgen05 core (whose rows finish independently).
-  const size_t counter_stride = row_counters ? static_cast<size_t>(L.bm) : 1;
+  // score row and output half for the tcgen05 core (whose rows and halves finish
+  // independently).
+  const size_t counter_stride = row_counters ? 2 * static_cast<size_t>(L.bm) : 1;
   L.counter_stride = static_cast<int>(counter_stride);
   L.off_counters = o;
   o = align_up(o + sizeof(int) * static_cast<size_t>(L.max_slots) * counter_stride, 256);
   L.off_masks = o;
   o = align_up(o + sizeof(uint32_t) * static_cast<size_t>(Q) * L.mask_words, 256);
   L.off_part_o = o;   o = align_up(o + static_cast<size_t>(per_slot) * L.max_slots, 256);
-  L.off_part_ml = o;
-  o = align_up(o + sizeof(float2) * static_cast<size_t>(L.bm) * L.max_slots, 256);
+  L.off_part_ml = o;  // (max, sum) per row; per row and output half for the tcgen05 core
+  o = align_up(o + sizeof(float2) * static_cast<size_t>(L.bm) * L.max_slots * (row_counters ? 2 : 1),
+               256);
   L.total = o;
   return L;
 }
@@ -100,7 +108,7 @@ struct DevLayout {
   float* part_o;
   float2* part_ml;
   int bm, mask_words, max_items, max_slots;
-  int counter_stride;  // split counters per (request, kv head, m-block): 1, or one per row
+  int counter_stride;  // split counters per (request, kv head, m-block): 1, or 2 per row
 };
 
 DevLayout device_layout(const Layout& L, void* ws) {
@@ -122,17 +130,6 @@ DevLayout device_layout(const Layout& L, void* ws) {
 }
 
 // ---- plan kernel --------------------------------------------------------------------
-__device__ __forceinline__ int64_t block_sum_i64(int64_t v, int64_t* scratch) {
-  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  __syncthreads();
-  if (lane == 0) scratch[warp] = v;
-  __syncthreads();
-  int64_t total = 0;
-  for (int w = 0; w < kPlanThreads / 32; ++w) total += scratch[w];
-  return total;
-}
-
 __device__ __forceinline__ int request_mblocks(int nodes, int groups, int bm) {
   return static_cast<int>((static_cast<int64_t>(nodes) * groups + bm - 1) / bm);
 }
@@ -143,6 +140,10 @@ __device__ __forceinline__ int request_splits(int prefix, int split_keys) {
 
 __global__ void __launch_bounds__(kPlanThreads)
     tree_plan_kernel(JtTreeAttnParams p, DevLayout w, int num_ctas) {
+  // The tcgen05 attention kernel is launched as a programmatic dependent: it may start its
+  // prologue now and waits (griddepcontrol.wait) for this grid's completion before it reads
+  // the plan.
+  asm volatile("griddepcontrol.launch_dependents;\n" ::: "memory");
   const int tid = threadIdx.x;
   if (blockIdx.x > 0) {
     // Ancestor bitmask of one packed tree node per warp.
@@ -166,8 +167,9 @@ __global__ void __launch_bounds__(kPlanThreads)
     return;
   }
 
-  __shared__ int64_t red[kPlanThreads / 32];
-  __shared__ int64_t cand_slots[kSplitCandidates];
+  __shared__ int cand_red[kPlanThreads / 32][3][kSplitCandidates];
+  __shared__ int64_t cand_est[kSplitCandidates];
+  __shared__ int cand_ok[kSplitCandidates];
   __shared__ int bucket_count[kBuckets];
   __shared__ int bucket_start[kBuckets];
   __shared__ int s_split;
@@ -176,47 +178,81 @@ __global__ void __launch_bounds__(kPlanThreads)
 
   const int R = p.num_requests, G = p.groups, H = p.num_kv_heads, bm = w.bm;
   const int cap = w.mask_words * 32;
+  const int warp = tid >> 5, lane = tid & 31;
 
-  // Total work in key x m-block units and, per candidate split length, the partial
-  // slots it would need.
-  int64_t work = 0;
-  int64_t cand[kSplitCandidates];
-#pragma unroll
-  for (int c = 0; c < kSplitCandidates; ++c) cand[c] = 0;
-  for (int r = tid; r < R; r += kPlanThreads) {
-    const int nodes = p.node_counts[r];
-    const int prefix = p.prefix_lens[r];
-    if (nodes < 1 || nodes > cap || prefix < 0) continue;
-    const int mb = request_mblocks(nodes, G, bm);
-    work += static_cast<int64_t>(prefix + nodes) * mb * H;
-#pragma unroll
-    for (int c = 0; c < kSplitCandidates; ++c) {
-      const int s = request_splits(prefix, 1024 << c);
-      if (s > 1) cand[c] += static_cast<int64_t>(s) * mb * H;
+  // Per candidate split length S = 1024 << c: the partial slots it needs, the total work
+  // in tile times (tiles of every item plus a fixed cost per item) and the longest item.
+  // Candidates are visited one at a time (few registers); each thread's first request is
+  // kept in registers across them.
+  const int r0 = tid;
+  const int nodes0 = r0 < R ? p.node_counts[r0] : 0;
+  const int prefix0 = r0 < R ? p.prefix_lens[r0] : 0;
+#pragma unroll 1
+  for (int c = 0; c < kSplitCandidates; ++c) {
+    const int len = kSplitBase << c;
+    // Reduced in 32 bits: each thread's terms are clamped to 2^24, so a warp's sum stays
+    // below 2^29 and a clamped slot count still exceeds any partial budget.
+    unsigned c_slots = 0, c_work = 0, c_long = 0;
+    for (int r = tid; r < R; r += kPlanThreads) {
+      const int nodes = r == r0 ? nodes0 : p.node_counts[r];
+      const int prefix = r == r0 ? prefix0 : p.prefix_lens[r];
+      if (nodes < 1 || nodes > cap || prefix < 0) continue;
+      const int mb = request_mblocks(nodes, G, bm);
+      const int ns = request_splits(prefix, len);
+      const int last_keys = prefix + nodes - (ns - 1) * len;
+      const int tiles = (ns - 1) * (len / 128) + (last_keys + 127) / 128;
+      const int64_t work = static_cast<int64_t>(mb) * H * (tiles + ns * kItemCostTiles);
+      c_work = static_cast<unsigned>(min(static_cast<int64_t>(c_work) + work, static_cast<int64_t>(1) << 24));
+      c_long = max(c_long, static_cast<unsigned>(max(ns > 1 ? len / 128 : 0, (last_keys + 127) / 128)));
+      if (ns > 1)
+        c_slots = static_cast<unsigned>(
+            min(static_cast<int64_t>(c_slots) + static_cast<int64_t>(ns) * mb * H,
+                static_cast<int64_t>(1) << 24));
+    }
+    c_slots = __reduce_add_sync(0xffffffffu, min(c_slots, 1u << 24));
+    c_work = min(c_work, 1u << 24);
+    c_work = __reduce_add_sync(0xffffffffu, c_work);
+    c_long = __reduce_max_sync(0xffffffffu, c_long);
+    if (lane == 0) {
+      cand_red[warp][0][c] = static_cast<int>(c_slots);
+      cand_red[warp][1][c] = static_cast<int>(c_work);
+      cand_red[warp][2][c] = static_cast<int>(c_long);
     }
   }
-  work = block_sum_i64(work, red);
-  for (int c = 0; c < kSplitCandidates; ++c) {
-    const int64_t v = block_sum_i64(cand[c], red);
-    if (tid == 0) cand_slots[c] = v;
-  }
   if (tid < kBuckets) bucket_count[tid] = 0;
+  __syncthreads();
+  if (tid < kSplitCandidates) {
+    // Candidate `tid`: partial slots, and the estimated makespan in tile times (longest-
+    // first list scheduling finishes within max(average load, longest item)) plus the
+    // fixed cost of a split plan.
+    int64_t sl = 0, wk = 0, lg = 0;
+#pragma unroll
+    for (int k = 0; k < kPlanThreads / 32; ++k) {
+      sl += cand_red[k][0][tid];
+      wk += cand_red[k][1][tid];
+      lg = max(lg, static_cast<int64_t>(cand_red[k][2][tid]));
+    }
+    cand_ok[tid] = sl <= w.max_slots;
+    cand_est[tid] = max((wk + num_ctas - 1) / num_ctas, lg + kItemCostTiles) +
+                    (sl > 0 ? kMergeCostTiles : 0);
+  }
+  __syncthreads();
   if (tid == 0) {
-    int split;
-    if (p.split_keys > 0) {
-      split = p.split_keys;
-      int c = 0;
-      while (c < kSplitCandidates && (1024 << c) < split) ++c;
-      // An explicit split that would overflow the partial budget is coarsened.
-      while (c < kSplitCandidates && cand_slots[c] > w.max_slots) { ++c; split = 1024 << c; }
-    } else {
-      // Aim for ~2 items per resident CTA; never below 1024 keys per split.
-      const int64_t target = work / (2ll * num_ctas);
-      int c = 0;
-      while (c < kSplitCandidates - 1 &&
-             ((1024ll << c) < target || cand_slots[c] > w.max_slots))
-        ++c;
-      split = 1024 << c;
+    // Explicit split (1024 times a power of two): the first candidate at least that long
+    // whose partials fit the budget.  Automatic: the smallest estimate within the budget;
+    // ties go to the longer split.  The last candidate (longer than any prefix: no split)
+    // always fits.  Shorter splits need more partials, so the scan stops at the first
+    // candidate over budget.
+    int split = kSplitBase << (kSplitCandidates - 1);
+    int64_t best_est = -1;
+    for (int c = kSplitCandidates - 1; c >= 0 && cand_ok[c]; --c) {
+      const int len = kSplitBase << c;
+      if (p.split_keys > 0) {
+        if (len >= p.split_keys) split = len;
+      } else if (best_est < 0 || cand_est[c] < best_est) {
+        best_est = cand_est[c];
+        split = len;
+      }
     }
     s_split = split;
     s_carry[0] = s_carry[1] = 0;
@@ -225,7 +261,6 @@ __global__ void __launch_bounds__(kPlanThreads)
   const int split = s_split;
 
   // Per-request split count plus exclusive scans of partial slots and counters.
-  const int warp = tid >> 5, lane = tid & 31;
   for (int base = 0; base < R; base += kPlanThreads) {
     const int r = base + tid;
     int n_split = 1, mb = 0, slots = 0, counters = 0;
@@ -815,9 +850,20 @@ int launch_tc(const JtTreeAttnParams& p, const Layout& L, const DevLayout& d,
   tree_plan_kernel<<<plan_blocks, kPlanThreads, 0, stream>>>(p, d, sms);
   rc = jt_cuda_check(cudaGetLastError(), "plan launch");
   if (rc != JT_OK) return rc;
-  const int grid = std::min(sms, L.max_items);
-  kernel<<<grid, tc::kThreads, tc::kSmemBytes, stream>>>(p, d, qmap, kmap, vmap);
-  return jt_cuda_check(cudaGetLastError(), "tcgen05 attention launch");
+  // Programmatic dependent launch: the attention grid's prologue (barrier setup, TMEM
+  // allocation) overlaps the plan kernel; the kernel waits for the plan before using it.
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = dim3(std::min(sms, L.max_items));
+  cfg.blockDim = dim3(tc::kThreads);
+  cfg.dynamicSmemBytes = tc::kSmemBytes;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return jt_cuda_check(cudaLaunchKernelEx(&cfg, kernel, p, d, qmap, kmap, vmap),
+                       "tcgen05 attention launch");
 }
 
 int dispatch_tc(const JtTreeAttnParams& p, const Layout& L, const DevLayout& d,
