@@ -55,7 +55,11 @@ constexpr int kOffMisc = kOffBar + 8 * 32;
 constexpr int kOffXl = kOffMisc + 64;                   // [2 halves][128] row sums
 constexpr int kOffXm = kOffXl + 2 * kM * 4;             // [tile parity][2 halves][128] maxima
 constexpr int kOffItem = kOffXm + 4 * kM * 4;           // [2] decoded work items (16 ints)
-constexpr int kSmemBytes = kOffItem + 2 * 64 + 1024;    // + alignment slack
+constexpr int kMaskWordsMax = 32;                       // tree nodes per request <= 1024
+constexpr int kOffMask = kOffItem + 2 * 64;             // single-launch mode: the item's
+                                                        // ancestor bitmasks [128][32] words
+constexpr int kSmemBytes = kOffMask + kM * kMaskWordsMax * 4 + 1024;  // + alignment slack
+static_assert(kSmemBytes <= 227 * 1024, "shared memory per CTA");
 constexpr long long kWaitLimit = 4000000000ll;          // cycles (~2 s) per wait
 
 // TMEM column map (512 columns x 128 lanes x 32 bit): O, then the S buffers.
@@ -327,8 +331,8 @@ __device__ __forceinline__ uint32_t visible_bits(int p0, int P, int key_end, int
     const int lo = max(0, -n0);  // first bit that is a tree node
     const int nb = n0 + lo;      // its node index
     const int widx = nb >> 5, sh = nb & 31;
-    uint32_t word = __ldg(mask_row + widx) >> sh;
-    if (sh != 0 && (widx + 1) * 32 < T) word |= __ldg(mask_row + widx + 1) << (32 - sh);
+    uint32_t word = mask_row[widx] >> sh;
+    if (sh != 0 && (widx + 1) * 32 < T) word |= mask_row[widx + 1] << (32 - sh);
     word <<= lo;
     bits |= word & (end >= 32 ? 0xffffffffu : ((1u << end) - 1u));
   }
@@ -365,6 +369,43 @@ __device__ __forceinline__ Item decode(const JtTreeAttnParams& p, const DevLayou
   }
   it.n_tiles = (it.key_end - it.key_begin + kN - 1) / kN;
   return it;
+}
+
+// Single-launch mode (no plan kernel, one item per CTA, no split): item `index` in the
+// plan's order for a split-free plan (requests in order, then KV head, then query tile).
+// Returns false past the last item; a request whose tree exceeds the mask capacity is
+// skipped and flagged, as the plan kernel does.
+__device__ __forceinline__ bool static_item(const JtTreeAttnParams& p, int index, int cap,
+                                            Item& it) {
+  for (int r = 0; r < p.num_requests; ++r) {
+    const int nodes = p.node_counts[r];
+    const int prefix = p.prefix_lens[r];
+    if (nodes < 1 || prefix < 0) continue;
+    if (nodes > cap) {
+      if (threadIdx.x == 0) atomicOr(&g_attn_errors, JT_DEVERR_TREE_TOO_LARGE);
+      continue;
+    }
+    const int mb = (nodes * p.groups + kM - 1) / kM;
+    if (index < mb * p.num_kv_heads) {
+      it.r = r;
+      it.split = 0;
+      it.h = index / mb;
+      it.tp = index - it.h * mb;
+      it.n_split = 1;
+      it.mblocks = mb;
+      it.slot_base = 0;
+      it.counter_base = 0;
+      it.P = prefix;
+      it.T = nodes;
+      it.q_start = p.cu_seqlens_q[r];
+      it.key_begin = 0;
+      it.key_end = prefix + min(nodes, (it.tp * kM + kM - 1) / p.groups + 1);
+      it.n_tiles = (it.key_end + kN - 1) / kN;
+      return true;
+    }
+    index -= mb * p.num_kv_heads;
+  }
+  return false;
 }
 
 // Gathers one 128-key K or V tile that touches tree nodes (scattered scratch slots) into
@@ -553,7 +594,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     tree_attn_tc_kernel(const JtTreeAttnParams p, const DevLayout w,
                         const __grid_constant__ CUtensorMap qmap,
                         const __grid_constant__ CUtensorMap kmap,
-                        const __grid_constant__ CUtensorMap vmap) {
+                        const __grid_constant__ CUtensorMap vmap, const int single_launch) {
   using Mma = jt::MmaOp<Elem>;
   constexpr bool kBf16 = std::is_same<Elem, __nv_bfloat16>::value;
   constexpr uint32_t kIdescQK = instr_desc(kM, kN, kBf16, false);
@@ -599,9 +640,31 @@ __global__ void __launch_bounds__(kThreads, 1)
   // the plan; from here on the plan's output (and, through it, every earlier launch on the
   // stream) is complete and visible.
   asm volatile("griddepcontrol.wait;\n" ::: "memory");
-  const int num_items = w.header[1];
-  const int split_keys = w.header[2];
   const int G = p.groups, bs = p.block_size;
+  // Single-launch mode (small batches, chosen on the host from the launch shape): no plan
+  // kernel ran; this CTA's only item comes from static_item, and the ancestor bitmasks of
+  // its tree rows are built here into shared memory (the plan's mask blocks, for one item).
+  const bool single = single_launch != 0;
+  Item s_it{};
+  const bool s_has = single && static_item(p, blockIdx.x, w.mask_words * 32, s_it);
+  const uint32_t* smask = reinterpret_cast<const uint32_t*>(sbase + kOffMask);
+  if (s_has) {
+    uint32_t* masks = reinterpret_cast<uint32_t*>(sbase + kOffMask);
+    const int rows = kM / G, j0 = s_it.tp * rows;
+    const int words = (s_it.T + 31) / 32;
+    const float* bias = p.qq_bias + p.qq_bias_offsets[s_it.r];
+    for (int task = warp; task < rows * words; task += kThreads / 32) {
+      const int jj = task / words, wd = task - jj * words;
+      const int jrow = j0 + jj, n = wd * 32 + lane;
+      const bool visible = jrow < s_it.T && n < s_it.T && n <= jrow &&
+                           bias[static_cast<int64_t>(jrow) * s_it.T + n] == 0.0f;
+      const uint32_t bits = __ballot_sync(0xffffffffu, visible);
+      if (lane == 0) masks[jj * kMaskWordsMax + wd] = bits;
+    }
+    __syncthreads();
+  }
+  const int num_items = single ? 0 : w.header[1];
+  const int split_keys = single ? 0 : w.header[2];
 
   // Work items: lane 0 of the TMA warp takes the next one from the device queue, decodes
   // it and publishes the decoded item through a two-entry ring in shared memory, one item
@@ -613,9 +676,11 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int slot = seq & 1;
     if (seq >= 2) mbar_wait(JT_BAR(kBarItemEmpty + slot), ((seq >> 1) - 1) & 1, abort);
     volatile int* e = item_ring + 16 * slot;
-    const int index = *abort ? num_items : atomicAdd(&w.header[0], 1);
-    if (index < num_items) {
-      const Item it = decode(p, w, index, split_keys);
+    int index = num_items;
+    if (single) index = (seq == 0 && s_has && !*abort) ? 0 : 1;
+    else if (!*abort) index = atomicAdd(&w.header[0], 1);
+    if (single ? index == 0 : index < num_items) {
+      const Item it = single ? s_it : decode(p, w, index, split_keys);
       const int f[14] = {it.r, it.split, it.h, it.tp, it.n_split, it.mblocks, it.slot_base,
                          it.counter_base, it.P, it.T, it.q_start, it.key_begin, it.key_end,
                          it.n_tiles};
@@ -836,7 +901,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       const bool row_ok = j < it.T;
       const bool warp_live = __any_sync(0xffffffffu, row_ok);
       const uint32_t* mask_row =
-          w.masks + static_cast<int64_t>(it.q_start + (row_ok ? j : 0)) * w.mask_words;
+          single ? smask + (row_ok ? j - it.tp * (kM / G) : 0) * kMaskWordsMax
+                 : w.masks + static_cast<int64_t>(it.q_start + (row_ok ? j : 0)) * w.mask_words;
       float m_run = -INFINITY;  // running max in log2 units (scaled scores)
       float l_run = 0.f;        // this half's partial row sum
       const uint32_t o_addr = tmem + lane_base + col_o();

@@ -44,6 +44,9 @@ constexpr int kSplitBase = 1024;
 // the release fence and counter of every split item, the merging loads).
 constexpr int kItemCostTiles = 2;
 constexpr int kMergeCostTiles = 16;
+// Longest prefix (block-table capacity) for which a one-item-per-CTA launch without a plan
+// beats a split plan (the plan's estimate gives splits no gain below about 32 tiles).
+constexpr int64_t kSingleLaunchMaxKeys = 4096;
 constexpr int64_t kPartialBudgetBytes = 256ll << 20;
 
 // ---- workspace layout ---------------------------------------------------------------
@@ -846,6 +849,21 @@ int launch_tc(const JtTreeAttnParams& p, const Layout& L, const DevLayout& d,
   int sms = 0;
   rc = device_sms(&sms);
   if (rc != JT_OK) return rc;
+  // Small batches run as one launch: when even the largest possible number of work items
+  // (every request's query tiles of every KV head) fits one wave of CTAs and the block
+  // table cannot address more than kSingleLaunchMaxKeys keys (beyond that a split plan can
+  // win), each CTA takes one item and builds its own ancestor bitmasks; the plan kernel
+  // and its launch latency go away.  Both bounds come from the launch shape alone, so the
+  // choice is the same on every replay of a captured graph.
+  const int64_t item_bound =
+      (static_cast<int64_t>(p.total_queries) * p.groups / tc::kM + p.num_requests) *
+      p.num_kv_heads;
+  const int64_t key_bound = static_cast<int64_t>(p.table_width) * p.block_size;
+  if (item_bound <= sms && key_bound <= kSingleLaunchMaxKeys && p.split_keys == 0) {
+    kernel<<<static_cast<int>(item_bound), tc::kThreads, tc::kSmemBytes, stream>>>(
+        p, d, qmap, kmap, vmap, 1);
+    return jt_cuda_check(cudaGetLastError(), "tcgen05 attention launch");
+  }
   const int plan_blocks = 1 + (p.total_queries + kPlanThreads / 32 - 1) / (kPlanThreads / 32);
   tree_plan_kernel<<<plan_blocks, kPlanThreads, 0, stream>>>(p, d, sms);
   rc = jt_cuda_check(cudaGetLastError(), "plan launch");
@@ -862,7 +880,7 @@ int launch_tc(const JtTreeAttnParams& p, const Layout& L, const DevLayout& d,
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  return jt_cuda_check(cudaLaunchKernelEx(&cfg, kernel, p, d, qmap, kmap, vmap),
+  return jt_cuda_check(cudaLaunchKernelEx(&cfg, kernel, p, d, qmap, kmap, vmap, 0),
                        "tcgen05 attention launch");
 }
 
