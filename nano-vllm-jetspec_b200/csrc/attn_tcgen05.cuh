@@ -891,6 +891,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     // tile ahead never overwrites a value the other warpgroup has yet to read.
     float* xm = reinterpret_cast<float*>(sbase + kOffXm);
     const float scale_log2 = p.scale * 1.4426950408889634f;
+    // Operand-type rows whose 32-column pieces start on 32-byte boundaries take 32-byte
+    // stores.
+    const bool wide_out = (reinterpret_cast<uintptr_t>(p.out) & 31u) == 0 &&
+                          (p.out_stride0 | p.out_stride1) % 16 == 0;
     uint32_t g0 = 0, mx_par = 0, lx_par = 0;
     for (uint32_t seq = 0;; ++seq) {
       Item it;
@@ -994,6 +998,22 @@ __global__ void __launch_bounds__(kThreads, 1)
               dst[k] = make_float4(__uint_as_float(o[4 * k]) * inv, __uint_as_float(o[4 * k + 1]) * inv,
                                    __uint_as_float(o[4 * k + 2]) * inv,
                                    __uint_as_float(o[4 * k + 3]) * inv);
+          } else if (wide_out) {
+            // 32-byte stores: each fills a whole sector, half the store transactions.
+            Elem* dst = static_cast<Elem*>(p.out) + off;
+#pragma unroll
+            for (int k = 0; k < 2; ++k) {
+              uint32_t v8[8];
+#pragma unroll
+              for (int e = 0; e < 8; ++e)
+                v8[e] = Mma::pack(__uint_as_float(o[16 * k + 2 * e]) * inv,
+                                  __uint_as_float(o[16 * k + 2 * e + 1]) * inv);
+              asm volatile("st.global.v8.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8};\n" ::"l"(
+                               dst + 16 * k),
+                           "r"(v8[0]), "r"(v8[1]), "r"(v8[2]), "r"(v8[3]), "r"(v8[4]), "r"(v8[5]),
+                           "r"(v8[6]), "r"(v8[7])
+                           : "memory");
+            }
           } else {
             uint4* dst = reinterpret_cast<uint4*>(static_cast<Elem*>(p.out) + off);
 #pragma unroll
