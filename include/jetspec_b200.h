@@ -219,6 +219,36 @@ typedef struct JtRopeScatterParams {
 
 int jt_rope_scatter_launch(const JtRopeScatterParams* params, cudaStream_t stream);
 
+/*
+ * Greedy acceptance walk over the packed verification trees (replaces the argmax
+ * download and host walk of accept_batch, nanovllm/speculative/jetspec/serving_ops.py:55-90,
+ * called from batch_runtime.py:551-553).  Per request r (nodes offsets[r]..offsets[r+1]-1,
+ * root first): path = [0]; while len(path) <= max_depth, follow the child c of the last
+ * node n with parent_indices[c] == n and token_ids[c] == argmax(logits[n]) (the last such
+ * child when siblings repeat a token); correction = argmax(logits[last node]).  argmax is
+ * torch.argmax's: NaN ranks highest, ties go to the lowest index.  Only the logits rows of
+ * the nodes on the path are read.  Outputs: path[r, :] (node indices, -1 padded),
+ * accepted_length[r] = len(path) - 1, correction[r], outputs[r, :] = token_ids[path[1:]]
+ * followed by the correction (-1 padded).  Depths along the path that are not 0, 1, 2, ...
+ * (when depths is given) set device error bit 0.
+ */
+typedef struct JtAcceptWalkParams {
+  const void* logits;              /* [Q, vocab] bf16, f16 or f32 (row stride below)      */
+  const int64_t* token_ids;        /* [Q] draft token of each node                        */
+  const int64_t* parent_indices;   /* [Q] request-local parent, -1 for the root           */
+  const int64_t* depths;           /* [Q] or NULL (no depth check)                        */
+  const int32_t* offsets;          /* [R + 1] packed node offsets (cu_seqlens_q)           */
+  int32_t* path;                   /* [R, path_stride]                                    */
+  int32_t* accepted_length;        /* [R]                                                 */
+  int64_t* correction;             /* [R]                                                 */
+  int64_t* outputs;                /* [R, path_stride]                                    */
+  int64_t logits_stride0;          /* elements between logits rows                        */
+  int32_t logits_dtype;            /* JT_BF16, JT_F16 or JT_F32                           */
+  int32_t vocab, num_requests, max_depth, path_stride;  /* path_stride >= max_depth + 1  */
+} JtAcceptWalkParams;
+
+int jt_accept_walk_launch(const JtAcceptWalkParams* params, cudaStream_t stream);
+
 /* Library information / diagnostics. */
 int32_t jt_abi_version(void);
 const char* jt_last_error(void);

@@ -9,12 +9,15 @@ verifier, scratch arena and block tables work unchanged:
 * copy_accepted_kv           - nanovllm/speculative/jetspec/state.py:64
 * PackedTreeMetadata         - nanovllm/speculative/jetspec/packed_metadata.py:16
 * rope_scatter(_prevalidated) - nanovllm/speculative/jetspec/tree_fusion.py:172-199
+* accept_batch               - nanovllm/speculative/jetspec/serving_ops.py:55 (plus the
+                               device-side accept_walk)
 
 All compute runs in libjetspec_b200.so (hand-written CUDA for sm_100a) through a C ABI
 (include/jetspec_b200.h).  There is no CPU or library fallback: without the built
 library every operator raises LibraryMissingError.
 """
 from ._lib import KernelLaunchError, LibraryMissingError, load_library, read_device_errors
+from .accept import accept_batch, accept_walk
 from .attention import store_kvcache
 from .packed_metadata import PackedTreeMetadata, ancestor_mask_from_parents
 from .paged_backend import packed_tree_attention, packed_tree_attention_reference
@@ -28,5 +31,5 @@ __all__ = [
     "store_kvcache", "PackedTreeMetadata", "ancestor_mask_from_parents",
     "packed_tree_attention", "packed_tree_attention_reference", "KvHeadShard",
     "shard_for_rank", "copy_accepted_kv", "scatter_tree_kv", "rope_scatter",
-    "rope_scatter_prevalidated", "packed_tree_attention_gqa",
+    "rope_scatter_prevalidated", "packed_tree_attention_gqa", "accept_batch", "accept_walk",
 ]

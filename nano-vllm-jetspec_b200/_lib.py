@@ -29,6 +29,7 @@ EXPORTED_SYMBOLS = (
     "jt_kv_store_launch",
     "jt_kv_commit_launch",
     "jt_rope_scatter_launch",
+    "jt_accept_walk_launch",
     "jt_kv_commit_max_slots",
     "jt_abi_version",
     "jt_last_error",
@@ -113,6 +114,16 @@ class JtRopeScatterParams(ctypes.Structure):
     ]
 
 
+class JtAcceptWalkParams(ctypes.Structure):
+    _fields_ = [
+        ("logits", c_void_p), ("token_ids", c_void_p), ("parent_indices", c_void_p),
+        ("depths", c_void_p), ("offsets", c_void_p), ("path", c_void_p),
+        ("accepted_length", c_void_p), ("correction", c_void_p), ("outputs", c_void_p),
+        ("logits_stride0", c_i64), ("logits_dtype", c_i32), ("vocab", c_i32),
+        ("num_requests", c_i32), ("max_depth", c_i32), ("path_stride", c_i32),
+    ]
+
+
 _lock = threading.Lock()
 _lib = None
 
@@ -132,6 +143,8 @@ def _declare(lib):
     lib.jt_kv_commit_launch.restype = ctypes.c_int
     lib.jt_rope_scatter_launch.argtypes = [P(JtRopeScatterParams), c_void_p]
     lib.jt_rope_scatter_launch.restype = ctypes.c_int
+    lib.jt_accept_walk_launch.argtypes = [P(JtAcceptWalkParams), c_void_p]
+    lib.jt_accept_walk_launch.restype = ctypes.c_int
     lib.jt_kv_commit_max_slots.argtypes = []
     lib.jt_kv_commit_max_slots.restype = c_i32
     lib.jt_abi_version.argtypes = []

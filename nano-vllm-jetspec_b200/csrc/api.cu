@@ -34,6 +34,9 @@ extern "C" int jt_read_device_errors(uint32_t* errors) {
   if (rc != JT_OK) return rc;
   rc = jt_read_errors_rope(&c);
   if (rc != JT_OK) return rc;
-  *errors = a | b | c;
+  uint32_t d = 0;
+  rc = jt_read_errors_accept(&d);
+  if (rc != JT_OK) return rc;
+  *errors = a | b | c | d;
   return JT_OK;
 }

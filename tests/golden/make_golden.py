@@ -15,6 +15,8 @@ Everything here executes the reference's own code on the CPU:
   * speculative/jetspec/state.py copy_accepted_kv (torch on CPU)   -> kv_commit.npz
   * speculative/jetspec/tree_fusion.py _rope_scatter_hf_order (interpreter; fp32) and the
     eager RoPE definition of its byte-exact test (bf16)           -> rope_scatter.npz
+  * speculative/jetspec/serving_ops.py accept_batch (host walk over argmax of the logits)
+                                                                  -> accept.npz
 
 The fixtures hold only live K/V rows (bf16 bit patterns) plus seeds and shapes, so they
 stay small; the tests rebuild the NaN-poisoned pools from them.  The GPU box never runs
@@ -251,6 +253,79 @@ def rope_cases():
     print("rope_scatter: bf16 and f32 cases")
 
 
+def accept_cases():
+    """The reference's accept_batch on packed trees (duplicate siblings, a depth cap, ties).
+
+    Trees carry host topology (host_token_ids, host_depths and child maps filled in node
+    order, last sibling winning: the rule accept_batch documents); the first tree is the
+    duplicate-sibling tree of the reference's own test (test_jetspec_serving_ops.py:37-56),
+    whose expected path [0, 2, 4] pins that rule.
+    """
+    from types import SimpleNamespace
+    from nanovllm.speculative.jetspec.serving_ops import accept_batch
+
+    vocab, max_depth = 80, 15
+    rng = np.random.default_rng(2024)
+    trees = [([3, 5, 5, 7, 9], [-1, 0, 0, 1, 2])]
+    for nodes in (1, 5, 16, 31, 64, 9):
+        parents = [-1] + [int(rng.integers(max(0, i - 4), i)) for i in range(1, nodes)]
+        tokens = [int(t) for t in rng.integers(0, 12, size=nodes)]
+        trees.append((tokens, parents))
+    chain = 24  # a chain deeper than max_depth
+    trees.append(([int(t) for t in rng.integers(0, 12, size=chain)], [-1] + list(range(chain - 1))))
+    offsets = [0]
+    for tokens, _ in trees:
+        offsets.append(offsets[-1] + len(tokens))
+    gen = torch.Generator().manual_seed(99)
+    logits = torch.randn(offsets[-1], vocab, generator=gen)
+    logits[0, 5] = 100      # the reference test's planted maxima: root -> token 5
+    logits[2, 9] = 100      # node 2 -> token 9
+    objs = []
+    for r, (tokens, parents) in enumerate(trees):
+        lo = offsets[r]
+        depth = [0] * len(tokens)
+        for i in range(1, len(tokens)):
+            depth[i] = depth[parents[i]] + 1
+        children = [dict() for _ in tokens]
+        for node, (token, parent) in enumerate(zip(tokens, parents)):
+            if parent >= 0:
+                children[parent][token] = node
+        if r >= 2:
+            # Plant a path: from the root follow a random child, making its token the
+            # greedy token of its parent (long paths, duplicate tokens included).
+            node = 0
+            while children[node]:
+                child = int(rng.choice(sorted(children[node].values())))
+                logits[lo + node, tokens[child]] = 50.0
+                node = child
+        if r == 3:
+            logits[lo + len(tokens) - 1, 7] = 60.0   # a tie: the first index (7) wins
+            logits[lo + len(tokens) - 1, 11] = 60.0
+        objs.append(SimpleNamespace(
+            token_ids=torch.tensor(tokens), parent_indices=torch.tensor(parents),
+            depth=torch.tensor(depth), num_nodes=len(tokens), host_token_ids=tokens,
+            host_depths=depth, child_maps=children))
+    results = accept_batch(logits, objs, offsets, max_depth)
+    assert results[0]["path"] == [0, 2, 4], results[0]
+    width = max_depth + 1
+    path = np.full((len(trees), width), -1, dtype=np.int32)
+    outputs = np.full((len(trees), width), -1, dtype=np.int64)
+    for r, res in enumerate(results):
+        path[r, :len(res["path"])] = res["path"]
+        outputs[r, :len(res["outputs"])] = res["outputs"]
+    np.savez_compressed(
+        HERE / "accept.npz", logits=logits.numpy(),
+        token_ids=np.concatenate([np.array(t, dtype=np.int64) for t, _ in trees]),
+        parents=np.concatenate([np.array(p, dtype=np.int64) for _, p in trees]),
+        depths=np.concatenate([o.depth.numpy() for o in objs]).astype(np.int64),
+        offsets=np.array(offsets, dtype=np.int32), max_depth=max_depth, path=path,
+        accepted_length=np.array([r["accepted_length"] for r in results], dtype=np.int32),
+        correction=np.array([r["correction"] for r in results], dtype=np.int64),
+        outputs=outputs)
+    print("accept: %d trees, accepted lengths %s" % (
+        len(trees), [r["accepted_length"] for r in results]))
+
+
 def main():
     parser = argparse.ArgumentParser()
     parser.add_argument("--reference", required=True, help="path of the reference checkout")
@@ -261,6 +336,7 @@ def main():
     metadata_case()
     kv_cases()
     rope_cases()
+    accept_cases()
     rng = np.random.default_rng(7)
     parents = [random_parents(rng, n) for n in (7, 5, 9)]
     attention_case("ragged3", (65, 0, 257), ((2,), (), (4, 0)), parents, 6 * 256, 8,
