@@ -7,7 +7,8 @@ commit.  At N GPUs the global batch has N x 64 requests and every GPU owns 8/N o
 8 KV heads of every request (KV-head sharding: per-GPU work is fixed, scaling "weak";
 there is no collective on the data path, only the timing max-reduction).
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference|reference-triton]
+    python bench.py [--gpus N] [--steps K] [--warmup W]
+                    [--impl ours|reference|reference-triton|accept-walk]
 
 Rank 0 prints one JSON line.  ``--impl reference`` times the reference's CPU path (the
 oracle port of its masked-SDPA attention) on the host cores for the same workload.
@@ -47,10 +48,11 @@ def parse():
     parser.add_argument("--gpus", type=int, default=1)
     parser.add_argument("--steps", type=int, default=200)
     parser.add_argument("--warmup", type=int, default=10)
-    parser.add_argument("--impl", choices=("ours", "reference", "reference-triton"),
+    parser.add_argument("--impl", choices=("ours", "reference", "reference-triton", "accept-walk"),
                         default="ours",
                         help="reference-triton: the reference's own Triton kernels (installed "
-                             "under baseline/_ref) beside ours on configs 1-4, one GPU")
+                             "under baseline/_ref) beside ours on configs 1-4, one GPU; "
+                             "accept-walk: the round's acceptance step, reference vs device walk")
     parser.add_argument("--requests-per-gpu", type=int, default=64)
     parser.add_argument("--no-cpu-baseline", action="store_true")
     parser.add_argument("--cpu-seconds", type=float, default=12.0,
@@ -275,6 +277,104 @@ def run_reference_triton(args, rank: int):
         torch.cuda.empty_cache()
 
 
+# ---- acceptance walk after verification ------------------------------------------------
+def run_accept_walk(args, rank: int):
+    """The round's acceptance step on config 3 trees with a Qwen3 vocabulary (151936).
+
+    Logits [Q, vocab] bf16 are random with the config's accepted paths planted (each path
+    node's greedy token is its next node's draft token).  Arms: the reference's
+    accept_batch (serving_ops.py:55-90: full argmax, one download, host walk; installed
+    under baseline/_ref) and this package's accept_walk (device walk, argmax only of path
+    nodes) and accept_batch (the same plus one small download).  CUDA events around the
+    device walk; wall clock (with the synchronising download) around the host-walk arms.
+    """
+    if rank != 0:
+        return
+    device = torch.device("cuda", 0)
+    torch.cuda.set_device(device)
+    vocab = 151936
+    batch = workloads.config3()
+    offsets = [0]
+    for n in batch.node_counts:
+        offsets.append(offsets[-1] + n)
+    rng = np.random.default_rng(11)
+    tokens = rng.integers(0, vocab, size=offsets[-1]).tolist()
+    gen = torch.Generator(device=device).manual_seed(12)
+    logits = torch.randn((offsets[-1], vocab), generator=gen, device=device).bfloat16()
+    trees = []
+    from types import SimpleNamespace
+    # Per-node arrays of all trees in one device allocation, each tree holding views of it
+    # (the layout the reference's build_trees produces, serving_ops.py:37-40).
+    packed = torch.tensor([tokens, [p for ps in batch.parents for p in ps]], device=device)
+    for r, parents in enumerate(batch.parents):
+        lo, path = offsets[r], batch.accepted_paths[r]
+        for a, b in zip(path[:-1], path[1:]):
+            logits[lo + a, tokens[lo + b]] = 40.0
+        depth = [0] * len(parents)
+        for i in range(1, len(parents)):
+            depth[i] = depth[parents[i]] + 1
+        children = [dict() for _ in parents]
+        for node, parent in enumerate(parents):
+            if parent >= 0:
+                children[parent][tokens[lo + node]] = node
+        tree_tokens = tokens[lo:lo + len(parents)]
+        trees.append(SimpleNamespace(
+            token_ids=packed[0, lo:lo + len(parents)],
+            parent_indices=packed[1, lo:lo + len(parents)],
+            depth=torch.tensor(depth, device=device), num_nodes=len(parents),
+            host_token_ids=tree_tokens, host_depths=depth, child_maps=children))
+    max_depth = max(len(p) for p in batch.accepted_paths) + 4
+    tok = torch.tensor(tokens, device=device)
+    par = torch.cat([t.parent_indices for t in trees])
+    offs = torch.tensor(offsets, dtype=torch.int32, device=device)
+    steps, warmup = max(args.steps, 1), max(args.warmup, 3)
+
+    def timed_events(fn):
+        times = []
+        for i in range(warmup + steps):
+            s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            s.record()
+            fn()
+            e.record()
+            torch.cuda.synchronize(device)
+            if i >= warmup:
+                times.append(s.elapsed_time(e))
+        return statistics.median(times)
+
+    def timed_wall(fn):
+        times = []
+        for i in range(warmup + steps):
+            torch.cuda.synchronize(device)
+            t0 = time.perf_counter()
+            fn()
+            torch.cuda.synchronize(device)
+            if i >= warmup:
+                times.append((time.perf_counter() - t0) * 1e3)
+        return statistics.median(times)
+
+    ours = jb.accept_batch(logits, trees, offsets, max_depth)
+    line = {"impl": "accept-walk", "workload": "config3 trees (64 requests, 3872 nodes), "
+            "vocab 151936 bf16 logits, config3 accepted paths planted",
+            "steps": steps, "warmup": warmup,
+            "accepted_lengths_total": sum(r["accepted_length"] for r in ours),
+            "ours_device_walk_ms": timed_events(
+                lambda: jb.accept_walk(logits, tok, par, offs, max_depth)),
+            "ours_accept_batch_ms": timed_wall(
+                lambda: jb.accept_batch(logits, trees, offsets, max_depth)),
+            "full_argmax_ms": timed_events(lambda: logits.argmax(-1)),
+            "logits_bytes": logits.numel() * 2,
+            "walk_rows_read": sum(r["accepted_length"] + 1 for r in ours)}
+    ref_root = ROOT / "baseline" / "_ref"
+    if (ref_root / "nanovllm").is_dir():
+        sys.path.insert(0, str(ref_root))
+        from nanovllm.speculative.jetspec.serving_ops import accept_batch as ref_accept
+        expected = ref_accept(logits, trees, offsets, max_depth)
+        line["matches_reference"] = expected == ours
+        line["reference_accept_batch_ms"] = timed_wall(
+            lambda: ref_accept(logits, trees, offsets, max_depth))
+    print(json.dumps(line), flush=True)
+
+
 # ---- GPU side -------------------------------------------------------------------------
 class Step:
     """Device-resident inputs of one verify step on this rank's KV-head shard."""
@@ -420,6 +520,8 @@ def main():
         return run_reference(args, rank, world)
     if args.impl == "reference-triton":
         return run_reference_triton(args, rank)
+    if args.impl == "accept-walk":
+        return run_accept_walk(args, rank)
     if world != args.gpus and "WORLD_SIZE" in os.environ:
         args.gpus = world
     device = torch.device("cuda", local_rank)

@@ -73,9 +73,24 @@ def accept_walk(logits: torch.Tensor, token_ids: torch.Tensor, parent_indices: t
 
 def _host_list(tree, host_name, name):
     values = getattr(tree, host_name, None)
-    if values is None:
-        values = getattr(tree, name).tolist()
-    return [int(x) for x in values]
+    return values if values is not None else getattr(tree, name).tolist()
+
+
+def _packed(tensors, device):
+    """One flat device tensor of the trees' per-node values.  build_trees leaves them as
+    back-to-back views of one packed allocation; then that storage is used as it is,
+    otherwise the pieces are concatenated."""
+    first = tensors[0]
+    start, total = first.storage_offset(), 0
+    contiguous = all(
+        t.device == device and t.dtype == first.dtype and t.dim() == 1 and
+        (t.numel() <= 1 or t.stride(0) == 1) and
+        t.untyped_storage().data_ptr() == first.untyped_storage().data_ptr() and
+        t.storage_offset() == start + (total := total + t.numel()) - t.numel()
+        for t in tensors)
+    if contiguous:
+        return first.as_strided((total,), (1,), start)
+    return torch.cat([t.reshape(-1).to(device) for t in tensors])
 
 
 def accept_batch(logits, trees, offsets, max_depth):
@@ -87,23 +102,22 @@ def accept_batch(logits, trees, offsets, max_depth):
     0, 1, 2, ... (the reference's check).
     """
     device = logits.device
-    token_ids = torch.cat([t.token_ids.reshape(-1).to(device) for t in trees])
-    parents = torch.cat([t.parent_indices.reshape(-1).to(device) for t in trees])
-    offs = torch.tensor([int(o) for o in offsets], dtype=torch.int32, device=device)
+    token_ids = _packed([t.token_ids for t in trees], device)
+    parents = _packed([t.parent_indices for t in trees], device)
+    offs = torch.tensor(offsets, dtype=torch.int32, device=device)
     path, accepted, correction, outputs = accept_walk(logits, token_ids, parents, offs,
                                                       max_depth)
-    host = torch.cat((path.to(torch.int64), accepted.to(torch.int64)[:, None],
-                      correction[:, None], outputs), dim=1).cpu()
+    rows = torch.cat((path.to(torch.int64), accepted.to(torch.int64)[:, None],
+                      correction[:, None], outputs), dim=1).tolist()  # the one download
     width = max_depth + 1
     results = []
-    for i, tree in enumerate(trees):
-        row = host[i].tolist()
-        length = int(row[width]) + 1
-        node_path = [int(x) for x in row[:length]]
+    for tree, row in zip(trees, rows):
+        length = row[width] + 1
+        node_path = row[:length]
         depths = _host_list(tree, "host_depths", "depth")
-        if [depths[node] for node in node_path] != list(range(len(node_path))):
+        if any(depths[node] != i for i, node in enumerate(node_path)):
             raise RuntimeError("accepted RoPE positions do not match canonical tail")
         results.append({"path": node_path, "accepted_length": length - 1,
-                        "correction": int(row[width + 1]),
-                        "outputs": [int(x) for x in row[width + 2:width + 2 + length]]})
+                        "correction": row[width + 1],
+                        "outputs": row[width + 2:width + 2 + length]})
     return results

@@ -16,21 +16,15 @@
 // index.  The depth check of the reference (depths along the path equal 0, 1, 2, ...)
 // sets JT_DEVERR_OUT_OF_RANGE instead of raising; a parent index outside the request is
 // skipped the same way.
+#include <type_traits>
+
 #include "common.cuh"
 
 namespace {
 
 __device__ uint32_t g_accept_errors;
 
-constexpr int kAcceptThreads = 512;
-
-// (value, index) order of torch.argmax: NaN first, then larger value, then lower index.
-__device__ __forceinline__ bool better(float a, int ia, float b, int ib) {
-  const bool na = a != a, nb = b != b;
-  if (na != nb) return na;
-  if (!na && a != b) return a > b;
-  return ia < ib;
-}
+constexpr int kAcceptThreads = 1024;  // 128 KB of a logits row in flight per CTA
 
 template <typename T>
 __device__ __forceinline__ float to_f32(T v);
@@ -47,68 +41,109 @@ __device__ __forceinline__ float to_f32<float>(float v) {
   return v;
 }
 
-// argmax of one logits row, over the whole block; every thread gets the result.
+// NaN-propagating max ("NaN ranks highest"), two lanes at a time for 16-bit types.
+__device__ __forceinline__ uint32_t vmax2(uint32_t a, uint32_t b, __nv_bfloat16) {
+  const __nv_bfloat162 r = __hmax2_nan(*reinterpret_cast<__nv_bfloat162*>(&a),
+                                       *reinterpret_cast<__nv_bfloat162*>(&b));
+  return *reinterpret_cast<const uint32_t*>(&r);
+}
+__device__ __forceinline__ uint32_t vmax2(uint32_t a, uint32_t b, __half) {
+  const __half2 r = __hmax2_nan(*reinterpret_cast<__half2*>(&a), *reinterpret_cast<__half2*>(&b));
+  return *reinterpret_cast<const uint32_t*>(&r);
+}
+__device__ __forceinline__ float fmax_nan(float a, float b) {
+  float d;
+  asm("max.NaN.f32 %0, %1, %2;\n" : "=f"(d) : "f"(a), "f"(b));
+  return d;
+}
+__device__ __forceinline__ float lo_f32(uint32_t v, __nv_bfloat16) {
+  return __uint_as_float(v << 16);
+}
+__device__ __forceinline__ float hi_f32(uint32_t v, __nv_bfloat16) {
+  return __uint_as_float(v & 0xffff0000u);
+}
+__device__ __forceinline__ float lo_f32(uint32_t v, __half) {
+  return __half2float(__ushort_as_half(static_cast<unsigned short>(v & 0xffffu)));
+}
+__device__ __forceinline__ float hi_f32(uint32_t v, __half) {
+  return __half2float(__ushort_as_half(static_cast<unsigned short>(v >> 16)));
+}
+
+// Block-wide NaN-propagating max of one float per thread (every thread gets it).
+__device__ float block_max_nan(float v, float* s_val) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  for (int o = 16; o > 0; o >>= 1) v = fmax_nan(v, __shfl_xor_sync(0xffffffffu, v, o));
+  if (lane == 0) s_val[warp] = v;
+  __syncthreads();
+  v = s_val[0];
+  for (int w = 1; w < kAcceptThreads / 32; ++w) v = fmax_nan(v, s_val[w]);
+  __syncthreads();
+  return v;
+}
+__device__ int block_min(int v, int* s_idx) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  for (int o = 16; o > 0; o >>= 1) v = min(v, __shfl_xor_sync(0xffffffffu, v, o));
+  if (lane == 0) s_idx[warp] = v;
+  __syncthreads();
+  v = s_idx[0];
+  for (int w = 1; w < kAcceptThreads / 32; ++w) v = min(v, s_idx[w]);
+  __syncthreads();
+  return v;
+}
+
+__device__ __forceinline__ bool same(float a, float m) { return a == m || (a != a && m != m); }
+
+// argmax of one logits row, over the whole block; every thread gets the result.  Pass 1:
+// the row's max (NaN highest) with packed max instructions while streaming the row;
+// pass 2: the first index holding it (the row is now in L2).
 template <typename T>
 __device__ int row_argmax(const T* row, int vocab, float* s_val, int* s_idx) {
   constexpr int kVec = 16 / sizeof(T);  // elements per 16-byte load
-  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  float best = -INFINITY;
-  int best_i = 0x7fffffff;
+  const int tid = threadIdx.x;
   const bool aligned = (reinterpret_cast<uintptr_t>(row) & 15u) == 0;
   const int nvec = aligned ? vocab / kVec : 0;
   const uint4* vrow = reinterpret_cast<const uint4*>(row);
-  // Four independent 16-byte loads in flight per thread.
-  int v = tid;
-  for (; v + 3 * kAcceptThreads < nvec; v += 4 * kAcceptThreads) {
-    uint4 x[4];
+  float best = -INFINITY;
+  constexpr int kInFlight = 8;
+  if constexpr (sizeof(T) == 2) {
+    uint32_t m2 = 0xff80ff80u;  // two -inf (bf16); for f16 0xfc00 pairs below
+    if constexpr (std::is_same<T, __half>::value) m2 = 0xfc00fc00u;
+    int v = tid;
+    for (; v + (kInFlight - 1) * kAcceptThreads < nvec; v += kInFlight * kAcceptThreads) {
+      uint4 x[kInFlight];
 #pragma unroll
-    for (int u = 0; u < 4; ++u) x[u] = __ldcs(vrow + v + u * kAcceptThreads);
+      for (int u = 0; u < kInFlight; ++u) x[u] = __ldcg(vrow + v + u * kAcceptThreads);
 #pragma unroll
-    for (int u = 0; u < 4; ++u) {
-      const T* e = reinterpret_cast<const T*>(&x[u]);
-#pragma unroll
-      for (int k = 0; k < kVec; ++k) {
-        const int idx = (v + u * kAcceptThreads) * kVec + k;
-        const float f = to_f32(e[k]);
-        if (better(f, idx, best, best_i)) { best = f; best_i = idx; }
-      }
+      for (int u = 0; u < kInFlight; ++u)
+        m2 = vmax2(vmax2(m2, vmax2(x[u].x, x[u].y, T()), T()), vmax2(x[u].z, x[u].w, T()), T());
+    }
+    for (; v < nvec; v += kAcceptThreads) {
+      const uint4 x = __ldcg(vrow + v);
+      m2 = vmax2(vmax2(m2, vmax2(x.x, x.y, T()), T()), vmax2(x.z, x.w, T()), T());
+    }
+    best = fmax_nan(lo_f32(m2, T()), hi_f32(m2, T()));
+  } else {
+    for (int v = tid; v < nvec; v += kAcceptThreads) {
+      const uint4 x = __ldcg(vrow + v);
+      best = fmax_nan(fmax_nan(fmax_nan(best, __uint_as_float(x.x)), __uint_as_float(x.y)),
+                      fmax_nan(__uint_as_float(x.z), __uint_as_float(x.w)));
     }
   }
-  for (; v < nvec; v += kAcceptThreads) {
-    const uint4 x = __ldcs(vrow + v);
+  for (int idx = nvec * kVec + tid; idx < vocab; idx += kAcceptThreads)
+    best = fmax_nan(best, to_f32(row[idx]));
+  const float m = block_max_nan(best, s_val);
+  // Pass 2: the lowest index whose value is the maximum (an equal NaN counts as equal).
+  int first = 0x7fffffff;
+  for (int v = tid; v < nvec && first == 0x7fffffff; v += kAcceptThreads) {
+    const uint4 x = __ldcg(vrow + v);
     const T* e = reinterpret_cast<const T*>(&x);
 #pragma unroll
-    for (int k = 0; k < kVec; ++k) {
-      const int idx = v * kVec + k;
-      const float f = to_f32(e[k]);
-      if (better(f, idx, best, best_i)) { best = f; best_i = idx; }
-    }
+    for (int k = kVec - 1; k >= 0; --k)
+      if (same(to_f32(e[k]), m)) first = v * kVec + k;
   }
-  for (int idx = nvec * kVec + tid; idx < vocab; idx += kAcceptThreads) {
-    const float f = to_f32(row[idx]);
-    if (better(f, idx, best, best_i)) { best = f; best_i = idx; }
-  }
-  for (int o = 16; o > 0; o >>= 1) {
-    const float ob = __shfl_xor_sync(0xffffffffu, best, o);
-    const int oi = __shfl_xor_sync(0xffffffffu, best_i, o);
-    if (better(ob, oi, best, best_i)) { best = ob; best_i = oi; }
-  }
-  if (lane == 0) { s_val[warp] = best; s_idx[warp] = best_i; }
-  __syncthreads();
-  if (warp == 0) {
-    best = lane < kAcceptThreads / 32 ? s_val[lane] : -INFINITY;
-    best_i = lane < kAcceptThreads / 32 ? s_idx[lane] : 0x7fffffff;
-    for (int o = 16; o > 0; o >>= 1) {
-      const float ob = __shfl_xor_sync(0xffffffffu, best, o);
-      const int oi = __shfl_xor_sync(0xffffffffu, best_i, o);
-      if (better(ob, oi, best, best_i)) { best = ob; best_i = oi; }
-    }
-    if (lane == 0) s_idx[32] = best_i;
-  }
-  __syncthreads();
-  const int result = s_idx[32];
-  __syncthreads();  // s_idx is reused by the next call
-  return result;
+  for (int idx = nvec * kVec + tid; idx < vocab && first == 0x7fffffff; idx += kAcceptThreads)
+    if (same(to_f32(row[idx]), m)) first = idx;
+  return block_min(first, s_idx);
 }
 
 template <typename T>
