@@ -249,6 +249,15 @@ typedef struct JtAcceptWalkParams {
 
 int jt_accept_walk_launch(const JtAcceptWalkParams* params, cudaStream_t stream);
 
+/*
+ * Failure detection without a GPU fault: runs one thread that waits, with the kernels'
+ * bounded-wait routine and a limit of limit_cycles, on an mbarrier nothing arrives on.
+ * Synchronous (diagnostics).  out[0] = 1 if the wait claimed completion (a failure),
+ * out[1] = the abort flag the wait raised (expected 1), out[2] = cycles spent waiting.
+ * Afterwards jt_read_device_errors reports bit 2 (timeout), and the context stays usable.
+ */
+int jt_selftest_bounded_wait(int64_t limit_cycles, int32_t* out);
+
 /* Library information / diagnostics. */
 int32_t jt_abi_version(void);
 const char* jt_last_error(void);

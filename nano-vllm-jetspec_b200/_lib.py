@@ -30,6 +30,7 @@ EXPORTED_SYMBOLS = (
     "jt_kv_commit_launch",
     "jt_rope_scatter_launch",
     "jt_accept_walk_launch",
+    "jt_selftest_bounded_wait",
     "jt_kv_commit_max_slots",
     "jt_abi_version",
     "jt_last_error",
@@ -145,6 +146,8 @@ def _declare(lib):
     lib.jt_rope_scatter_launch.restype = ctypes.c_int
     lib.jt_accept_walk_launch.argtypes = [P(JtAcceptWalkParams), c_void_p]
     lib.jt_accept_walk_launch.restype = ctypes.c_int
+    lib.jt_selftest_bounded_wait.argtypes = [c_i64, P(c_i32)]
+    lib.jt_selftest_bounded_wait.restype = ctypes.c_int
     lib.jt_kv_commit_max_slots.argtypes = []
     lib.jt_kv_commit_max_slots.restype = c_i32
     lib.jt_abi_version.argtypes = []
@@ -199,3 +202,11 @@ def read_device_errors() -> int:
     bits = c_u32(0)
     check(lib.jt_read_device_errors(ctypes.byref(bits)))
     return int(bits.value)
+
+
+def selftest_bounded_wait(limit_cycles: int) -> tuple[int, int, int]:
+    """Run the bounded-wait self-test (synchronous): (claimed completion, abort flag, cycles)."""
+    lib = load_library()
+    out = (c_i32 * 3)()
+    check(lib.jt_selftest_bounded_wait(int(limit_cycles), out))
+    return int(out[0]), int(out[1]), int(out[2])

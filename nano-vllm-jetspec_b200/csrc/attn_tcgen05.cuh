@@ -118,13 +118,14 @@ __device__ __forceinline__ bool mbar_try(uint32_t bar, uint32_t parity) {
 }
 // Bounded wait for the completion of the phase with the given parity.
 __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatile int* abort,
-                                          bool abortable = true) {
+                                          bool abortable = true,
+                                          long long limit = kWaitLimit) {
   if (mbar_try(bar, parity)) return true;
   const long long start = clock64();
   for (;;) {
     if (mbar_try(bar, parity)) return true;
     if (abortable && *abort) return false;
-    if (clock64() - start > kWaitLimit) {
+    if (clock64() - start > limit) {
       *abort = 1;
       atomicOr(&g_attn_errors, JT_DEVERR_TIMEOUT);
       return false;
@@ -1107,6 +1108,27 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (warp == 0) {
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, 512;\n" ::"r"(tmem) : "memory");
   }
+}
+
+// Self-test of the bounded wait (failure detection without a GPU fault): one thread waits
+// on an mbarrier nothing arrives on, with a short limit.  The wait must give up, raise the
+// CTA's abort flag and the timeout error bit, and the kernel must return normally.
+// out[0]: 1 if the wait claimed completion (a failure); out[1]: the abort flag afterwards;
+// out[2]: cycles spent in the wait (saturated).
+__global__ void wait_selftest_kernel(long long limit, int* out) {
+  __shared__ __align__(8) unsigned long long bar;
+  __shared__ int abort_flag;
+  if (threadIdx.x != 0) return;
+  abort_flag = 0;
+  const uint32_t addr = jt::smem_u32(&bar);
+  mbar_init(addr, 1);
+  asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
+  const long long t0 = clock64();
+  const bool ok = mbar_wait(addr, 0, &abort_flag, true, limit);
+  const long long spent = clock64() - t0;
+  out[0] = ok ? 1 : 0;
+  out[1] = abort_flag;
+  out[2] = static_cast<int>(spent < 0x7fffffffll ? spent : 0x7fffffffll);
 }
 
 }  // namespace tc

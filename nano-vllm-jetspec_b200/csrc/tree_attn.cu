@@ -1046,3 +1046,27 @@ extern "C" int jt_tree_attn_launch_noalloc(const JtTreeAttnParams* pp, cudaStrea
   p.workspace_bytes = kStaticWorkspaceBytes;
   return run_tree_attn(p, kStaticPartialBudget, stream);
 }
+
+// ---- bounded-wait self-test ---------------------------------------------------------
+namespace {
+__device__ int g_wait_selftest[3];
+}  // namespace
+
+extern "C" int jt_selftest_bounded_wait(int64_t limit_cycles, int32_t* out) {
+  if (out == nullptr || limit_cycles < 1 || limit_cycles > (1ll << 32))
+    return jt_fail(JT_ERR_INVALID, "selftest_bounded_wait: limit must be in [1, 2^32] cycles");
+  int* dev = nullptr;
+  int rc = jt_cuda_check(cudaGetSymbolAddress(reinterpret_cast<void**>(&dev), g_wait_selftest),
+                         "self-test buffer");
+  if (rc != JT_OK) return rc;
+  tc::wait_selftest_kernel<<<1, 32>>>(limit_cycles, dev);
+  rc = jt_cuda_check(cudaGetLastError(), "self-test launch");
+  if (rc != JT_OK) return rc;
+  rc = jt_cuda_check(cudaDeviceSynchronize(), "self-test run");
+  if (rc != JT_OK) return rc;
+  int host[3] = {0, 0, 0};
+  rc = jt_cuda_check(cudaMemcpyFromSymbol(host, g_wait_selftest, sizeof(host)), "self-test read");
+  if (rc != JT_OK) return rc;
+  for (int i = 0; i < 3; ++i) out[i] = host[i];
+  return JT_OK;
+}
