@@ -8,7 +8,7 @@ commit.  At N GPUs the global batch has N x 64 requests and every GPU owns 8/N o
 there is no collective on the data path, only the timing max-reduction).
 
     python bench.py [--gpus N] [--steps K] [--warmup W]
-                    [--impl ours|reference|reference-triton|accept-walk]
+                    [--impl ours|reference|reference-triton|accept-walk|metadata-build]
 
 Rank 0 prints one JSON line.  ``--impl reference`` times the reference's CPU path (the
 oracle port of its masked-SDPA attention) on the host cores for the same workload.
@@ -48,11 +48,13 @@ def parse():
     parser.add_argument("--gpus", type=int, default=1)
     parser.add_argument("--steps", type=int, default=200)
     parser.add_argument("--warmup", type=int, default=10)
-    parser.add_argument("--impl", choices=("ours", "reference", "reference-triton", "accept-walk"),
+    parser.add_argument("--impl", choices=("ours", "reference", "reference-triton", "accept-walk",
+                                           "metadata-build"),
                         default="ours",
                         help="reference-triton: the reference's own Triton kernels (installed "
                              "under baseline/_ref) beside ours on configs 1-4, one GPU; "
-                             "accept-walk: the round's acceptance step, reference vs device walk")
+                             "accept-walk: the round's acceptance step, reference vs device walk; "
+                             "metadata-build: round metadata, reference host build vs device build")
     parser.add_argument("--requests-per-gpu", type=int, default=64)
     parser.add_argument("--no-cpu-baseline", action="store_true")
     parser.add_argument("--cpu-seconds", type=float, default=12.0,
@@ -375,6 +377,67 @@ def run_accept_walk(args, rank: int):
     print(json.dumps(line), flush=True)
 
 
+# ---- metadata build for a verification round ---------------------------------------------
+def run_metadata_build(args, rank: int):
+    """Round metadata for the config 3 trees: the reference's from_host_trees (host numpy
+    bias matrices, three uploads; installed under baseline/_ref) against
+    PackedTreeMetadata.from_parents_device (one int32 upload, one kernel).  Wall clock per
+    call with a device synchronisation on both sides, medians."""
+    if rank != 0:
+        return
+    from types import SimpleNamespace
+    from jetspec_b200 import PackedTreeMetadata, ancestor_mask_from_parents
+    device = torch.device("cuda", 0)
+    torch.cuda.set_device(device)
+    batch = workloads.config3()
+    used = {p for t in batch.block_tables for p in t}
+    total = sum(batch.node_counts)
+    arena = [p for p in range(batch.num_blocks) if p not in used][:-(-total // BLOCK)]
+    steps, warmup = max(args.steps, 1), max(args.warmup, 3)
+
+    def timed(fn):
+        times = []
+        for i in range(warmup + steps):
+            torch.cuda.synchronize(device)
+            t0 = time.perf_counter()
+            fn()
+            torch.cuda.synchronize(device)
+            if i >= warmup:
+                times.append((time.perf_counter() - t0) * 1e3)
+        return statistics.median(times)
+
+    ours = lambda: PackedTreeMetadata.from_parents_device(  # noqa: E731
+        batch.prefix_lens, batch.block_tables, batch.parents, arena, BLOCK, device=device)
+    line = {"impl": "metadata-build", "workload": "config3 round metadata (64 requests, "
+            f"{total} nodes, {sum(n * n for n in batch.node_counts) * 4} bias bytes)",
+            "steps": steps, "warmup": warmup, "ours_device_build_ms": timed(ours),
+            "upload_bytes_ours": 4 * (2 * batch.num_requests + total + len(arena) +
+                                      batch.num_requests * max(1, max(len(t) for t in batch.block_tables)))}
+    ref_root = ROOT / "baseline" / "_ref"
+    if (ref_root / "nanovllm").is_dir():
+        sys.path.insert(0, str(ref_root))
+        from nanovllm.speculative.jetspec.packed_metadata import PackedTreeMetadata as RefMeta
+        trees = []
+        for parents in batch.parents:
+            depth = [0] * len(parents)
+            for i in range(1, len(parents)):
+                depth[i] = depth[parents[i]] + 1
+            trees.append(SimpleNamespace(
+                num_nodes=len(parents), host_parents=list(parents), host_depths=depth,
+                host_ancestor=torch.from_numpy(ancestor_mask_from_parents(parents))))
+        ids = list(range(batch.num_requests))
+        ref = lambda: RefMeta.from_host_trees(  # noqa: E731
+            batch.prefix_lens, batch.block_tables, trees, arena, BLOCK, device=device,
+            request_ids=ids)
+        a, b = ref(), ours()
+        line["matches_reference"] = all(
+            torch.equal(getattr(a, n), getattr(b, n)) for n in (
+                "cu_seqlens_q", "query_to_request", "query_local_row", "prefix_lens",
+                "block_tables", "tree_slots", "qq_bias", "qq_bias_offsets", "node_counts"))
+        line["reference_from_host_trees_ms"] = timed(ref)
+    print(json.dumps(line), flush=True)
+
+
 # ---- GPU side -------------------------------------------------------------------------
 class Step:
     """Device-resident inputs of one verify step on this rank's KV-head shard."""
@@ -522,6 +585,8 @@ def main():
         return run_reference_triton(args, rank)
     if args.impl == "accept-walk":
         return run_accept_walk(args, rank)
+    if args.impl == "metadata-build":
+        return run_metadata_build(args, rank)
     if world != args.gpus and "WORLD_SIZE" in os.environ:
         args.gpus = world
     device = torch.device("cuda", local_rank)

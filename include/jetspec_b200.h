@@ -250,6 +250,33 @@ typedef struct JtAcceptWalkParams {
 int jt_accept_walk_launch(const JtAcceptWalkParams* params, cudaStream_t stream);
 
 /*
+ * Device-side build of the packed verification metadata (the fields of
+ * PackedTreeMetadata, nanovllm/speculative/jetspec/packed_metadata.py:16-33, as
+ * from_host_trees builds them, :128-198) from compact topology: per request its node count
+ * and each node's request-local parent (parents[0] = -1, every parent before its child),
+ * plus the round's arena pages (scratch slot of packed node q = arena_pages[q / block_size]
+ * * block_size + q % block_size).  Writes cu_seqlens_q, query_to_request, query_local_row,
+ * tree_slots, qq_bias (0 where node j sees node n: n is j or an ancestor of j; -inf
+ * elsewhere) and qq_bias_offsets.  A parent out of order sets device error bit 0 and
+ * leaves the node seeing only itself.
+ */
+typedef struct JtMetadataBuildParams {
+  const int32_t* node_counts;  /* [R]                                               */
+  const int32_t* parents;      /* [Q] request-local parent indices                  */
+  const int32_t* arena_pages;  /* [ceil(Q / block_size)] scratch pages of the round */
+  int32_t* cu_seqlens_q;       /* [R + 1]                                           */
+  int32_t* query_to_request;   /* [Q]                                               */
+  int32_t* query_local_row;    /* [Q]                                               */
+  int64_t* tree_slots;         /* [Q]                                               */
+  float* qq_bias;              /* [sum of T_r^2]                                    */
+  int64_t* qq_bias_offsets;    /* [R + 1]                                           */
+  int32_t num_requests, block_size;
+  int32_t max_nodes;           /* max T_r (<= 1024): sizes the kernel's shared memory */
+} JtMetadataBuildParams;
+
+int jt_metadata_build_launch(const JtMetadataBuildParams* params, cudaStream_t stream);
+
+/*
  * Failure detection without a GPU fault: runs one thread that waits, with the kernels'
  * bounded-wait routine and a limit of limit_cycles, on an mbarrier nothing arrives on.
  * Synchronous (diagnostics).  out[0] = 1 if the wait claimed completion (a failure),

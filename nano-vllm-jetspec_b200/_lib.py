@@ -31,6 +31,7 @@ EXPORTED_SYMBOLS = (
     "jt_rope_scatter_launch",
     "jt_accept_walk_launch",
     "jt_selftest_bounded_wait",
+    "jt_metadata_build_launch",
     "jt_kv_commit_max_slots",
     "jt_abi_version",
     "jt_last_error",
@@ -125,6 +126,16 @@ class JtAcceptWalkParams(ctypes.Structure):
     ]
 
 
+class JtMetadataBuildParams(ctypes.Structure):
+    _fields_ = [
+        ("node_counts", c_void_p), ("parents", c_void_p), ("arena_pages", c_void_p),
+        ("cu_seqlens_q", c_void_p), ("query_to_request", c_void_p),
+        ("query_local_row", c_void_p), ("tree_slots", c_void_p), ("qq_bias", c_void_p),
+        ("qq_bias_offsets", c_void_p), ("num_requests", c_i32), ("block_size", c_i32),
+        ("max_nodes", c_i32),
+    ]
+
+
 _lock = threading.Lock()
 _lib = None
 
@@ -148,6 +159,8 @@ def _declare(lib):
     lib.jt_accept_walk_launch.restype = ctypes.c_int
     lib.jt_selftest_bounded_wait.argtypes = [c_i64, P(c_i32)]
     lib.jt_selftest_bounded_wait.restype = ctypes.c_int
+    lib.jt_metadata_build_launch.argtypes = [P(JtMetadataBuildParams), c_void_p]
+    lib.jt_metadata_build_launch.restype = ctypes.c_int
     lib.jt_kv_commit_max_slots.argtypes = []
     lib.jt_kv_commit_max_slots.restype = c_i32
     lib.jt_abi_version.argtypes = []

@@ -34,9 +34,11 @@ extern "C" int jt_read_device_errors(uint32_t* errors) {
   if (rc != JT_OK) return rc;
   rc = jt_read_errors_rope(&c);
   if (rc != JT_OK) return rc;
-  uint32_t d = 0;
+  uint32_t d = 0, e = 0;
   rc = jt_read_errors_accept(&d);
   if (rc != JT_OK) return rc;
-  *errors = a | b | c | d;
+  rc = jt_read_errors_meta(&e);
+  if (rc != JT_OK) return rc;
+  *errors = a | b | c | d | e;
   return JT_OK;
 }

@@ -14,6 +14,7 @@ Device fields (R requests, Q = sum of node counts):
 """
 from __future__ import annotations
 
+import ctypes
 from dataclasses import dataclass
 from typing import Sequence
 
@@ -167,6 +168,93 @@ class PackedTreeMetadata:
             cursor += mask.shape[0]
         return cls._assemble(prefixes, tables, slot_lists, masks, int(block_size), ids,
                              torch.device(device), validate_slots=False)
+
+    @classmethod
+    def from_parents_device(cls, prefix_lens, block_tables, parents, arena_blocks, block_size,
+                            *, device, request_ids=None) -> "PackedTreeMetadata":
+        """from_host_trees' metadata, derived on the device from compact topology.
+
+        Uploads node counts, prefix lengths, block tables, parents and the arena pages
+        as one int32 buffer (about 4 bytes per node instead of 4 T^2 bytes of bias per
+        request) and builds cu_seqlens_q, query_to_request, query_local_row, tree_slots,
+        qq_bias and qq_bias_offsets with one launch of jt_metadata_build_launch; the
+        prefix lengths, node counts and block tables are views of the uploaded buffer.
+        Node j's scratch slot is the j-th slot of the packed arena pages, as in
+        from_host_trees.  Host-side checks: tight canonical tables, parents in
+        topological order, enough arena pages, no arena page inside a prefix.
+        """
+        from . import _launch, _lib
+
+        prefixes = tuple(int(v) for v in prefix_lens)
+        tables = tuple(tuple(int(v) for v in table) for table in block_tables)
+        parent_lists = [[int(v) for v in p] for p in parents]
+        count = len(prefixes)
+        ids = tuple(range(count)) if request_ids is None else tuple(request_ids)
+        if not count or not (len(tables) == len(parent_lists) == len(ids) == count):
+            raise ValueError("packed metadata request lists must align")
+        if block_size <= 0 or any(v < 0 for v in prefixes) or len(set(ids)) != count:
+            raise ValueError("invalid packed prefix geometry or duplicate request ID")
+        for prefix, table in zip(prefixes, tables):
+            if (len(table) != (prefix + block_size - 1) // block_size or
+                    len(set(table)) != len(table) or any(v < 0 for v in table)):
+                raise ValueError("prefix block table must be a tight canonical page table")
+        for plist in parent_lists:
+            if not plist or plist[0] != -1 or any(not 0 <= p < j for j, p in enumerate(plist) if j):
+                raise ValueError("tree parents must start at a root (-1) and precede their children")
+        counts = [len(p) for p in parent_lists]
+        if max(counts) > 1024:
+            raise ValueError("trees are limited to 1024 nodes")
+        total = sum(counts)
+        pages = tuple(int(v) for v in arena_blocks)
+        if (len(pages) * block_size < total or len(set(pages)) != len(pages) or
+                any(v < 0 for v in pages)):
+            raise ValueError("invalid or insufficient scratch page ownership")
+        if set(pages).intersection(v for table in tables for v in table):
+            raise ValueError("scratch pages overlap a live committed prefix")
+        width = max(1, max(len(t) for t in tables))
+        padded = [v for t in tables for v in (*t, *([-1] * (width - len(t))))]
+        host = [*counts, *prefixes, *padded, *(p for plist in parent_lists for p in plist), *pages]
+        device = torch.device(device)
+        staged = torch.tensor(host, dtype=torch.int32).to(device)   # the one upload
+        cursor = 0
+
+        def take(n):
+            nonlocal cursor
+            view = staged[cursor:cursor + n]
+            cursor += n
+            return view
+
+        node_counts, prefix_lens_d = take(count), take(count)
+        block_tables_d, parents_d, pages_d = take(count * width), take(total), take(len(pages))
+        bias_offsets = [0]
+        offsets = [0]
+        for c in counts:
+            offsets.append(offsets[-1] + c)
+            bias_offsets.append(bias_offsets[-1] + c * c)
+        out = dict(
+            cu_seqlens_q=torch.empty(count + 1, dtype=torch.int32, device=device),
+            query_to_request=torch.empty(total, dtype=torch.int32, device=device),
+            query_local_row=torch.empty(total, dtype=torch.int32, device=device),
+            tree_slots=torch.empty(total, dtype=torch.int64, device=device),
+            qq_bias=torch.empty(bias_offsets[-1], dtype=torch.float32, device=device),
+            qq_bias_offsets=torch.empty(count + 1, dtype=torch.int64, device=device))
+        p = _lib.JtMetadataBuildParams()
+        p.node_counts, p.parents, p.arena_pages = (node_counts.data_ptr(), parents_d.data_ptr(),
+                                                   pages_d.data_ptr())
+        for name, tensor in out.items():
+            setattr(p, name, tensor.data_ptr())
+        p.num_requests, p.block_size, p.max_nodes = count, int(block_size), max(counts)
+        lib = _lib.load_library()
+        _lib.check(lib.jt_metadata_build_launch(ctypes.byref(p), _launch.stream_handle(device)))
+        slots = tuple(pages[j // block_size] * block_size + j % block_size for j in range(total))
+        return cls(
+            cu_seqlens_q=out["cu_seqlens_q"], query_to_request=out["query_to_request"],
+            query_local_row=out["query_local_row"], prefix_lens=prefix_lens_d,
+            block_tables=block_tables_d.view(count, width), tree_slots=out["tree_slots"],
+            qq_bias=out["qq_bias"], qq_bias_offsets=out["qq_bias_offsets"],
+            node_counts=node_counts, block_size=int(block_size), prefix_lengths=prefixes,
+            query_offsets=tuple(offsets), node_counts_host=tuple(counts),
+            block_tables_host=tables, tree_slot_ids=slots, request_ids=ids)
 
     @classmethod
     def from_parents(cls, prefix_lens, block_tables, parents, tree_slots, block_size, *,
