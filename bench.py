@@ -208,6 +208,38 @@ def run_reference(args, rank: int, world: int):
 
 
 # ---- the reference's own GPU kernels on this GPU ---------------------------------------
+def reference_gpu_attention(step, device, reps: int = 5):
+    """The reference's Triton GQA kernel (tree_gqa.py:114-140, installed under
+    baseline/_ref) on this step's inputs, timed like the bench's attention launch (CUDA
+    events, median of a few calls), beside ours; informational."""
+    ref_root = ROOT / "baseline" / "_ref"
+    if not (ref_root / "nanovllm").is_dir():
+        return {"unavailable": "reference package not installed under baseline/_ref"}
+    try:
+        sys.path.insert(0, str(ref_root))
+        from nanovllm.speculative.jetspec.tree_gqa import packed_tree_attention_gqa as ref_gqa
+
+        def median_ms(fn):
+            fn()
+            torch.cuda.synchronize(device)
+            times = []
+            for _ in range(reps):
+                s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                s.record()
+                fn()
+                e.record()
+                torch.cuda.synchronize(device)
+                times.append(s.elapsed_time(e))
+            return statistics.median(times)
+
+        ref_ms = median_ms(lambda: ref_gqa(step.q, step.k_pool, step.v_pool, step.meta,
+                                           step.scale, GROUPS))
+        ours_ms = median_ms(step.attend)
+        return {"kernel": "reference packed_tree_attention_gqa (Triton)", "ms": ref_ms,
+                "ours_ms": ours_ms, "speedup_of_ours": ref_ms / ours_ms}
+    except Exception as exc:  # noqa: BLE001 - informational only
+        return {"unavailable": f"{type(exc).__name__}: {exc}"[:200]}
+
 def run_reference_triton(args, rank: int):
     """Reference Triton kernels and ours on the same inputs (attention launch only).
 
@@ -637,6 +669,8 @@ def main():
             }
             if cpu is not None:
                 line["cpu_baseline"] = cpu
+            if not args.no_cpu_baseline:
+                line["reference_gpu"] = reference_gpu_attention(step, device)
             print(json.dumps(line), flush=True)
     finally:
         if world > 1:
