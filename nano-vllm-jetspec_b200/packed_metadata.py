@@ -187,10 +187,10 @@ class PackedTreeMetadata:
 
         prefixes = tuple(int(v) for v in prefix_lens)
         tables = tuple(tuple(int(v) for v in table) for table in block_tables)
-        parent_lists = [[int(v) for v in p] for p in parents]
+        parent_arrays = [np.asarray(p, dtype=np.int64).reshape(-1) for p in parents]
         count = len(prefixes)
         ids = tuple(range(count)) if request_ids is None else tuple(request_ids)
-        if not count or not (len(tables) == len(parent_lists) == len(ids) == count):
+        if not count or not (len(tables) == len(parent_arrays) == len(ids) == count):
             raise ValueError("packed metadata request lists must align")
         if block_size <= 0 or any(v < 0 for v in prefixes) or len(set(ids)) != count:
             raise ValueError("invalid packed prefix geometry or duplicate request ID")
@@ -198,13 +198,21 @@ class PackedTreeMetadata:
             if (len(table) != (prefix + block_size - 1) // block_size or
                     len(set(table)) != len(table) or any(v < 0 for v in table)):
                 raise ValueError("prefix block table must be a tight canonical page table")
-        for plist in parent_lists:
-            if not plist or plist[0] != -1 or any(not 0 <= p < j for j, p in enumerate(plist) if j):
-                raise ValueError("tree parents must start at a root (-1) and precede their children")
-        counts = [len(p) for p in parent_lists]
+        counts = [int(p.size) for p in parent_arrays]
+        if min(counts) < 1:
+            raise ValueError("tree parents must start at a root (-1) and precede their children")
         if max(counts) > 1024:
             raise ValueError("trees are limited to 1024 nodes")
         total = sum(counts)
+        # Vectorised topology check: local index j of every node, its parent p; the root
+        # (j = 0) needs p = -1, every other node 0 <= p < j.
+        flat_parents = np.concatenate(parent_arrays)
+        local = np.arange(total, dtype=np.int64) - np.repeat(
+            np.cumsum([0] + counts[:-1], dtype=np.int64), counts)
+        root = local == 0
+        if (np.any(flat_parents[root] != -1) or
+                np.any((flat_parents[~root] < 0) | (flat_parents[~root] >= local[~root]))):
+            raise ValueError("tree parents must start at a root (-1) and precede their children")
         pages = tuple(int(v) for v in arena_blocks)
         if (len(pages) * block_size < total or len(set(pages)) != len(pages) or
                 any(v < 0 for v in pages)):
@@ -212,10 +220,13 @@ class PackedTreeMetadata:
         if set(pages).intersection(v for table in tables for v in table):
             raise ValueError("scratch pages overlap a live committed prefix")
         width = max(1, max(len(t) for t in tables))
-        padded = [v for t in tables for v in (*t, *([-1] * (width - len(t))))]
-        host = [*counts, *prefixes, *padded, *(p for plist in parent_lists for p in plist), *pages]
+        padded = np.full((count, width), -1, dtype=np.int64)
+        for row, table in enumerate(tables):
+            padded[row, :len(table)] = table
+        host = np.concatenate((np.asarray(counts, dtype=np.int64), np.asarray(prefixes, dtype=np.int64),
+                               padded.reshape(-1), flat_parents, np.asarray(pages, dtype=np.int64)))
         device = torch.device(device)
-        staged = torch.tensor(host, dtype=torch.int32).to(device)   # the one upload
+        staged = torch.from_numpy(host.astype(np.int32)).to(device)   # the one upload
         cursor = 0
 
         def take(n):
@@ -246,7 +257,9 @@ class PackedTreeMetadata:
         p.num_requests, p.block_size, p.max_nodes = count, int(block_size), max(counts)
         lib = _lib.load_library()
         _lib.check(lib.jt_metadata_build_launch(ctypes.byref(p), _launch.stream_handle(device)))
-        slots = tuple(pages[j // block_size] * block_size + j % block_size for j in range(total))
+        node = np.arange(total, dtype=np.int64)
+        slots = tuple((np.asarray(pages, dtype=np.int64)[node // block_size] * block_size +
+                       node % block_size).tolist())
         return cls(
             cu_seqlens_q=out["cu_seqlens_q"], query_to_request=out["query_to_request"],
             query_local_row=out["query_local_row"], prefix_lens=prefix_lens_d,
