@@ -245,6 +245,9 @@ typedef struct JtAcceptWalkParams {
   int64_t logits_stride0;          /* elements between logits rows                        */
   int32_t logits_dtype;            /* JT_BF16, JT_F16 or JT_F32                           */
   int32_t vocab, num_requests, max_depth, path_stride;  /* path_stride >= max_depth + 1  */
+  int32_t num_nodes;               /* Q: rows of logits / entries of the node arrays; a
+                                      request whose offsets leave [0, Q] is skipped and
+                                      flagged (device error bit 0)                      */
 } JtAcceptWalkParams;
 
 int jt_accept_walk_launch(const JtAcceptWalkParams* params, cudaStream_t stream);
@@ -272,6 +275,8 @@ typedef struct JtMetadataBuildParams {
   int64_t* qq_bias_offsets;    /* [R + 1]                                           */
   int32_t num_requests, block_size;
   int32_t max_nodes;           /* max T_r (<= 1024): sizes the kernel's shared memory */
+  int32_t num_nodes;           /* Q = sum of node_counts (entries of parents)        */
+  int32_t num_pages;           /* entries of arena_pages; ceil(Q / block_size) needed */
 } JtMetadataBuildParams;
 
 int jt_metadata_build_launch(const JtMetadataBuildParams* params, cudaStream_t stream);

@@ -123,6 +123,7 @@ class JtAcceptWalkParams(ctypes.Structure):
         ("accepted_length", c_void_p), ("correction", c_void_p), ("outputs", c_void_p),
         ("logits_stride0", c_i64), ("logits_dtype", c_i32), ("vocab", c_i32),
         ("num_requests", c_i32), ("max_depth", c_i32), ("path_stride", c_i32),
+        ("num_nodes", c_i32),
     ]
 
 
@@ -132,7 +133,7 @@ class JtMetadataBuildParams(ctypes.Structure):
         ("cu_seqlens_q", c_void_p), ("query_to_request", c_void_p),
         ("query_local_row", c_void_p), ("tree_slots", c_void_p), ("qq_bias", c_void_p),
         ("qq_bias_offsets", c_void_p), ("num_requests", c_i32), ("block_size", c_i32),
-        ("max_nodes", c_i32),
+        ("max_nodes", c_i32), ("num_nodes", c_i32), ("num_pages", c_i32),
     ]
 
 

@@ -66,6 +66,7 @@ def accept_walk(logits: torch.Tensor, token_ids: torch.Tensor, parent_indices: t
     p.logits_dtype = _launch.DTYPE_CODES[logits.dtype]
     p.vocab, p.num_requests = logits.shape[1], requests
     p.max_depth, p.path_stride = int(max_depth), width
+    p.num_nodes = nodes
     lib = _lib.load_library()
     _lib.check(lib.jt_accept_walk_launch(ctypes.byref(p), _launch.stream_handle(device)))
     return path, accepted, correction, outputs
@@ -102,6 +103,10 @@ def accept_batch(logits, trees, offsets, max_depth):
     0, 1, 2, ... (the reference's check).
     """
     device = logits.device
+    offsets = [int(o) for o in offsets]
+    if (len(offsets) != len(trees) + 1 or offsets[0] != 0 or offsets[-1] != logits.shape[0] or
+            any(b - a != int(t.num_nodes) for a, b, t in zip(offsets, offsets[1:], trees))):
+        raise ValueError("offsets must be the packed node offsets of the trees")
     token_ids = _packed([t.token_ids for t in trees], device)
     parents = _packed([t.parent_indices for t in trees], device)
     offs = torch.tensor(offsets, dtype=torch.int32, device=device)

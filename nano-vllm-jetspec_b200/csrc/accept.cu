@@ -154,7 +154,9 @@ __global__ void __launch_bounds__(kAcceptThreads)
   __shared__ int s_child;
   const int r = blockIdx.x, tid = threadIdx.x;
   const int lo = p.offsets[r], hi = p.offsets[r + 1];
-  const int nodes = hi - lo;
+  // A request outside [0, num_nodes] is treated as empty (skipped and flagged), so no
+  // row or node entry beyond the arrays is ever read.
+  const int nodes = (lo >= 0 && hi <= p.num_nodes) ? hi - lo : 0;
   int32_t* path = p.path + static_cast<int64_t>(r) * p.path_stride;
   int64_t* outputs = p.outputs + static_cast<int64_t>(r) * p.path_stride;
   for (int i = tid; i < p.path_stride; i += kAcceptThreads) {
@@ -222,7 +224,7 @@ int jt_read_errors_accept(uint32_t* bits) {
 extern "C" int jt_accept_walk_launch(const JtAcceptWalkParams* pp, cudaStream_t stream) {
   if (pp == nullptr) return jt_fail(JT_ERR_INVALID, "accept_walk: null params");
   const JtAcceptWalkParams& p = *pp;
-  if (p.num_requests < 1 || p.vocab < 1 || p.max_depth < 0 ||
+  if (p.num_requests < 1 || p.vocab < 1 || p.max_depth < 0 || p.num_nodes < 1 ||
       p.path_stride < p.max_depth + 1 || p.logits_stride0 < p.vocab)
     return jt_fail(JT_ERR_INVALID, "accept_walk: invalid geometry");
   if (!p.logits || !p.token_ids || !p.parent_indices || !p.offsets || !p.path ||

@@ -53,8 +53,11 @@ __global__ void __launch_bounds__(kMetaThreads)
       p.qq_bias_offsets[r + 1] = bias_off + static_cast<int64_t>(nodes) * nodes;
     }
   }
-  if (nodes < 1 || nodes > p.max_nodes) {
-    // The shared-memory rows are sized for max_nodes: such a request is skipped, flagged.
+  const int64_t pages_needed = (node_off + nodes + p.block_size - 1) / p.block_size;
+  if (nodes < 1 || nodes > p.max_nodes || node_off + nodes > p.num_nodes ||
+      pages_needed > p.num_pages) {
+    // The shared-memory rows are sized for max_nodes, and parents / arena pages must hold
+    // the request: otherwise it is skipped and flagged.
     if (tid == 0) atomicOr(&g_meta_errors, JT_DEVERR_TREE_TOO_LARGE);
     return;
   }
@@ -105,7 +108,8 @@ int jt_read_errors_meta(uint32_t* bits) {
 extern "C" int jt_metadata_build_launch(const JtMetadataBuildParams* pp, cudaStream_t stream) {
   if (pp == nullptr) return jt_fail(JT_ERR_INVALID, "metadata_build: null params");
   const JtMetadataBuildParams& p = *pp;
-  if (p.num_requests < 1 || p.block_size < 1 || p.max_nodes < 1 || p.max_nodes > 1024)
+  if (p.num_requests < 1 || p.block_size < 1 || p.max_nodes < 1 || p.max_nodes > 1024 ||
+      p.num_nodes < 1 || p.num_pages < 1)
     return jt_fail(JT_ERR_INVALID, "metadata_build: invalid geometry (1 <= max_nodes <= 1024)");
   if (!p.node_counts || !p.parents || !p.arena_pages || !p.cu_seqlens_q ||
       !p.query_to_request || !p.query_local_row || !p.tree_slots || !p.qq_bias ||

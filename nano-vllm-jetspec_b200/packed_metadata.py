@@ -255,6 +255,7 @@ class PackedTreeMetadata:
         for name, tensor in out.items():
             setattr(p, name, tensor.data_ptr())
         p.num_requests, p.block_size, p.max_nodes = count, int(block_size), max(counts)
+        p.num_nodes, p.num_pages = total, len(pages)
         lib = _lib.load_library()
         _lib.check(lib.jt_metadata_build_launch(ctypes.byref(p), _launch.stream_handle(device)))
         node = np.arange(total, dtype=np.int64)

@@ -132,3 +132,16 @@ def test_depth_zero_returns_root_and_its_greedy_token():
     assert (path[:, 0] == 0).all() and (accepted == 0).all()
     assert correction.cpu().tolist() == greedy[torch.from_numpy(z["offsets"][:-1]).long()].tolist()
     assert outputs[:, 0].cpu().tolist() == correction.cpu().tolist()
+
+
+def test_offsets_outside_the_nodes_are_skipped_and_flagged():
+    """A request whose offsets reach past the node arrays reads nothing beyond them."""
+    z = load_npz("accept.npz")
+    logits, tokens, parents, offsets, _ = _device_case(z, torch.float32)
+    jb.read_device_errors()
+    bad = torch.tensor([0, 5, logits.shape[0] + 10], dtype=torch.int32, device=DEV)
+    path, accepted, correction, _ = jb.accept_walk(logits, tokens, parents, bad, 4)
+    torch.cuda.synchronize()
+    assert int(accepted[1]) == -1 and (path[1] == -1).all()
+    assert int(accepted[0]) == int(z["accepted_length"][0])
+    assert jb.read_device_errors() & 1
