@@ -8,7 +8,7 @@ commit.  At N GPUs the global batch has N x 64 requests and every GPU owns 8/N o
 there is no collective on the data path, only the timing max-reduction).
 
     python bench.py [--gpus N] [--steps K] [--warmup W]
-                    [--impl ours|reference|reference-triton|accept-walk|metadata-build]
+                    [--impl ours|reference|reference-triton|accept-walk|metadata-build|row-linear]
 
 Rank 0 prints one JSON line.  ``--impl reference`` times the reference's CPU path (the
 oracle port of its masked-SDPA attention) on the host cores for the same workload.
@@ -49,12 +49,14 @@ def parse():
     parser.add_argument("--steps", type=int, default=200)
     parser.add_argument("--warmup", type=int, default=10)
     parser.add_argument("--impl", choices=("ours", "reference", "reference-triton", "accept-walk",
-                                           "metadata-build"),
+                                           "metadata-build", "row-linear"),
                         default="ours",
                         help="reference-triton: the reference's own Triton kernels (installed "
                              "under baseline/_ref) beside ours on configs 1-4, one GPU; "
                              "accept-walk: the round's acceptance step, reference vs device walk; "
-                             "metadata-build: round metadata, reference host build vs device build")
+                             "metadata-build: round metadata, reference host build vs device build; "
+                             "row-linear: the model's o_proj / down_proj (GEMM + all-reduce over "
+                             "the GPUs), reference F.linear + NCCL all_reduce vs the fused kernel")
     parser.add_argument("--requests-per-gpu", type=int, default=64)
     parser.add_argument("--no-cpu-baseline", action="store_true")
     parser.add_argument("--cpu-seconds", type=float, default=12.0,
@@ -470,6 +472,104 @@ def run_metadata_build(args, rank: int):
     print(json.dumps(line), flush=True)
 
 
+def run_row_linear(args, rank: int, world: int, local_rank: int):
+    """Config 5's row-parallel projections (Qwen3-8B o_proj 4096 -> 4096 and down_proj
+    12288 -> 4096; rows = 32 requests x 64 tree nodes) at tensor parallelism = the number
+    of GPUs: the reference's RowParallelLinear.forward (F.linear on the shard, then NCCL
+    all_reduce; its own class from baseline/_ref when installed) against the fused kernel,
+    on the same inputs.  Each timed call uses the next of several layers' weights and
+    inputs (more bytes than L2 in all), CUDA events on the launching stream, max over ranks."""
+    import torch.nn.functional as F
+    from jetspec_b200.row_linear import group_state_for, row_parallel_linear
+    device = torch.device("cuda", local_rank)
+    torch.cuda.set_device(device)
+    if world > 1:
+        torch.distributed.init_process_group("nccl", timeout=timedelta(seconds=300),
+                                             device_id=device)
+    reference_forward, ref_kind = None, "inline F.linear + all_reduce (baseline/_ref missing)"
+    ref_root = ROOT / "baseline" / "_ref"
+    if (ref_root / "nanovllm").is_dir() and world > 1:
+        sys.path.insert(0, str(ref_root))
+        from nanovllm.layers.linear import RowParallelLinear as RefRow
+        ref_kind = "nanovllm.layers.linear.RowParallelLinear.forward"
+    else:
+        RefRow = None
+        if world == 1:
+            ref_kind = "F.linear (RowParallelLinear.forward at tp_size 1: no all_reduce)"
+    state = group_state_for(device) if world > 1 else None
+    rows, hidden = 32 * 64, 4096
+    steps, warmup = max(args.steps, 1), max(args.warmup, 3)
+    result = {"impl": "row-linear", "n_gpus": world, "steps": steps, "warmup": warmup,
+              "rows": rows, "reference": ref_kind, "dtype": "bf16", "projections": {}}
+    peak = peaks()
+    try:
+        for name, fin in (("o_proj", 4096), ("down_proj", 12288)):
+            k = fin // world
+            layer_bytes = 2 * (rows * k + hidden * k)
+            layers = max(2, -(-300 * 2 ** 20 // layer_bytes))
+            gen = torch.Generator(device=device).manual_seed(77 + rank)
+            xs = [torch.randn(rows, k, generator=gen, device=device).bfloat16() for _ in range(layers)]
+            ws = [(torch.randn(hidden, k, generator=gen, device=device) / fin ** 0.5).bfloat16()
+                  for _ in range(layers)]
+            if RefRow is not None:
+                ref_layers = []
+                for w in ws:
+                    layer = RefRow.__new__(RefRow)
+                    torch.nn.Module.__init__(layer)
+                    layer.tp_rank, layer.tp_size, layer.tp_dim = rank, world, 1
+                    layer.weight = torch.nn.Parameter(w, requires_grad=False)
+                    layer.register_parameter("bias", None)
+                    ref_layers.append(layer)
+                reference_forward = lambda i: ref_layers[i](xs[i])  # noqa: E731
+            else:
+                def reference_forward(i):
+                    y = F.linear(xs[i], ws[i])
+                    if world > 1:
+                        torch.distributed.all_reduce(y)
+                    return y
+            ours = lambda i: row_parallel_linear(xs[i], ws[i], None, state)  # noqa: E731
+
+            def timed(fn):
+                with torch.no_grad():
+                    for i in range(warmup):
+                        fn(i % layers)
+                    if world > 1:
+                        torch.distributed.barrier()
+                    torch.cuda.synchronize(device)
+                    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                    start.record()
+                    for i in range(steps):
+                        fn(i % layers)
+                    end.record()
+                    torch.cuda.synchronize(device)
+                    if world > 1:
+                        torch.distributed.barrier()
+                ms = start.elapsed_time(end) / steps
+                return max_over_ranks([ms], world, device)[0]
+
+            with torch.no_grad():
+                diff = float((ours(0).float() - reference_forward(0).float()).abs().max())
+            ref_ms, our_ms = timed(reference_forward), timed(ours)
+            flops = 2.0 * rows * hidden * k
+            link_bytes = 2 * (world - 1) / world * rows * hidden * 2
+            bound_ms = max(flops / (peak["bf16_tflops"] * 1e12),
+                           link_bytes / 770e9) * 1e3
+            result["projections"][name] = {
+                "k_per_gpu": k, "layers_rotated": layers, "reference_ms": ref_ms, "ours_ms": our_ms,
+                "speedup": ref_ms / our_ms, "ours_tflops_per_gpu": flops / our_ms / 1e9,
+                "nvlink_bytes_per_gpu_each_way": link_bytes, "bound_ms": bound_ms,
+                "frac_of_bound": bound_ms / our_ms, "max_abs_diff_vs_reference": diff}
+        if rank == 0:
+            result["peak_bf16_tflops"] = peak["bf16_tflops"]
+            result["errors"] = jb.read_device_errors()
+            print(json.dumps(result), flush=True)
+    finally:
+        if state is not None:
+            state.close()
+        if world > 1:
+            torch.distributed.destroy_process_group()
+
+
 # ---- GPU side -------------------------------------------------------------------------
 class Step:
     """Device-resident inputs of one verify step on this rank's KV-head shard."""
@@ -653,6 +753,8 @@ def main():
         return run_accept_walk(args, rank)
     if args.impl == "metadata-build":
         return run_metadata_build(args, rank)
+    if args.impl == "row-linear":
+        return run_row_linear(args, rank, world, local_rank)
     if world != args.gpus and "WORLD_SIZE" in os.environ:
         args.gpus = world
     device = torch.device("cuda", local_rank)

@@ -282,6 +282,49 @@ typedef struct JtMetadataBuildParams {
 int jt_metadata_build_launch(const JtMetadataBuildParams* params, cudaStream_t stream);
 
 /*
+ * Row-parallel linear with its all-reduce fused in: out = sum over the group's ranks of
+ * x_r W_r^T (+ bias, added once).  Replaces RowParallelLinear.forward
+ * (nanovllm/layers/linear.py:153-156: F.linear on the rank's input shard with the bias on
+ * rank 0 only, then dist.all_reduce of the [M, N] result), used by the Qwen3 o_proj and
+ * down_proj.  One launch per rank, on each rank's own GPU; every rank of the group makes
+ * the same call (same m, n, k, dtype, epoch).  x [m, k] (row stride x_stride), weight
+ * [n, k] (nn.Linear layout, row stride w_stride), out [m, n] contiguous, bias [n] or NULL;
+ * bf16 or f16; n a multiple of 32, k a multiple of 8.  For world > 1, workspaces[r] is
+ * rank r's workspace (jt_row_linear_workspace_size bytes, zeroed once when allocated,
+ * 256-byte aligned) as this process addresses it (its own, and the peers' opened through
+ * jt_ipc_open_handle); epoch starts at 1 and grows by one per call of the group.  A
+ * rank whose peers do not arrive within wait_limit_cycles (0: about ten seconds) flags
+ * device error bit 2 and leaves its output incomplete.
+ */
+typedef struct JtRowLinearParams {
+  const void* x;
+  const void* weight;
+  const void* bias;          /* [n] or NULL; only rank 0's is added                   */
+  void* out;
+  int64_t m, n, k;
+  int64_t x_stride, w_stride;
+  int32_t dtype;             /* JT_BF16 or JT_F16                                     */
+  int32_t rank, world;       /* 1 <= world <= 8                                       */
+  void* const* workspaces;   /* [world], or NULL when world == 1                      */
+  uint32_t epoch;
+  int64_t wait_limit_cycles;
+} JtRowLinearParams;
+
+int jt_row_linear_launch(const JtRowLinearParams* params, cudaStream_t stream);
+/* Bytes of one rank's exchange workspace (0 for world == 1, -1 for invalid sizes). */
+int64_t jt_row_linear_workspace_size(int64_t m, int64_t n, int32_t world);
+/* Test form on one GPU: one cooperative launch plays every rank of a group whose inputs,
+ * outputs and workspaces all live on the current device; ranks[i].rank == i. */
+int jt_row_linear_emulate(const JtRowLinearParams* ranks, int32_t count, cudaStream_t stream);
+/* Workspace plumbing: a zeroed cudaMalloc allocation (its IPC handle maps its first byte),
+ * and the CUDA IPC handle exchange between the ranks' processes (64-byte handles). */
+int jt_device_alloc_zeroed(int64_t bytes, void** ptr);
+int jt_device_free(void* ptr);
+int jt_ipc_get_handle(const void* ptr, void* handle);
+int jt_ipc_open_handle(const void* handle, void** ptr);
+int jt_ipc_close_handle(void* ptr);
+
+/*
  * Failure detection without a GPU fault: runs one thread that waits, with the kernels'
  * bounded-wait routine and a limit of limit_cycles, on an mbarrier nothing arrives on.
  * Synchronous (diagnostics).  out[0] = 1 if the wait claimed completion (a failure),

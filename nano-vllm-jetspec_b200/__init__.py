@@ -11,6 +11,7 @@ verifier, scratch arena and block tables work unchanged:
 * rope_scatter(_prevalidated) - nanovllm/speculative/jetspec/tree_fusion.py:172-199
 * accept_batch               - nanovllm/speculative/jetspec/serving_ops.py:55 (plus the
                                device-side accept_walk)
+* RowParallelLinear          - nanovllm/layers/linear.py:131 (GEMM + all-reduce fused)
 
 All compute runs in libjetspec_b200.so (hand-written CUDA for sm_100a) through a C ABI
 (include/jetspec_b200.h).  There is no CPU or library fallback: without the built
@@ -20,6 +21,7 @@ from ._lib import KernelLaunchError, LibraryMissingError, load_library, read_dev
 from .accept import accept_batch, accept_walk
 from .attention import store_kvcache
 from .packed_metadata import PackedTreeMetadata, ancestor_mask_from_parents
+from .row_linear import RowParallelLinear, row_parallel_linear
 from .paged_backend import packed_tree_attention, packed_tree_attention_reference
 from .sharding import KvHeadShard, shard_for_rank
 from .state import _slots_for_blocks, copy_accepted_kv
@@ -32,4 +34,5 @@ __all__ = [
     "packed_tree_attention", "packed_tree_attention_reference", "KvHeadShard",
     "shard_for_rank", "copy_accepted_kv", "scatter_tree_kv", "rope_scatter",
     "rope_scatter_prevalidated", "packed_tree_attention_gqa", "accept_batch", "accept_walk",
+    "RowParallelLinear", "row_parallel_linear",
 ]

@@ -32,6 +32,14 @@ EXPORTED_SYMBOLS = (
     "jt_accept_walk_launch",
     "jt_selftest_bounded_wait",
     "jt_metadata_build_launch",
+    "jt_row_linear_launch",
+    "jt_row_linear_workspace_size",
+    "jt_row_linear_emulate",
+    "jt_device_alloc_zeroed",
+    "jt_device_free",
+    "jt_ipc_get_handle",
+    "jt_ipc_open_handle",
+    "jt_ipc_close_handle",
     "jt_kv_commit_max_slots",
     "jt_abi_version",
     "jt_last_error",
@@ -137,6 +145,16 @@ class JtMetadataBuildParams(ctypes.Structure):
     ]
 
 
+class JtRowLinearParams(ctypes.Structure):
+    _fields_ = [
+        ("x", c_void_p), ("weight", c_void_p), ("bias", c_void_p), ("out", c_void_p),
+        ("m", c_i64), ("n", c_i64), ("k", c_i64), ("x_stride", c_i64), ("w_stride", c_i64),
+        ("dtype", c_i32), ("rank", c_i32), ("world", c_i32),
+        ("workspaces", ctypes.POINTER(c_void_p)), ("epoch", c_u32),
+        ("wait_limit_cycles", c_i64),
+    ]
+
+
 _lock = threading.Lock()
 _lib = None
 
@@ -162,6 +180,22 @@ def _declare(lib):
     lib.jt_selftest_bounded_wait.restype = ctypes.c_int
     lib.jt_metadata_build_launch.argtypes = [P(JtMetadataBuildParams), c_void_p]
     lib.jt_metadata_build_launch.restype = ctypes.c_int
+    lib.jt_row_linear_launch.argtypes = [P(JtRowLinearParams), c_void_p]
+    lib.jt_row_linear_launch.restype = ctypes.c_int
+    lib.jt_row_linear_emulate.argtypes = [P(JtRowLinearParams), c_i32, c_void_p]
+    lib.jt_row_linear_emulate.restype = ctypes.c_int
+    lib.jt_row_linear_workspace_size.argtypes = [c_i64, c_i64, c_i32]
+    lib.jt_row_linear_workspace_size.restype = c_i64
+    lib.jt_device_alloc_zeroed.argtypes = [c_i64, P(c_void_p)]
+    lib.jt_device_alloc_zeroed.restype = ctypes.c_int
+    lib.jt_device_free.argtypes = [c_void_p]
+    lib.jt_device_free.restype = ctypes.c_int
+    lib.jt_ipc_get_handle.argtypes = [c_void_p, c_void_p]
+    lib.jt_ipc_get_handle.restype = ctypes.c_int
+    lib.jt_ipc_open_handle.argtypes = [c_void_p, P(c_void_p)]
+    lib.jt_ipc_open_handle.restype = ctypes.c_int
+    lib.jt_ipc_close_handle.argtypes = [c_void_p]
+    lib.jt_ipc_close_handle.restype = ctypes.c_int
     lib.jt_kv_commit_max_slots.argtypes = []
     lib.jt_kv_commit_max_slots.restype = c_i32
     lib.jt_abi_version.argtypes = []

@@ -39,6 +39,9 @@ extern "C" int jt_read_device_errors(uint32_t* errors) {
   if (rc != JT_OK) return rc;
   rc = jt_read_errors_meta(&e);
   if (rc != JT_OK) return rc;
-  *errors = a | b | c | d | e;
+  uint32_t f = 0;
+  rc = jt_read_errors_rowlin(&f);
+  if (rc != JT_OK) return rc;
+  *errors = a | b | c | d | e | f;
   return JT_OK;
 }

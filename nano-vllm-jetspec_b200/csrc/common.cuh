@@ -21,6 +21,7 @@ int jt_read_errors_attn(uint32_t* bits);
 int jt_read_errors_rope(uint32_t* bits);
 int jt_read_errors_accept(uint32_t* bits);
 int jt_read_errors_meta(uint32_t* bits);
+int jt_read_errors_rowlin(uint32_t* bits);
 
 #define JT_DEVERR_OUT_OF_RANGE 1u
 #define JT_DEVERR_TREE_TOO_LARGE 2u

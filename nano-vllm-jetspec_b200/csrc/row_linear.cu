@@ -1,0 +1,724 @@
+// Row-parallel linear with its all-reduce fused in: y = sum over ranks of x_r W_r^T (+ bias).
+//
+// The reference's RowParallelLinear.forward (nanovllm/layers/linear.py:153-156) runs
+// F.linear on this rank's input shard (bias on rank 0 only) and then dist.all_reduce on
+// the [M, N] result; the Qwen3 o_proj (qwen3.py:59, :97 ... :302) and down_proj (:334,
+// :345) are its callers.  Here one persistent kernel per GPU does both:
+//
+//   warp 0      TMA producer: x [128 rows x 64 K] and W [256 rows x 64 K] tiles, 128-byte
+//               swizzle, into a 4-stage ring (48 KB per stage)
+//   warp 1      tcgen05.mma issuer (kind::f16, M128 N256 K16) and TMEM owner; two 256-column
+//               fp32 accumulators so one tile's epilogue overlaps the next tile's MMAs
+//   warps 2-5   epilogue: TMEM -> registers -> bf16/f16 partial tile, stored straight into
+//               the tile owner's receive slot (a peer GPU's memory over NVLink, or this
+//               GPU's), then a release flag in the owner's memory
+//   warps 6-9   exchange: for the tiles this rank owns (tile t belongs to rank t % world)
+//               wait for every rank's partial, sum them in fp32, round once, write the
+//               tile to this rank's output and to its result area and raise a done flag on
+//               every rank; then copy the tiles other ranks own from their result areas
+//               into this rank's output as each one is done
+//
+// The all-reduce therefore moves the reduce-scatter + all-gather volume ((world-1)/world of
+// the output out and back per rank) with plain peer stores and loads, tile by tile while
+// the GEMM is still running, and without a separate collective launch.  Flags carry the
+// call's epoch (the host increments it per call), so nothing is reset between calls; a
+// rank reuses its receive and result areas only after every rank finished reading them in
+// the previous call (each rank leaves a call only after all its output tiles are done, and
+// an owner writes a result only after every rank's next partial arrived).  Every wait is
+// bounded: a flag that does not arrive within the limit sets JT_DEVERR_TIMEOUT and the
+// exchange warps skip the rest of their work.  No load uses cluster multicast.
+//
+// With world == 1 the epilogue writes the output directly (plain F.linear).  For tests on
+// one GPU, one launch can play every rank of a group (jt_row_linear_emulate): its CTAs
+// are split between the ranks, each with its own inputs, and the launch is cooperative so
+// that all of them are resident at once (a CTA waits only on CTAs of the same launch).
+#include <cuda.h>
+#include <cudaTypedefs.h>
+#include <string.h>
+
+#include <algorithm>
+#include <type_traits>
+
+#include "common.cuh"
+
+namespace {
+
+__device__ uint32_t g_rowlin_errors;
+
+namespace rl {
+
+constexpr int kBM = 128, kBN = 256, kBK = 64;
+constexpr int kStages = 4;
+constexpr int kATileBytes = kBM * kBK * 2;  // 16 KB
+constexpr int kBTileBytes = kBN * kBK * 2;  // 32 KB
+constexpr int kStageBytes = kATileBytes + kBTileBytes;
+constexpr int kOffA = 0;
+constexpr int kOffB = kOffA + kStages * kATileBytes;
+constexpr int kOffBar = kOffB + kStages * kBTileBytes;
+constexpr int kOffMisc = kOffBar + 16 * 8;
+constexpr int kSmemBytes = kOffMisc + 64 + 1024;  // + alignment slack
+static_assert(kSmemBytes <= 227 * 1024, "shared memory per CTA");
+constexpr int kThreads = 320;
+constexpr int kTileElems = kBM * kBN;  // elements per partial / result tile
+constexpr int kMaxRanks = 8;
+constexpr long long kLocalWaitLimit = 4000000000ll;  // cycles per pipeline wait
+
+// Barriers.
+constexpr int kBarFull = 0;       // [kStages] TMA bytes
+constexpr int kBarEmpty = 4;      // [kStages] MMA commit
+constexpr int kBarAccFull = 8;    // [2] MMA commit after a tile's last K step
+constexpr int kBarAccEmpty = 10;  // [2] 4 epilogue warps
+constexpr int kBarDrain = 12;
+constexpr int kNumBars = 13;
+
+struct Args {
+  int64_t M, N, K;
+  int32_t world, ranks_in_launch, base_rank, grid_per_rank;
+  int32_t m_tiles, n_tiles, tiles, owned_max;
+  uint32_t epoch;
+  long long wait_limit;
+  const void* bias[kMaxRanks];   // per rank of this launch (nullptr: no bias)
+  void* out[kMaxRanks];          // per rank of this launch, [M, N] row-major
+  unsigned char* ws[kMaxRanks];  // per rank of the group, as addressable from this GPU
+};
+
+// Workspace of one rank: [ready: tiles x world u32][done: tiles u32] (256-byte aligned),
+// then the receive slots [owned_max][world][tile], then the result tiles [owned_max][tile].
+__host__ __device__ inline int64_t ws_flag_bytes(int tiles, int world) {
+  return ((static_cast<int64_t>(tiles) * (world + 1) * 4) + 255) / 256 * 256;
+}
+__host__ __device__ inline int64_t ws_recv_offset(int tiles, int world) {
+  return ws_flag_bytes(tiles, world);
+}
+__host__ __device__ inline int64_t ws_result_offset(int tiles, int world, int owned_max) {
+  return ws_recv_offset(tiles, world) +
+         static_cast<int64_t>(owned_max) * world * kTileElems * 2;
+}
+__host__ __device__ inline int64_t ws_total(int tiles, int world, int owned_max) {
+  return ws_result_offset(tiles, world, owned_max) +
+         static_cast<int64_t>(owned_max) * kTileElems * 2;
+}
+
+// ---- PTX wrappers --------------------------------------------------------------------
+__device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;\n" ::"r"(bar), "r"(count));
+}
+__device__ __forceinline__ void mbar_arrive(uint32_t bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];\n" ::"r"(bar) : "memory");
+}
+__device__ __forceinline__ void mbar_arrive_tx(uint32_t bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;\n" ::"r"(bar), "r"(bytes)
+               : "memory");
+}
+__device__ __forceinline__ bool mbar_try(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n"
+      " selp.u32 %0, 1, 0, p;\n}\n"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+// Bounded wait for the phase with the given parity; a wait that runs out flags a timeout.
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity) {
+  if (mbar_try(bar, parity)) return true;
+  const long long start = clock64();
+  for (;;) {
+    if (mbar_try(bar, parity)) return true;
+    if (clock64() - start > kLocalWaitLimit) {
+      atomicOr(&g_rowlin_errors, JT_DEVERR_TIMEOUT);
+      return false;
+    }
+  }
+}
+__device__ __forceinline__ void tc_fence_before() {
+  asm volatile("tcgen05.fence::before_thread_sync;\n" ::: "memory");
+}
+__device__ __forceinline__ void tc_fence_after() {
+  asm volatile("tcgen05.fence::after_thread_sync;\n" ::: "memory");
+}
+__device__ __forceinline__ void tc_commit_warp(uint32_t bar) {
+  asm volatile(
+      "{\n .reg .pred e;\n elect.sync _|e, 0xffffffff;\n"
+      " @e tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];\n}\n" ::"r"(
+          bar)
+      : "memory");
+}
+__device__ __forceinline__ void mma_ss_warp(uint32_t d, uint64_t a, uint64_t b, uint32_t idesc,
+                                            uint32_t acc) {
+  asm volatile(
+      "{\n .reg .pred p, e;\n setp.ne.b32 p, %4, 0;\n elect.sync _|e, 0xffffffff;\n"
+      " @e tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}\n" ::"r"(d),
+      "l"(a), "l"(b), "r"(idesc), "r"(acc));
+}
+// K-major operand in shared memory with the 128-byte swizzle: rows of 128 B, 8-row groups
+// 1024 B apart (descriptor version 1 for sm_100).
+__device__ __forceinline__ uint64_t smem_desc(uint32_t addr) {
+  uint64_t d = static_cast<uint64_t>((addr & 0x3FFFFu) >> 4);
+  d |= static_cast<uint64_t>(16u >> 4) << 16;
+  d |= static_cast<uint64_t>(1024u >> 4) << 32;
+  d |= 1ull << 46;
+  d |= 2ull << 61;
+  return d;
+}
+// kind::f16 instruction descriptor, fp32 accumulate, both operands K-major.
+__host__ __device__ constexpr uint32_t instr_desc(int m, int n, bool bf16) {
+  return (1u << 4) | ((bf16 ? 1u : 0u) << 7) | ((bf16 ? 1u : 0u) << 10) |
+         (static_cast<uint32_t>(n >> 3) << 17) | (static_cast<uint32_t>(m >> 4) << 24);
+}
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&v)[32]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,"
+      "%14,%15,%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];\n"
+      : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]),
+        "=r"(v[7]), "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]),
+        "=r"(v[14]), "=r"(v[15]), "=r"(v[16]), "=r"(v[17]), "=r"(v[18]), "=r"(v[19]),
+        "=r"(v[20]), "=r"(v[21]), "=r"(v[22]), "=r"(v[23]), "=r"(v[24]), "=r"(v[25]),
+        "=r"(v[26]), "=r"(v[27]), "=r"(v[28]), "=r"(v[29]), "=r"(v[30]), "=r"(v[31])
+      : "r"(taddr));
+}
+__device__ __forceinline__ void tmem_wait_ld() {
+  asm volatile("tcgen05.wait::ld.sync.aligned;\n" ::: "memory");
+}
+__device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map, int c0, int c1,
+                                            uint32_t bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%2, %3}], [%4];\n" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(bar)
+      : "memory");
+}
+__device__ __forceinline__ void named_sync(int id, int threads) {
+  asm volatile("bar.sync %0, %1;\n" ::"r"(id), "r"(threads) : "memory");
+}
+// Flags shared with other GPUs: release stores, acquire loads at system scope.
+__device__ __forceinline__ void st_release_sys(uint32_t* addr, uint32_t v) {
+  asm volatile("st.release.sys.global.u32 [%0], %1;\n" ::"l"(addr), "r"(v) : "memory");
+}
+__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* addr) {
+  uint32_t v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];\n" : "=r"(v) : "l"(addr) : "memory");
+  return v;
+}
+// Bounded wait until a flag reaches the epoch (flags only grow; a difference below 2^31
+// counts as reached).  Returns false, and flags a timeout, when the limit runs out or an
+// earlier wait of this CTA already did.
+__device__ __forceinline__ bool wait_flag(const uint32_t* flag, uint32_t epoch, long long limit,
+                                          volatile int* abort) {
+  if (static_cast<int>(ld_acquire_sys(flag) - epoch) >= 0) return true;
+  const long long start = clock64();
+  for (;;) {
+    if (static_cast<int>(ld_acquire_sys(flag) - epoch) >= 0) return true;
+    if (*abort) return false;
+    if (clock64() - start > limit) {
+      *abort = 1;
+      atomicOr(&g_rowlin_errors, JT_DEVERR_TIMEOUT);
+      return false;
+    }
+  }
+}
+
+template <bool kBf16>
+struct Conv;
+template <>
+struct Conv<true> {
+  __device__ __forceinline__ static uint32_t pack(float lo, float hi) {
+    __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
+    return *reinterpret_cast<uint32_t*>(&v);
+  }
+  __device__ __forceinline__ static float2 unpack(uint32_t v) {
+    return __bfloat1622float2(*reinterpret_cast<__nv_bfloat162*>(&v));
+  }
+};
+template <>
+struct Conv<false> {
+  __device__ __forceinline__ static uint32_t pack(float lo, float hi) {
+    __half2 v = __floats2half2_rn(lo, hi);
+    return *reinterpret_cast<uint32_t*>(&v);
+  }
+  __device__ __forceinline__ static float2 unpack(uint32_t v) {
+    return __half22float2(*reinterpret_cast<__half2*>(&v));
+  }
+};
+
+}  // namespace rl
+
+namespace rl {
+
+struct Maps {
+  CUtensorMap x[kMaxRanks];  // [M, K] input shard of each rank of this launch
+  CUtensorMap w[kMaxRanks];  // [N, K] weight shard of each rank of this launch
+};
+
+__device__ __forceinline__ uint32_t* ready_flags(unsigned char* ws) {
+  return reinterpret_cast<uint32_t*>(ws);
+}
+__device__ __forceinline__ uint32_t* done_flags(unsigned char* ws, int tiles, int world) {
+  return reinterpret_cast<uint32_t*>(ws) + static_cast<int64_t>(tiles) * world;
+}
+
+// 16-byte chunk `ch` (0..4095) of a partial / result tile: chunks are stored so that the
+// 32 lanes of an epilogue warp write 512 contiguous bytes (one row per lane, 8 columns per
+// chunk); this maps a chunk back to its row and first column inside the 128 x 256 tile.
+__device__ __forceinline__ void chunk_coords(int ch, int& row, int& col) {
+  const int lane = ch & 31, i = (ch >> 5) & 3, c = (ch >> 7) & 7, q = ch >> 10;
+  row = q * 32 + lane;
+  col = c * 32 + i * 8;
+}
+
+template <bool kBf16>
+__global__ void __launch_bounds__(kThreads, 1)
+    row_linear_kernel(const __grid_constant__ Args a, const __grid_constant__ Maps maps) {
+  using Cv = Conv<kBf16>;
+  constexpr uint32_t kIdesc = instr_desc(kBM, kBN, kBf16);
+  extern __shared__ unsigned char smem_raw[];
+  const uint32_t raw = jt::smem_u32(smem_raw);
+  const uint32_t base = (raw + 1023u) & ~1023u;
+  unsigned char* sbase = smem_raw + (base - raw);
+  const uint32_t bar0 = base + kOffBar;
+#define RL_BAR(i) (bar0 + 8u * static_cast<uint32_t>(i))
+  volatile int* misc = reinterpret_cast<volatile int*>(sbase + kOffMisc);
+  volatile int* abort = misc + 1;  // misc[0]: TMEM base
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int lr = blockIdx.x % a.ranks_in_launch;  // rank of this launch the CTA works for
+  const int cta = blockIdx.x / a.ranks_in_launch;
+  const int rank = a.base_rank + lr;
+  const int world = a.world;
+  const int k_blocks = static_cast<int>((a.K + kBK - 1) / kBK);
+
+  if (tid == 0) {
+    for (int i = 0; i < kNumBars; ++i)
+      mbar_init(RL_BAR(i), (i == kBarAccEmpty || i == kBarAccEmpty + 1) ? 4u : 1u);
+    misc[1] = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], 512;\n" ::"r"(
+                     base + kOffMisc)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;\n" ::: "memory");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = static_cast<uint32_t>(misc[0]);
+
+  if (warp == 0) {
+    // ---------------------------------------------------------------- TMA producer
+    if (lane == 0) {
+      uint32_t r = 0;
+      for (int t = cta; t < a.tiles; t += a.grid_per_rank) {
+        const int m0 = (t % a.m_tiles) * kBM, n0 = (t / a.m_tiles) * kBN;
+        for (int kb = 0; kb < k_blocks; ++kb, ++r) {
+          const int s = static_cast<int>(r % kStages);
+          mbar_wait(RL_BAR(kBarEmpty + s), ((r / kStages) & 1u) ^ 1u);
+          mbar_arrive_tx(RL_BAR(kBarFull + s), kStageBytes);
+          tma_load_2d(base + kOffA + s * kATileBytes, &maps.x[lr], kb * kBK, m0,
+                      RL_BAR(kBarFull + s));
+          tma_load_2d(base + kOffB + s * kBTileBytes, &maps.w[lr], kb * kBK, n0,
+                      RL_BAR(kBarFull + s));
+        }
+      }
+    }
+    __syncwarp();
+  } else if (warp == 1) {
+    // ---------------------------------------------------------------- MMA issuer
+    uint32_t r = 0, acc = 0;
+    const uint64_t adesc0 = smem_desc(base + kOffA), bdesc0 = smem_desc(base + kOffB);
+    for (int t = cta; t < a.tiles; t += a.grid_per_rank, ++acc) {
+      const int buf = static_cast<int>(acc & 1u);
+      mbar_wait(RL_BAR(kBarAccEmpty + buf), ((acc >> 1) & 1u) ^ 1u);
+      tc_fence_after();
+      const uint32_t d = tmem + static_cast<uint32_t>(buf * kBN);
+      for (int kb = 0; kb < k_blocks; ++kb, ++r) {
+        const int s = static_cast<int>(r % kStages);
+        mbar_wait(RL_BAR(kBarFull + s), (r / kStages) & 1u);
+        tc_fence_after();
+        const uint64_t ad = adesc0 + static_cast<uint64_t>((s * kATileBytes) >> 4);
+        const uint64_t bd = bdesc0 + static_cast<uint64_t>((s * kBTileBytes) >> 4);
+#pragma unroll
+        for (int kk = 0; kk < kBK / 16; ++kk)  // 16 K elements = 32 bytes along the row
+          mma_ss_warp(d, ad + 2 * kk, bd + 2 * kk, kIdesc, (kb > 0 || kk > 0) ? 1u : 0u);
+        tc_commit_warp(RL_BAR(kBarEmpty + s));
+      }
+      tc_commit_warp(RL_BAR(kBarAccFull + buf));
+    }
+    // Drain: every MMA this warp issued has completed before TMEM is released.
+    tc_commit_warp(RL_BAR(kBarDrain));
+    mbar_wait(RL_BAR(kBarDrain), 0);
+  } else if (warp < 6) {
+    // ---------------------------------------------------------------- epilogue
+    const int q = warp & 3;  // TMEM lane quadrant this warp may read
+    const int row = q * 32 + lane;
+    const uint16_t* bias = static_cast<const uint16_t*>(a.bias[lr]);
+    uint32_t acc = 0;
+    for (int t = cta; t < a.tiles; t += a.grid_per_rank, ++acc) {
+      const int buf = static_cast<int>(acc & 1u);
+      const int m0 = (t % a.m_tiles) * kBM, n0 = (t / a.m_tiles) * kBN;
+      const int owner = t % world, j = t / world;
+      mbar_wait(RL_BAR(kBarAccFull + buf), (acc >> 1) & 1u);
+      tc_fence_after();
+      const int64_t m = m0 + row;
+      unsigned char* slot =
+          world == 1 ? nullptr
+                     : a.ws[owner] + ws_recv_offset(a.tiles, world) +
+                           (static_cast<int64_t>(j) * world + rank) * kTileElems * 2;
+#pragma unroll 1
+      for (int c = 0; c < kBN / 32; ++c) {
+        uint32_t v[32];
+        tmem_ld32(tmem + (static_cast<uint32_t>(q * 32) << 16) +
+                      static_cast<uint32_t>(buf * kBN + c * 32),
+                  v);
+        tmem_wait_ld();
+        const int64_t n = n0 + c * 32;
+        uint32_t packed[16];
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+          float lo = __uint_as_float(v[2 * i]), hi = __uint_as_float(v[2 * i + 1]);
+          if (bias != nullptr && n < a.N) {
+            const float2 b = Cv::unpack(*reinterpret_cast<const uint32_t*>(bias + n + 2 * i));
+            lo += b.x;
+            hi += b.y;
+          }
+          packed[i] = Cv::pack(lo, hi);
+        }
+        if (world == 1) {
+          if (m < a.M && n < a.N) {
+            uint4* o = reinterpret_cast<uint4*>(static_cast<unsigned char*>(a.out[lr]) +
+                                                (m * a.N + n) * 2);
+#pragma unroll
+            for (int i = 0; i < 4; ++i)
+              o[i] = make_uint4(packed[4 * i], packed[4 * i + 1], packed[4 * i + 2],
+                                packed[4 * i + 3]);
+          }
+        } else {
+          uint4* o = reinterpret_cast<uint4*>(slot) + (q * 8 + c) * 128 + lane;
+#pragma unroll
+          for (int i = 0; i < 4; ++i)
+            o[32 * i] = make_uint4(packed[4 * i], packed[4 * i + 1], packed[4 * i + 2],
+                                   packed[4 * i + 3]);
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(RL_BAR(kBarAccEmpty + buf));
+      if (world > 1) {
+        // Every epilogue thread's stores of this partial are visible system-wide before
+        // the owner's ready flag for (tile, this rank) is raised.
+        __threadfence_system();
+        named_sync(2, 128);
+        if (warp == 2 && lane == 0)
+          st_release_sys(ready_flags(a.ws[owner]) + static_cast<int64_t>(t) * world + rank,
+                         a.epoch);
+      }
+    }
+  } else if (world > 1) {
+    // ---------------------------------------------------------------- exchange
+    const int et = tid - 192;  // 0..127
+    unsigned char* mine = a.ws[rank];
+    const int64_t res_off = ws_result_offset(a.tiles, world, a.owned_max);
+    const int owned = (a.tiles - rank + world - 1) / world;  // tiles j * world + rank
+    for (int j = cta; j < owned; j += a.grid_per_rank) {
+      const int t = j * world + rank;
+      if (et < world)
+        wait_flag(ready_flags(mine) + static_cast<int64_t>(t) * world + et, a.epoch,
+                  a.wait_limit, abort);
+      named_sync(1, 128);
+      if (!*abort) {
+        const int m0 = (t % a.m_tiles) * kBM, n0 = (t / a.m_tiles) * kBN;
+        const uint4* slots = reinterpret_cast<const uint4*>(
+            mine + ws_recv_offset(a.tiles, world) +
+            static_cast<int64_t>(j) * world * kTileElems * 2);
+        uint4* result = reinterpret_cast<uint4*>(mine + res_off +
+                                                 static_cast<int64_t>(j) * kTileElems * 2);
+#pragma unroll 1
+        for (int c0 = et; c0 < kTileElems / 8; c0 += 4 * 128) {
+          float sum[4][8];
+#pragma unroll
+          for (int u = 0; u < 4; ++u)
+#pragma unroll
+            for (int e = 0; e < 8; ++e) sum[u][e] = 0.f;
+#pragma unroll 2
+          for (int s = 0; s < world; ++s) {
+            uint4 in[4];
+#pragma unroll
+            for (int u = 0; u < 4; ++u)
+              in[u] = __ldcg(slots + static_cast<int64_t>(s) * (kTileElems / 8) + c0 + 128 * u);
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+              const uint32_t w4[4] = {in[u].x, in[u].y, in[u].z, in[u].w};
+#pragma unroll
+              for (int e = 0; e < 4; ++e) {
+                const float2 f = Cv::unpack(w4[e]);
+                sum[u][2 * e] += f.x;
+                sum[u][2 * e + 1] += f.y;
+              }
+            }
+          }
+#pragma unroll
+          for (int u = 0; u < 4; ++u) {
+            const int ch = c0 + 128 * u;
+            const uint4 o = make_uint4(Cv::pack(sum[u][0], sum[u][1]), Cv::pack(sum[u][2], sum[u][3]),
+                                       Cv::pack(sum[u][4], sum[u][5]), Cv::pack(sum[u][6], sum[u][7]));
+            result[ch] = o;
+            int row, col;
+            chunk_coords(ch, row, col);
+            const int64_t m = m0 + row, n = n0 + col;
+            if (m < a.M && n < a.N)
+              *reinterpret_cast<uint4*>(static_cast<unsigned char*>(a.out[lr]) +
+                                        (m * a.N + n) * 2) = o;
+          }
+        }
+      }
+      __threadfence_system();
+      named_sync(1, 128);
+      if (et < world && !*abort)
+        st_release_sys(done_flags(a.ws[et], a.tiles, world) + t, a.epoch);
+    }
+    // Tiles other ranks own: copy each into this rank's output once its owner is done.
+    uint32_t* done = done_flags(mine, a.tiles, world);
+    for (int t = cta; t < a.tiles; t += a.grid_per_rank) {
+      const int owner = t % world;
+      if (owner == rank) continue;
+      if (et == 0) wait_flag(done + t, a.epoch, a.wait_limit, abort);
+      named_sync(1, 128);
+      if (*abort) continue;
+      const int m0 = (t % a.m_tiles) * kBM, n0 = (t / a.m_tiles) * kBN;
+      const uint4* src = reinterpret_cast<const uint4*>(
+          a.ws[owner] + res_off + static_cast<int64_t>(t / world) * kTileElems * 2);
+#pragma unroll 1
+      for (int c0 = et; c0 < kTileElems / 8; c0 += 8 * 128) {
+        uint4 v[8];
+#pragma unroll
+        for (int u = 0; u < 8; ++u) v[u] = __ldcg(src + c0 + 128 * u);
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+          int row, col;
+          chunk_coords(c0 + 128 * u, row, col);
+          const int64_t m = m0 + row, n = n0 + col;
+          if (m < a.M && n < a.N)
+            *reinterpret_cast<uint4*>(static_cast<unsigned char*>(a.out[lr]) +
+                                      (m * a.N + n) * 2) = v[u];
+        }
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, 512;\n" ::"r"(tmem)
+                 : "memory");
+  }
+#undef RL_BAR
+}
+
+}  // namespace rl
+
+PFN_cuTensorMapEncodeTiled_v12000 rl_tensor_map_encoder() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  if (fn == nullptr) {
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult query{};
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &query) ==
+            cudaSuccess &&
+        query == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(ptr);
+  }
+  return fn;
+}
+
+// 2-D K-major map [rows, cols] (row stride in elements) with a 64-column x box_rows box and
+// the 128-byte swizzle; elements outside the matrix read as zero.
+bool encode_kmajor(CUtensorMap* map, const void* ptr, int32_t dtype, int64_t rows, int64_t cols,
+                   int64_t row_stride, int box_rows) {
+  auto encode = rl_tensor_map_encoder();
+  if (encode == nullptr) return false;
+  const cuuint64_t dims[2] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(rows)};
+  const cuuint64_t strides[1] = {static_cast<cuuint64_t>(row_stride * 2)};
+  const cuuint32_t box[2] = {static_cast<cuuint32_t>(rl::kBK), static_cast<cuuint32_t>(box_rows)};
+  const cuuint32_t elem[2] = {1, 1};
+  return encode(map,
+                dtype == JT_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
+                                 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16,
+                2, const_cast<void*>(ptr), dims, strides, box, elem,
+                CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+bool al16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+int rl_tiles(int64_t m, int64_t n, int* m_tiles, int* n_tiles) {
+  const int64_t mt = (m + rl::kBM - 1) / rl::kBM, nt = (n + rl::kBN - 1) / rl::kBN;
+  if (mt * nt > (1ll << 30)) return jt_fail(JT_ERR_INVALID, "row_linear: output too large");
+  *m_tiles = static_cast<int>(mt);
+  *n_tiles = static_cast<int>(nt);
+  return JT_OK;
+}
+
+// Checks one rank's call (every check the kernel relies on) and encodes its maps.
+int rl_check_rank(const JtRowLinearParams& p, CUtensorMap* xmap, CUtensorMap* wmap) {
+  if (p.dtype != JT_BF16 && p.dtype != JT_F16)
+    return jt_fail(JT_ERR_INVALID, "row_linear: dtype must be bf16 or f16");
+  if (p.m < 1 || p.n < 32 || p.n % 32 != 0 || p.k < 8 || p.k % 8 != 0)
+    return jt_fail(JT_ERR_INVALID,
+                   "row_linear: need m >= 1, n a positive multiple of 32, k a positive multiple "
+                   "of 8 (m=%lld n=%lld k=%lld)",
+                   static_cast<long long>(p.m), static_cast<long long>(p.n),
+                   static_cast<long long>(p.k));
+  if (p.world < 1 || p.world > rl::kMaxRanks || p.rank < 0 || p.rank >= p.world)
+    return jt_fail(JT_ERR_INVALID, "row_linear: rank %d of world %d (1 <= world <= 8)", p.rank,
+                   p.world);
+  if (!p.x || !p.weight || !p.out)
+    return jt_fail(JT_ERR_INVALID, "row_linear: null x / weight / out");
+  if (!al16(p.x) || !al16(p.weight) || !al16(p.out) || (p.bias && (reinterpret_cast<uintptr_t>(p.bias) & 3u)))
+    return jt_fail(JT_ERR_INVALID, "row_linear: x, weight and out need 16-byte alignment");
+  if (p.x_stride < p.k || p.x_stride % 8 != 0 || p.w_stride < p.k || p.w_stride % 8 != 0)
+    return jt_fail(JT_ERR_INVALID,
+                   "row_linear: row strides must be >= k and multiples of 8 elements");
+  if (p.world > 1) {
+    if (p.workspaces == nullptr)
+      return jt_fail(JT_ERR_INVALID, "row_linear: world > 1 needs the ranks' workspaces");
+    for (int r = 0; r < p.world; ++r)
+      if (p.workspaces[r] == nullptr || (reinterpret_cast<uintptr_t>(p.workspaces[r]) & 255u))
+        return jt_fail(JT_ERR_INVALID, "row_linear: workspace %d null or not 256-byte aligned", r);
+  }
+  if (!encode_kmajor(xmap, p.x, p.dtype, p.m, p.k, p.x_stride, rl::kBM) ||
+      !encode_kmajor(wmap, p.weight, p.dtype, p.n, p.k, p.w_stride, rl::kBN))
+    return jt_fail(JT_ERR_CUDA, "row_linear: cuTensorMapEncodeTiled rejected x or weight");
+  return JT_OK;
+}
+
+// ranks[0..count) are the ranks this launch plays (count 1, or the whole group).
+int rl_launch(const JtRowLinearParams* ranks, int count, cudaStream_t stream) {
+  const JtRowLinearParams& p0 = ranks[0];
+  rl::Args a{};
+  rl::Maps maps{};
+  for (int i = 0; i < count; ++i) {
+    const JtRowLinearParams& p = ranks[i];
+    int rc = rl_check_rank(p, &maps.x[i], &maps.w[i]);
+    if (rc != JT_OK) return rc;
+    if (i > 0 && (p.m != p0.m || p.n != p0.n || p.k != p0.k || p.dtype != p0.dtype ||
+                  p.world != p0.world || p.epoch != p0.epoch || p.rank != p0.rank + i))
+      return jt_fail(JT_ERR_INVALID, "row_linear: emulated ranks must share the geometry and "
+                                     "be given in rank order");
+    a.bias[i] = p.rank == 0 ? p.bias : nullptr;  // the bias is added once, by rank 0
+    a.out[i] = p.out;
+  }
+  int m_tiles = 0, n_tiles = 0;
+  int rc = rl_tiles(p0.m, p0.n, &m_tiles, &n_tiles);
+  if (rc != JT_OK) return rc;
+  a.M = p0.m;
+  a.N = p0.n;
+  a.K = p0.k;
+  a.world = p0.world;
+  a.ranks_in_launch = count;
+  a.base_rank = p0.rank;
+  a.m_tiles = m_tiles;
+  a.n_tiles = n_tiles;
+  a.tiles = m_tiles * n_tiles;
+  a.owned_max = (a.tiles + a.world - 1) / a.world;
+  a.epoch = p0.epoch;
+  a.wait_limit = p0.wait_limit_cycles > 0 ? p0.wait_limit_cycles : 20000000000ll;
+  for (int r = 0; r < p0.world && p0.world > 1; ++r)
+    a.ws[r] = static_cast<unsigned char*>(p0.workspaces[r]);
+  int dev = 0, sms = 0;
+  rc = jt_cuda_check(cudaGetDevice(&dev), "row_linear: device");
+  if (rc != JT_OK) return rc;
+  rc = jt_cuda_check(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev),
+                     "row_linear: SM count");
+  if (rc != JT_OK) return rc;
+  if (sms < count) return jt_fail(JT_ERR_INVALID, "row_linear: more ranks than SMs");
+  a.grid_per_rank = std::min(a.tiles, sms / count);
+  auto kernel = p0.dtype == JT_BF16 ? rl::row_linear_kernel<true> : rl::row_linear_kernel<false>;
+  rc = jt_cuda_check(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                          rl::kSmemBytes),
+                     "row_linear: smem attribute");
+  if (rc != JT_OK) return rc;
+  // Cooperative: every CTA is resident at once (an exchange warp waits on other CTAs).
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = dim3(static_cast<unsigned>(a.grid_per_rank * count));
+  cfg.blockDim = dim3(rl::kThreads);
+  cfg.dynamicSmemBytes = rl::kSmemBytes;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeCooperative;
+  attr[0].val.cooperative = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return jt_cuda_check(cudaLaunchKernelEx(&cfg, kernel, a, maps), "row_linear launch");
+}
+
+}  // namespace
+
+int jt_read_errors_rowlin(uint32_t* bits) {
+  uint32_t zero = 0;
+  int rc = jt_cuda_check(cudaMemcpyFromSymbol(bits, g_rowlin_errors, sizeof(uint32_t)),
+                         "read row_linear error word");
+  if (rc != JT_OK) return rc;
+  return jt_cuda_check(cudaMemcpyToSymbol(g_rowlin_errors, &zero, sizeof(uint32_t)),
+                       "clear row_linear error word");
+}
+
+extern "C" int64_t jt_row_linear_workspace_size(int64_t m, int64_t n, int32_t world) {
+  if (m < 1 || n < 1 || world < 1 || world > rl::kMaxRanks) return -1;
+  if (world == 1) return 0;
+  int m_tiles = 0, n_tiles = 0;
+  if (rl_tiles(m, n, &m_tiles, &n_tiles) != JT_OK) return -1;
+  const int tiles = m_tiles * n_tiles;
+  return rl::ws_total(tiles, world, (tiles + world - 1) / world);
+}
+
+extern "C" int jt_row_linear_launch(const JtRowLinearParams* p, cudaStream_t stream) {
+  if (p == nullptr) return jt_fail(JT_ERR_INVALID, "row_linear: null params");
+  return rl_launch(p, 1, stream);
+}
+
+extern "C" int jt_row_linear_emulate(const JtRowLinearParams* ranks, int32_t count,
+                                     cudaStream_t stream) {
+  if (ranks == nullptr || count < 1 || count > rl::kMaxRanks)
+    return jt_fail(JT_ERR_INVALID, "row_linear_emulate: 1..8 rank params");
+  if (ranks[0].rank != 0 || ranks[0].world != count)
+    return jt_fail(JT_ERR_INVALID, "row_linear_emulate: give every rank of the group, rank 0 first");
+  return rl_launch(ranks, count, stream);
+}
+
+extern "C" int jt_device_alloc_zeroed(int64_t bytes, void** ptr) {
+  if (ptr == nullptr || bytes < 1) return jt_fail(JT_ERR_INVALID, "device_alloc: bad arguments");
+  *ptr = nullptr;
+  int rc = jt_cuda_check(cudaMalloc(ptr, static_cast<size_t>(bytes)), "device_alloc");
+  if (rc != JT_OK) return rc;
+  rc = jt_cuda_check(cudaMemset(*ptr, 0, static_cast<size_t>(bytes)), "device_alloc: zero");
+  if (rc != JT_OK) {
+    cudaFree(*ptr);
+    *ptr = nullptr;
+  }
+  return rc;
+}
+
+extern "C" int jt_device_free(void* ptr) {
+  return jt_cuda_check(cudaFree(ptr), "device_free");
+}
+
+extern "C" int jt_ipc_get_handle(const void* ptr, void* handle) {
+  if (ptr == nullptr || handle == nullptr) return jt_fail(JT_ERR_INVALID, "ipc_get_handle: null");
+  cudaIpcMemHandle_t h;
+  int rc = jt_cuda_check(cudaIpcGetMemHandle(&h, const_cast<void*>(ptr)), "ipc_get_handle");
+  if (rc != JT_OK) return rc;
+  memcpy(handle, &h, sizeof(h));
+  return JT_OK;
+}
+
+extern "C" int jt_ipc_open_handle(const void* handle, void** ptr) {
+  if (ptr == nullptr || handle == nullptr) return jt_fail(JT_ERR_INVALID, "ipc_open_handle: null");
+  cudaIpcMemHandle_t h;
+  memcpy(&h, handle, sizeof(h));
+  return jt_cuda_check(cudaIpcOpenMemHandle(ptr, h, cudaIpcMemLazyEnablePeerAccess),
+                       "ipc_open_handle");
+}
+
+extern "C" int jt_ipc_close_handle(void* ptr) {
+  return jt_cuda_check(cudaIpcCloseMemHandle(ptr), "ipc_close_handle");
+}

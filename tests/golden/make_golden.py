@@ -17,6 +17,8 @@ Everything here executes the reference's own code on the CPU:
     eager RoPE definition of its byte-exact test (bf16)           -> rope_scatter.npz
   * speculative/jetspec/serving_ops.py accept_batch (host walk over argmax of the logits)
                                                                   -> accept.npz
+  * layers/linear.py RowParallelLinear (weight_loader + forward: F.linear on each rank's
+    shard, dist.all_reduce over gloo ranks on the CPU, bf16)       -> row_linear.npz
 
 The fixtures hold only live K/V rows (bf16 bit patterns) plus seeds and shapes, so they
 stay small; the tests rebuild the NaN-poisoned pools from them.  The GPU box never runs
@@ -326,6 +328,55 @@ def accept_cases():
         len(trees), [r["accepted_length"] for r in results]))
 
 
+ROW_LINEAR_CASES = (  # name, world, rows, in features, out features, bias, seed
+    ("w1", 1, 5, 64, 64, True, 41),
+    ("w2", 2, 37, 256, 96, True, 42),
+    ("w4", 4, 130, 512, 288, False, 43),
+)
+
+
+def _row_linear_rank(rank, world, reference, port, case, out_path):
+    """One gloo rank running the reference's RowParallelLinear on its input shard."""
+    import torch.distributed as dist
+    sys.path.insert(0, reference)
+    os.environ["MASTER_ADDR"], os.environ["MASTER_PORT"] = "127.0.0.1", str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    from nanovllm.layers.linear import RowParallelLinear
+    _, _, rows, fin, fout, bias, seed = case
+    gen = torch.Generator().manual_seed(seed)
+    x = torch.randn(rows, fin, generator=gen).bfloat16()
+    weight = (torch.randn(fout, fin, generator=gen) / fin ** 0.5).bfloat16()
+    b = torch.randn(fout, generator=gen).bfloat16()
+    layer = RowParallelLinear(fin, fout, bias=bias).to(torch.bfloat16)
+    layer.weight_loader(layer.weight, weight)
+    if bias:
+        layer.weight_loader(layer.bias, b)
+    with torch.no_grad():
+        y = layer(x.chunk(world, 1)[rank].contiguous())
+    if rank == 0:
+        np.savez(out_path, x=bf16_bits(x), weight=bf16_bits(weight), bias=bf16_bits(b),
+                 has_bias=np.int32(bias), world=np.int32(world), y=bf16_bits(y))
+    dist.destroy_process_group()
+
+
+def row_linear_cases():
+    import tempfile
+    import torch.multiprocessing as mp
+    arrays = {}
+    with tempfile.TemporaryDirectory() as tmp:
+        for i, case in enumerate(ROW_LINEAR_CASES):
+            name, world = case[0], case[1]
+            path = os.path.join(tmp, name + ".npz")
+            mp.spawn(_row_linear_rank, args=(world, str(REFERENCE), 29650 + i, case, path),
+                     nprocs=world)
+            with np.load(path) as z:
+                for key in z.files:
+                    arrays[f"{name}_{key}"] = z[key]
+    np.savez_compressed(HERE / "row_linear.npz", names=np.array([c[0] for c in ROW_LINEAR_CASES]),
+                        **arrays)
+    print("row_linear: %d cases" % len(ROW_LINEAR_CASES))
+
+
 def main():
     parser = argparse.ArgumentParser()
     parser.add_argument("--reference", required=True, help="path of the reference checkout")
@@ -337,6 +388,7 @@ def main():
     kv_cases()
     rope_cases()
     accept_cases()
+    row_linear_cases()
     rng = np.random.default_rng(7)
     parents = [random_parents(rng, n) for n in (7, 5, 9)]
     attention_case("ragged3", (65, 0, 257), ((2,), (), (4, 0)), parents, 6 * 256, 8,

@@ -1,0 +1,66 @@
+"""Row-parallel linear on the CPU: the oracle pinned to the reference's golden, the layer's
+host logic (shards, bias on rank 0) under gloo ranks, and the workspace size rule."""
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch.multiprocessing as mp
+
+import _row_linear_worker
+from golden_cases import GOLDEN
+from oracle import row_linear as orl
+
+
+def _case(name):
+    z = np.load(GOLDEN / "row_linear.npz")
+    g = lambda key: z[f"{name}_{key}"]
+    bias = orl.bf16_to_f32(g("bias")) if int(g("has_bias")) else None
+    return (orl.bf16_to_f32(g("x")), orl.bf16_to_f32(g("weight")), bias, int(g("world")),
+            g("y"))
+
+
+@pytest.mark.parametrize("name", ["w1", "w2", "w4"])
+def test_oracle_matches_reference_golden(name):
+    x, weight, bias, world, y_bits = _case(name)
+    y = orl.bf16_to_f32(y_bits)
+    ours = orl.row_parallel_linear(x, weight, bias, world)
+    assert (np.abs(ours - y) <= orl.tolerance(x, weight, bias, world)).all()
+    if world <= 2:  # one rounding of the sum either way: bit-exact
+        assert np.array_equal(ours, y)
+
+
+def test_bf16_rounding_is_nearest_even():
+    values = np.array([1 + 2 ** -8, 1 + 3 * 2 ** -8, -(1 + 2 ** -8), 1 + 2 ** -9, 3.0],
+                      dtype=np.float32)
+    assert orl.round_bf16(values).tolist() == [1.0, 1 + 2 ** -6, -1.0, 1.0, 3.0]
+
+
+@pytest.mark.parametrize("name,world,port", [("w2", 2, 29731), ("w4", 4, 29741)])
+def test_layer_shards_and_bias_rule_under_gloo(tmp_path, name, world, port):
+    """The layer's weight_loader and rank-0 bias rule give the reference's output bits."""
+    out = tmp_path / "y.npy"
+    ctx = mp.get_context("spawn")
+    procs = [ctx.Process(target=_row_linear_worker.cpu_rank, args=(r, world, port, name, str(out)))
+             for r in range(world)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(120)
+        assert p.exitcode == 0
+    z = np.load(GOLDEN / "row_linear.npz")
+    assert np.array_equal(np.load(out).view(np.uint16), z[f"{name}_y"])
+
+
+def test_workspace_rule():
+    from jetspec_b200 import _lib
+
+    lib = _lib.load_library()
+    assert lib.jt_row_linear_workspace_size(2048, 4096, 1) == 0
+    assert lib.jt_row_linear_workspace_size(0, 4096, 2) == -1
+    assert lib.jt_row_linear_workspace_size(10, 64, 9) == -1
+    tiles = 16 * 16
+    for world in (2, 4, 8):
+        owned = -(-tiles // world)
+        flags = -(-tiles * (world + 1) * 4 // 256) * 256
+        expect = flags + owned * world * 65536 + owned * 65536
+        assert lib.jt_row_linear_workspace_size(2048, 4096, world) == expect
