@@ -55,10 +55,14 @@ def row_parallel_linear(x, weight, bias, world: int, dtype: str = "bf16") -> np.
 
 
 def tolerance(x, weight, bias, world: int, dtype: str = "bf16") -> np.ndarray:
-    """Per-element bound on |y - row_parallel_linear| for any implementation that rounds
-    each rank's partial and the sum once, in any order: one unit in the last place of every
-    partial and of the result (fp32 accumulation order may flip either rounding)."""
+    """Per-element bound on |y - row_parallel_linear| for any implementation that sums
+    each rank's products in float32 (in any order), rounds each partial and the sum once:
+    one unit in the last place of every partial and of the result, plus the float32
+    accumulation bound gamma_K * sum |x_i w_i| (gamma_K ~ K 2^-24) of each partial."""
     eps = 2.0 ** -7 if dtype == "bf16" else 2.0 ** -10
     partials = rank_partials(x, weight, bias, world, dtype)
     total = row_parallel_linear(x, weight, bias, world, dtype)
-    return eps * (np.sum(np.abs(np.stack(partials)), axis=0) + np.abs(total)) + 1e-6
+    shard = np.asarray(x).shape[1] // world
+    absdot = np.abs(np.asarray(x, dtype=np.float64)) @ np.abs(np.asarray(weight, np.float64)).T
+    return (eps * (np.sum(np.abs(np.stack(partials)), axis=0) + np.abs(total)) +
+            shard * 2.0 ** -24 * absdot + 1e-6)

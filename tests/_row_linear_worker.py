@@ -91,8 +91,11 @@ def gpu_rank(rank: int, world: int, port: int, result_path: str):
             parts = [(x[:, r * shard:(r + 1) * shard].float() @
                       weight[:, r * shard:(r + 1) * shard].float().T +
                       (bias.float() if r == 0 else 0)).bfloat16().float() for r in range(world)]
-            ref = torch.stack(parts).sum(0)
-            tol = 2.0 ** -7 * (torch.stack(parts).abs().sum(0) + ref.abs()) + 1e-6
+            ref = torch.stack(parts).sum(0).bfloat16().float()
+            absdot = sum(x[:, r * shard:(r + 1) * shard].float().abs() @
+                         weight[:, r * shard:(r + 1) * shard].float().abs().T for r in range(world))
+            tol = (2.0 ** -7 * (torch.stack(parts).abs().sum(0) + ref.abs()) +
+                   shard * 2.0 ** -24 * absdot + 1e-6)
             err = (y.float() - ref).abs()
             report[f"call{call}_max_over_tol"] = float((err / tol).max())
             report[f"call{call}_vs_nccl_max_abs"] = float((y.float() - nccl.float()).abs().max())

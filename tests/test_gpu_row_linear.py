@@ -25,6 +25,7 @@ from oracle import row_linear as orl
 
 pytestmark = pytest.mark.gpu
 DEV = torch.device("cuda", 0)
+torch.backends.cuda.matmul.allow_tf32 = False  # the float32 reference stays float32
 
 
 def _golden(name):
@@ -41,12 +42,24 @@ def _shards(x, weight, world):
 
 
 def _torch_reference(xs, ws, bias, dtype):
+    """float32 partials rounded to the dtype and summed, with the per-element bound of
+    oracle/row_linear.tolerance (one ulp of each partial and of the sum, plus the float32
+    accumulation bound K 2^-24 sum |x_i w_i| of each partial)."""
     parts = [(x.float() @ w.float().T + (bias.float() if (r == 0 and bias is not None) else 0))
              .to(dtype).float() for r, (x, w) in enumerate(zip(xs, ws))]
     stacked = torch.stack(parts)
     total = stacked.sum(0).to(dtype).float()
     eps = 2.0 ** -7 if dtype == torch.bfloat16 else 2.0 ** -10
-    return total, eps * (stacked.abs().sum(0) + total.abs()) + 1e-6
+    absdot = sum(x.float().abs() @ w.float().abs().T for x, w in zip(xs, ws))
+    k = xs[0].shape[1]
+    return total, eps * (stacked.abs().sum(0) + total.abs()) + k * 2.0 ** -24 * absdot + 1e-6
+
+
+def _assert_close(out, ref, tol):
+    err = (out.float() - ref).abs()
+    assert (err <= tol).all(), f"{int((err > tol).sum())} elements outside the bound"
+    # In aggregate the two roundings differ by well under one ulp.
+    assert err.mean() <= 2.0 ** -9 * ref.abs().mean()
 
 
 def _run(xs, ws, bias, workspaces=None):
@@ -87,7 +100,7 @@ def test_matches_float32_reference(world, m, n, k, dtype):
     outs = _run(xs, ws, bias)
     ref, tol = _torch_reference(xs, ws, bias, dtype)
     for out in outs:
-        assert ((out.float() - ref).abs() <= tol).all()
+        _assert_close(out, ref, tol)
     assert jb.read_device_errors() == 0
 
 
@@ -103,7 +116,7 @@ def test_two_calls_reuse_the_exchange_workspaces():
         outs = row_parallel_linear_emulated(xs, ws, None, workspaces=(buffers, epoch))
         ref, tol = _torch_reference(xs, ws, None, torch.bfloat16)
         for out in outs:
-            assert ((out.float() - ref).abs() <= tol).all()
+            _assert_close(out, ref, tol)
     assert jb.read_device_errors() == 0
 
 
@@ -116,12 +129,12 @@ def test_strided_input_rows_and_leading_dims():
     out = row_parallel_linear(x, weight)
     assert out.shape == (2, m // 2, n)
     ref, tol = _torch_reference([x.reshape(m, k)], [weight], None, torch.bfloat16)
-    assert ((out.reshape(m, n).float() - ref).abs() <= tol).all()
+    _assert_close(out.reshape(m, n), ref, tol)
 
 
 def test_shapes_the_kernel_does_not_take_are_rejected():
     x = torch.randn(8, 64, device=DEV).bfloat16()
-    with pytest.raises(jb.KernelLaunchError, match="multiple of 32"):
+    with pytest.raises(ValueError, match="multiple of 32"):
         row_parallel_linear(x, torch.randn(40, 64, device=DEV).bfloat16())
     with pytest.raises(ValueError):
         row_parallel_linear(x, torch.randn(64, 64, device=DEV).half())
@@ -151,7 +164,7 @@ def test_peer_that_never_arrives_times_out_and_the_context_stays_usable():
     assert jb.read_device_errors() & 4
     y = row_parallel_linear(x, weight)
     ref, tol = _torch_reference([x], [weight], None, torch.bfloat16)
-    assert ((y.float() - ref).abs() <= tol).all()
+    _assert_close(y, ref, tol)
     assert jb.read_device_errors() == 0
 
 
