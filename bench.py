@@ -530,6 +530,7 @@ def run_row_linear(args, rank: int, world: int, local_rank: int):
             ours = lambda i: row_parallel_linear(xs[i], ws[i], None, state)  # noqa: E731
 
             def timed(fn):
+                """Eager: one launch (or two) per call from Python, CUDA events around."""
                 with torch.no_grad():
                     for i in range(warmup):
                         fn(i % layers)
@@ -547,15 +548,47 @@ def run_row_linear(args, rank: int, world: int, local_rank: int):
                 ms = start.elapsed_time(end) / steps
                 return max_over_ranks([ms], world, device)[0]
 
+            def graph_timed(fn):
+                """The layers' calls captured once in a CUDA graph and replayed, as the
+                reference's serving loop replays its captured verify step."""
+                with torch.no_grad():
+                    graph = torch.cuda.CUDAGraph()
+                    with torch.cuda.graph(graph):
+                        for i in range(layers):
+                            fn(i)
+                    replays = max(2, steps // layers)
+                    for _ in range(3):
+                        graph.replay()
+                    if world > 1:
+                        torch.distributed.barrier()
+                    torch.cuda.synchronize(device)
+                    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                    start.record()
+                    for _ in range(replays):
+                        graph.replay()
+                    end.record()
+                    torch.cuda.synchronize(device)
+                    if world > 1:
+                        torch.distributed.barrier()
+                    del graph
+                ms = start.elapsed_time(end) / (replays * layers)
+                return max_over_ranks([ms], world, device)[0]
+
             with torch.no_grad():
                 diff = float((ours(0).float() - reference_forward(0).float()).abs().max())
-            ref_ms, our_ms = timed(reference_forward), timed(ours)
+            ref_eager, our_eager = timed(reference_forward), timed(ours)
+            try:
+                ref_ms, our_ms, launch = graph_timed(reference_forward), graph_timed(ours), "cuda-graph replay"
+            except Exception as exc:  # capture unsupported here: eager numbers stand
+                ref_ms, our_ms, launch = ref_eager, our_eager, f"eager ({type(exc).__name__})"
             flops = 2.0 * rows * hidden * k
             link_bytes = 2 * (world - 1) / world * rows * hidden * 2
             bound_ms = max(flops / (peak["bf16_tflops"] * 1e12),
                            link_bytes / 770e9) * 1e3
             result["projections"][name] = {
-                "k_per_gpu": k, "layers_rotated": layers, "reference_ms": ref_ms, "ours_ms": our_ms,
+                "k_per_gpu": k, "layers_rotated": layers, "launch": launch,
+                "reference_ms": ref_ms, "ours_ms": our_ms,
+                "reference_eager_ms": ref_eager, "ours_eager_ms": our_eager,
                 "speedup": ref_ms / our_ms, "ours_tflops_per_gpu": flops / our_ms / 1e9,
                 "nvlink_bytes_per_gpu_each_way": link_bytes, "bound_ms": bound_ms,
                 "frac_of_bound": bound_ms / our_ms, "max_abs_diff_vs_reference": diff}

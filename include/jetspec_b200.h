@@ -292,9 +292,12 @@ int jt_metadata_build_launch(const JtMetadataBuildParams* params, cudaStream_t s
  * bf16 or f16; n a multiple of 32, k a multiple of 8.  For world > 1, workspaces[r] is
  * rank r's workspace (jt_row_linear_workspace_size bytes, zeroed once when allocated,
  * 256-byte aligned) as this process addresses it (its own, and the peers' opened through
- * jt_ipc_open_handle); epoch starts at 1 and grows by one per call of the group.  A
- * rank whose peers do not arrive within wait_limit_cycles (0: about ten seconds) flags
- * device error bit 2 and leaves its output incomplete.
+ * jt_ipc_open_handle).  epoch 0 (the usual value) takes the call's epoch from a counter in
+ * the rank's workspace that the kernel advances itself, so a captured launch replays
+ * correctly; a nonzero epoch (1, 2, 3, ... on every rank, never mixed with 0 on one
+ * workspace) is used as given.  A rank whose peers do not arrive within
+ * wait_limit_cycles (0: about ten seconds) flags device error bit 2 and leaves its output
+ * incomplete.
  */
 typedef struct JtRowLinearParams {
   const void* x;

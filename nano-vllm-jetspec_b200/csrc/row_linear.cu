@@ -12,19 +12,21 @@
 //   warps 2-5   epilogue: TMEM -> registers -> bf16/f16 partial tile, stored straight into
 //               the tile owner's receive slot (a peer GPU's memory over NVLink, or this
 //               GPU's), then a release flag in the owner's memory
-//   warps 6-9   exchange: for the tiles this rank owns (tile t belongs to rank t % world)
+//   warps 6-13  exchange: for the tiles this rank owns (tile t belongs to rank t % world)
 //               wait for every rank's partial, sum them in fp32, round once, write the
-//               tile to this rank's output and to its result area and raise a done flag on
-//               every rank; then copy the tiles other ranks own from their result areas
-//               into this rank's output as each one is done
+//               tile to this rank's output and into every other rank's inbox, and raise
+//               a done flag there; then copy the tiles other ranks own from this rank's
+//               inbox into its output as each one is done
 //
 // The all-reduce therefore moves the reduce-scatter + all-gather volume ((world-1)/world of
-// the output out and back per rank) with plain peer stores and loads, tile by tile while
-// the GEMM is still running, and without a separate collective launch.  Flags carry the
-// call's epoch (the host increments it per call), so nothing is reset between calls; a
-// rank reuses its receive and result areas only after every rank finished reading them in
-// the previous call (each rank leaves a call only after all its output tiles are done, and
-// an owner writes a result only after every rank's next partial arrived).  Every wait is
+// the output out and back per rank), tile by tile while the GEMM is still running, and
+// without a separate collective launch; every transfer over NVLink is a posted store
+// (partials to their owner, results to the inboxes), every load is from this GPU's memory.
+// Flags carry the call's epoch (the host increments it per call), so nothing is reset
+// between calls; a rank's receive slots and inbox are rewritten only after it finished
+// reading them in the previous call (a rank sends its next partial only after leaving the
+// previous call, which it does after copying its whole inbox, and an owner pushes a result
+// only after every rank's next partial for that tile arrived).  Every wait is
 // bounded: a flag that does not arrive within the limit sets JT_DEVERR_TIMEOUT and the
 // exchange warps skip the rest of their work.  No load uses cluster multicast.
 //
@@ -58,7 +60,8 @@ constexpr int kOffBar = kOffB + kStages * kBTileBytes;
 constexpr int kOffMisc = kOffBar + 16 * 8;
 constexpr int kSmemBytes = kOffMisc + 64 + 1024;  // + alignment slack
 static_assert(kSmemBytes <= 227 * 1024, "shared memory per CTA");
-constexpr int kThreads = 320;
+constexpr int kThreads = 448;
+constexpr int kExchangeThreads = 256;  // warps 6-13
 constexpr int kTileElems = kBM * kBN;  // elements per partial / result tile
 constexpr int kMaxRanks = 8;
 constexpr long long kLocalWaitLimit = 4000000000ll;  // cycles per pipeline wait
@@ -82,10 +85,13 @@ struct Args {
   unsigned char* ws[kMaxRanks];  // per rank of the group, as addressable from this GPU
 };
 
-// Workspace of one rank: [ready: tiles x world u32][done: tiles u32] (256-byte aligned),
-// then the receive slots [owned_max][world][tile], then the result tiles [owned_max][tile].
+// Workspace of one rank: a 256-byte control block (u32 call counter at 0, u32 CTA exit
+// counter at 4), [ready: tiles x world u32][done: tiles u32] (256-byte aligned), then the
+// receive slots [owned_max][world][tile], then the inbox [tiles][tile] where the owners of
+// the other tiles put the reduced results.
+constexpr int kCtrlBytes = 256;
 __host__ __device__ inline int64_t ws_flag_bytes(int tiles, int world) {
-  return ((static_cast<int64_t>(tiles) * (world + 1) * 4) + 255) / 256 * 256;
+  return kCtrlBytes + ((static_cast<int64_t>(tiles) * (world + 1) * 4) + 255) / 256 * 256;
 }
 __host__ __device__ inline int64_t ws_recv_offset(int tiles, int world) {
   return ws_flag_bytes(tiles, world);
@@ -95,8 +101,7 @@ __host__ __device__ inline int64_t ws_result_offset(int tiles, int world, int ow
          static_cast<int64_t>(owned_max) * world * kTileElems * 2;
 }
 __host__ __device__ inline int64_t ws_total(int tiles, int world, int owned_max) {
-  return ws_result_offset(tiles, world, owned_max) +
-         static_cast<int64_t>(owned_max) * kTileElems * 2;
+  return ws_result_offset(tiles, world, owned_max) + static_cast<int64_t>(tiles) * kTileElems * 2;
 }
 
 // ---- PTX wrappers --------------------------------------------------------------------
@@ -252,10 +257,10 @@ struct Maps {
 };
 
 __device__ __forceinline__ uint32_t* ready_flags(unsigned char* ws) {
-  return reinterpret_cast<uint32_t*>(ws);
+  return reinterpret_cast<uint32_t*>(ws + kCtrlBytes);
 }
 __device__ __forceinline__ uint32_t* done_flags(unsigned char* ws, int tiles, int world) {
-  return reinterpret_cast<uint32_t*>(ws) + static_cast<int64_t>(tiles) * world;
+  return ready_flags(ws) + static_cast<int64_t>(tiles) * world;
 }
 
 // 16-byte chunk `ch` (0..4095) of a partial / result tile: chunks are stored so that the
@@ -291,6 +296,12 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int i = 0; i < kNumBars; ++i)
       mbar_init(RL_BAR(i), (i == kBarAccEmpty || i == kBarAccEmpty + 1) ? 4u : 1u);
     misc[1] = 0;
+    // The call's epoch: given by the host, or (0) one past this rank's call counter, which
+    // the last CTA of the previous call advanced (stream order makes it visible here).
+    misc[2] = static_cast<int>(
+        a.epoch != 0 || world == 1
+            ? a.epoch
+            : *reinterpret_cast<volatile uint32_t*>(a.ws[rank]) + 1u);
     asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
   }
   if (warp == 1) {
@@ -303,6 +314,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = static_cast<uint32_t>(misc[0]);
+  const uint32_t epoch = static_cast<uint32_t>(misc[2]);
 
   if (warp == 0) {
     // ---------------------------------------------------------------- TMA producer
@@ -410,30 +422,29 @@ __global__ void __launch_bounds__(kThreads, 1)
         named_sync(2, 128);
         if (warp == 2 && lane == 0)
           st_release_sys(ready_flags(a.ws[owner]) + static_cast<int64_t>(t) * world + rank,
-                         a.epoch);
+                         epoch);
       }
     }
   } else if (world > 1) {
     // ---------------------------------------------------------------- exchange
-    const int et = tid - 192;  // 0..127
+    const int et = tid - 192;  // 0..255
     unsigned char* mine = a.ws[rank];
-    const int64_t res_off = ws_result_offset(a.tiles, world, a.owned_max);
+    const int64_t inbox_off = ws_result_offset(a.tiles, world, a.owned_max);
     const int owned = (a.tiles - rank + world - 1) / world;  // tiles j * world + rank
     for (int j = cta; j < owned; j += a.grid_per_rank) {
       const int t = j * world + rank;
       if (et < world)
-        wait_flag(ready_flags(mine) + static_cast<int64_t>(t) * world + et, a.epoch,
+        wait_flag(ready_flags(mine) + static_cast<int64_t>(t) * world + et, epoch,
                   a.wait_limit, abort);
-      named_sync(1, 128);
+      named_sync(1, kExchangeThreads);
       if (!*abort) {
         const int m0 = (t % a.m_tiles) * kBM, n0 = (t / a.m_tiles) * kBN;
         const uint4* slots = reinterpret_cast<const uint4*>(
             mine + ws_recv_offset(a.tiles, world) +
             static_cast<int64_t>(j) * world * kTileElems * 2);
-        uint4* result = reinterpret_cast<uint4*>(mine + res_off +
-                                                 static_cast<int64_t>(j) * kTileElems * 2);
+        const int64_t inbox_tile = inbox_off + static_cast<int64_t>(t) * kTileElems * 2;
 #pragma unroll 1
-        for (int c0 = et; c0 < kTileElems / 8; c0 += 4 * 128) {
+        for (int c0 = et; c0 < kTileElems / 8; c0 += 4 * kExchangeThreads) {
           float sum[4][8];
 #pragma unroll
           for (int u = 0; u < 4; ++u)
@@ -444,7 +455,8 @@ __global__ void __launch_bounds__(kThreads, 1)
             uint4 in[4];
 #pragma unroll
             for (int u = 0; u < 4; ++u)
-              in[u] = __ldcg(slots + static_cast<int64_t>(s) * (kTileElems / 8) + c0 + 128 * u);
+              in[u] = __ldcg(slots + static_cast<int64_t>(s) * (kTileElems / 8) + c0 +
+                             kExchangeThreads * u);
 #pragma unroll
             for (int u = 0; u < 4; ++u) {
               const uint32_t w4[4] = {in[u].x, in[u].y, in[u].z, in[u].w};
@@ -458,10 +470,11 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
 #pragma unroll
           for (int u = 0; u < 4; ++u) {
-            const int ch = c0 + 128 * u;
+            const int ch = c0 + kExchangeThreads * u;
             const uint4 o = make_uint4(Cv::pack(sum[u][0], sum[u][1]), Cv::pack(sum[u][2], sum[u][3]),
                                        Cv::pack(sum[u][4], sum[u][5]), Cv::pack(sum[u][6], sum[u][7]));
-            result[ch] = o;
+            for (int r = 0; r < world; ++r)  // posted stores into the other ranks' inboxes
+              if (r != rank) reinterpret_cast<uint4*>(a.ws[r] + inbox_tile)[ch] = o;
             int row, col;
             chunk_coords(ch, row, col);
             const int64_t m = m0 + row, n = n0 + col;
@@ -472,30 +485,30 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
       __threadfence_system();
-      named_sync(1, 128);
-      if (et < world && !*abort)
-        st_release_sys(done_flags(a.ws[et], a.tiles, world) + t, a.epoch);
+      named_sync(1, kExchangeThreads);
+      if (et < world && et != rank && !*abort)
+        st_release_sys(done_flags(a.ws[et], a.tiles, world) + t, epoch);
     }
-    // Tiles other ranks own: copy each into this rank's output once its owner is done.
+    // Tiles other ranks own: copy each from this rank's inbox once its owner is done.
     uint32_t* done = done_flags(mine, a.tiles, world);
     for (int t = cta; t < a.tiles; t += a.grid_per_rank) {
       const int owner = t % world;
       if (owner == rank) continue;
-      if (et == 0) wait_flag(done + t, a.epoch, a.wait_limit, abort);
-      named_sync(1, 128);
+      if (et == 0) wait_flag(done + t, epoch, a.wait_limit, abort);
+      named_sync(1, kExchangeThreads);
       if (*abort) continue;
       const int m0 = (t % a.m_tiles) * kBM, n0 = (t / a.m_tiles) * kBN;
-      const uint4* src = reinterpret_cast<const uint4*>(
-          a.ws[owner] + res_off + static_cast<int64_t>(t / world) * kTileElems * 2);
+      const uint4* src =
+          reinterpret_cast<const uint4*>(mine + inbox_off + static_cast<int64_t>(t) * kTileElems * 2);
 #pragma unroll 1
-      for (int c0 = et; c0 < kTileElems / 8; c0 += 8 * 128) {
+      for (int c0 = et; c0 < kTileElems / 8; c0 += 8 * kExchangeThreads) {
         uint4 v[8];
 #pragma unroll
-        for (int u = 0; u < 8; ++u) v[u] = __ldcg(src + c0 + 128 * u);
+        for (int u = 0; u < 8; ++u) v[u] = __ldcg(src + c0 + kExchangeThreads * u);
 #pragma unroll
         for (int u = 0; u < 8; ++u) {
           int row, col;
-          chunk_coords(c0 + 128 * u, row, col);
+          chunk_coords(c0 + kExchangeThreads * u, row, col);
           const int64_t m = m0 + row, n = n0 + col;
           if (m < a.M && n < a.N)
             *reinterpret_cast<uint4*>(static_cast<unsigned char*>(a.out[lr]) +
@@ -510,6 +523,17 @@ __global__ void __launch_bounds__(kThreads, 1)
     tc_fence_after();
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, 512;\n" ::"r"(tmem)
                  : "memory");
+  }
+  if (tid == 0 && world > 1 && a.epoch == 0) {
+    // Every CTA of this rank read the counter at its start; the last one to leave
+    // advances it for the next call.
+    uint32_t* ctrl = reinterpret_cast<uint32_t*>(a.ws[rank]);
+    __threadfence();
+    if (atomicAdd(ctrl + 1, 1u) == static_cast<uint32_t>(a.grid_per_rank - 1)) {
+      atomicExch(ctrl + 1, 0u);
+      __threadfence();
+      atomicAdd(ctrl, 1u);
+    }
   }
 #undef RL_BAR
 }
@@ -624,19 +648,29 @@ int rl_launch(const JtRowLinearParams* ranks, int count, cudaStream_t stream) {
   a.wait_limit = p0.wait_limit_cycles > 0 ? p0.wait_limit_cycles : 20000000000ll;
   for (int r = 0; r < p0.world && p0.world > 1; ++r)
     a.ws[r] = static_cast<unsigned char*>(p0.workspaces[r]);
-  int dev = 0, sms = 0;
+  // Per-device facts, looked up once: the SM count and the kernels' shared-memory opt-in.
+  static int sm_count[64] = {0};
+  int dev = 0;
   rc = jt_cuda_check(cudaGetDevice(&dev), "row_linear: device");
   if (rc != JT_OK) return rc;
-  rc = jt_cuda_check(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev),
-                     "row_linear: SM count");
-  if (rc != JT_OK) return rc;
+  if (dev < 0 || dev >= 64) return jt_fail(JT_ERR_INVALID, "row_linear: device index");
+  auto kernel = p0.dtype == JT_BF16 ? rl::row_linear_kernel<true> : rl::row_linear_kernel<false>;
+  if (sm_count[dev] == 0) {
+    int sms = 0;
+    rc = jt_cuda_check(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev),
+                       "row_linear: SM count");
+    if (rc != JT_OK) return rc;
+    for (auto k : {rl::row_linear_kernel<true>, rl::row_linear_kernel<false>}) {
+      rc = jt_cuda_check(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                              rl::kSmemBytes),
+                         "row_linear: smem attribute");
+      if (rc != JT_OK) return rc;
+    }
+    sm_count[dev] = sms;
+  }
+  const int sms = sm_count[dev];
   if (sms < count) return jt_fail(JT_ERR_INVALID, "row_linear: more ranks than SMs");
   a.grid_per_rank = std::min(a.tiles, sms / count);
-  auto kernel = p0.dtype == JT_BF16 ? rl::row_linear_kernel<true> : rl::row_linear_kernel<false>;
-  rc = jt_cuda_check(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                          rl::kSmemBytes),
-                     "row_linear: smem attribute");
-  if (rc != JT_OK) return rc;
   // Cooperative: every CTA is resident at once (an exchange warp waits on other CTAs).
   cudaLaunchConfig_t cfg{};
   cfg.gridDim = dim3(static_cast<unsigned>(a.grid_per_rank * count));

@@ -36,7 +36,6 @@ class RowLinearGroup:
         self.world = dist.get_world_size(group) if dist.is_initialized() else 1
         self.rank = dist.get_rank(group) if dist.is_initialized() else 0
         self.device = device or torch.device("cuda", torch.cuda.current_device())
-        self.epoch = 0
         self.capacity = (0, 0)
         self._own = None
         self._peers: list[int] = []
@@ -83,7 +82,6 @@ class RowLinearGroup:
         self._own, self._peers = own.value, peers
         self._array = (ctypes.c_void_p * self.world)(*peers)
         self.capacity = (rows, n)
-        self.epoch = 0
         # Every rank's zeroed workspace exists before any rank's first exchange.
         torch.cuda.synchronize(self.device)
         dist.barrier(group=self.group)
@@ -92,8 +90,9 @@ class RowLinearGroup:
         return self._array
 
     def next_epoch(self) -> int:
-        self.epoch = (self.epoch + 1) & 0xFFFFFFFF or 1
-        return self.epoch
+        """0: the kernel takes each call's epoch from the counter in this rank's workspace
+        (advanced on the device, so captured launches replay correctly)."""
+        return 0
 
     def close(self) -> None:
         if self._own:

@@ -61,6 +61,6 @@ def test_workspace_rule():
     tiles = 16 * 16
     for world in (2, 4, 8):
         owned = -(-tiles // world)
-        flags = -(-tiles * (world + 1) * 4 // 256) * 256
-        expect = flags + owned * world * 65536 + owned * 65536
+        flags = 256 + -(-tiles * (world + 1) * 4 // 256) * 256  # control block + flags
+        expect = flags + owned * world * 65536 + tiles * 65536
         assert lib.jt_row_linear_workspace_size(2048, 4096, world) == expect

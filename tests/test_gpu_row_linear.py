@@ -120,6 +120,40 @@ def test_two_calls_reuse_the_exchange_workspaces():
     assert jb.read_device_errors() == 0
 
 
+def test_device_epoch_counter_and_graph_replay():
+    """epoch 0: every call takes its epoch from the workspaces' own counters, so repeated
+    calls and replays of one captured launch (inputs changed in place) stay correct."""
+    world, m, n, k = 4, 384, 768, 1024
+    nbytes = int(_lib.load_library().jt_row_linear_workspace_size(m, n, world))
+    buffers = [torch.zeros(nbytes, dtype=torch.uint8, device=DEV) for _ in range(world)]
+    gen = torch.Generator(device=DEV).manual_seed(21)
+    x = torch.randn(m, k, generator=gen, device=DEV).bfloat16()
+    weight = (torch.randn(n, k, generator=gen, device=DEV) / k ** 0.5).bfloat16()
+    xs, ws = _shards(x, weight, world)
+    for _ in range(3):
+        outs = row_parallel_linear_emulated(xs, ws, None, workspaces=(buffers, 0))
+        ref, tol = _torch_reference(xs, ws, None, torch.bfloat16)
+        for out in outs:
+            _assert_close(out, ref, tol)
+    graph = torch.cuda.CUDAGraph()
+    stream = torch.cuda.Stream(DEV)
+    stream.wait_stream(torch.cuda.current_stream(DEV))
+    with torch.cuda.stream(stream):
+        with torch.cuda.graph(graph):
+            outs = row_parallel_linear_emulated(xs, ws, None, workspaces=(buffers, 0))
+    torch.cuda.current_stream(DEV).wait_stream(stream)
+    for seed in (22, 23):
+        gen = torch.Generator(device=DEV).manual_seed(seed)
+        for xr in xs:
+            xr.copy_(torch.randn(xr.shape, generator=gen, device=DEV).bfloat16())
+        graph.replay()
+        ref, tol = _torch_reference(xs, ws, None, torch.bfloat16)
+        for out in outs:
+            _assert_close(out, ref, tol)
+    torch.cuda.synchronize()
+    assert jb.read_device_errors() == 0
+
+
 def test_strided_input_rows_and_leading_dims():
     m, n, k = 130, 256, 320
     gen = torch.Generator(device=DEV).manual_seed(9)
