@@ -5,10 +5,11 @@
 // the [M, N] result; the Qwen3 o_proj (qwen3.py:59, :97 ... :302) and down_proj (:334,
 // :345) are its callers.  Here one persistent kernel per GPU does both:
 //
-//   warp 0      TMA producer: x [128 rows x 64 K] and W [256 rows x 64 K] tiles, 128-byte
-//               swizzle, into a 4-stage ring (48 KB per stage)
-//   warp 1      tcgen05.mma issuer (kind::f16, M128 N256 K16) and TMEM owner; two 256-column
-//               fp32 accumulators so one tile's epilogue overlaps the next tile's MMAs
+//   warp 0      TMA producer: x [256 rows x 64 K] and W [256 rows x 64 K] tiles, 128-byte
+//               swizzle, into a 3-stage ring (64 KB per stage)
+//   warp 1      tcgen05.mma issuer (kind::f16, M128 N256 K16, two per K step: the two
+//               128-row halves of the x tile share each W tile) and TMEM owner; the
+//               256 x 256 fp32 tile fills all 512 columns
 //   warps 2-5   epilogue: TMEM -> registers -> bf16/f16 partial tile, stored straight into
 //               the tile owner's receive slot (a peer GPU's memory over NVLink, or this
 //               GPU's), then a release flag in the owner's memory
@@ -49,10 +50,11 @@ __device__ uint32_t g_rowlin_errors;
 
 namespace rl {
 
-constexpr int kBM = 128, kBN = 256, kBK = 64;
-constexpr int kStages = 4;
-constexpr int kATileBytes = kBM * kBK * 2;  // 16 KB
+constexpr int kBM = 256, kBN = 256, kBK = 64;  // output tile; MMAs are M128 halves
+constexpr int kStages = 3;
+constexpr int kATileBytes = kBM * kBK * 2;  // 32 KB
 constexpr int kBTileBytes = kBN * kBK * 2;  // 32 KB
+constexpr int kAHalfBytes = kATileBytes / 2;  // rows 128..255 of the x tile
 constexpr int kStageBytes = kATileBytes + kBTileBytes;
 constexpr int kOffA = 0;
 constexpr int kOffB = kOffA + kStages * kATileBytes;
@@ -67,12 +69,12 @@ constexpr int kMaxRanks = 8;
 constexpr long long kLocalWaitLimit = 4000000000ll;  // cycles per pipeline wait
 
 // Barriers.
-constexpr int kBarFull = 0;       // [kStages] TMA bytes
-constexpr int kBarEmpty = 4;      // [kStages] MMA commit
-constexpr int kBarAccFull = 8;    // [2] MMA commit after a tile's last K step
-constexpr int kBarAccEmpty = 10;  // [2] 4 epilogue warps
-constexpr int kBarDrain = 12;
-constexpr int kNumBars = 13;
+constexpr int kBarFull = 0;      // [kStages] TMA bytes
+constexpr int kBarEmpty = 3;     // [kStages] MMA commit
+constexpr int kBarAccFull = 6;   // MMA commit after a tile's last K step
+constexpr int kBarAccEmpty = 7;  // 4 epilogue warps
+constexpr int kBarDrain = 8;
+constexpr int kNumBars = 9;
 
 struct Args {
   int64_t M, N, K;
@@ -263,12 +265,13 @@ __device__ __forceinline__ uint32_t* done_flags(unsigned char* ws, int tiles, in
   return ready_flags(ws) + static_cast<int64_t>(tiles) * world;
 }
 
-// 16-byte chunk `ch` (0..4095) of a partial / result tile: chunks are stored so that the
+// 16-byte chunk `ch` (0..8191) of a partial / result tile: chunks are stored so that the
 // 32 lanes of an epilogue warp write 512 contiguous bytes (one row per lane, 8 columns per
-// chunk); this maps a chunk back to its row and first column inside the 128 x 256 tile.
+// chunk); this maps a chunk back to its row and first column inside the 256 x 256 tile
+// (chunk = half * 4096 + quadrant * 1024 + column group * 128 + i * 32 + lane).
 __device__ __forceinline__ void chunk_coords(int ch, int& row, int& col) {
-  const int lane = ch & 31, i = (ch >> 5) & 3, c = (ch >> 7) & 7, q = ch >> 10;
-  row = q * 32 + lane;
+  const int lane = ch & 31, i = (ch >> 5) & 3, c = (ch >> 7) & 7, q = (ch >> 10) & 3;
+  row = (ch >> 12) * 128 + q * 32 + lane;
   col = c * 32 + i * 8;
 }
 
@@ -276,7 +279,7 @@ template <bool kBf16>
 __global__ void __launch_bounds__(kThreads, 1)
     row_linear_kernel(const __grid_constant__ Args a, const __grid_constant__ Maps maps) {
   using Cv = Conv<kBf16>;
-  constexpr uint32_t kIdesc = instr_desc(kBM, kBN, kBf16);
+  constexpr uint32_t kIdesc = instr_desc(128, kBN, kBf16);  // one 128-row half per MMA
   extern __shared__ unsigned char smem_raw[];
   const uint32_t raw = jt::smem_u32(smem_raw);
   const uint32_t base = (raw + 1023u) & ~1023u;
@@ -294,7 +297,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   if (tid == 0) {
     for (int i = 0; i < kNumBars; ++i)
-      mbar_init(RL_BAR(i), (i == kBarAccEmpty || i == kBarAccEmpty + 1) ? 4u : 1u);
+      mbar_init(RL_BAR(i), i == kBarAccEmpty ? 4u : 1u);
     misc[1] = 0;
     // The call's epoch: given by the host, or (0) one past this rank's call counter, which
     // the last CTA of the previous call advanced (stream order makes it visible here).
@@ -339,10 +342,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint32_t r = 0, acc = 0;
     const uint64_t adesc0 = smem_desc(base + kOffA), bdesc0 = smem_desc(base + kOffB);
     for (int t = cta; t < a.tiles; t += a.grid_per_rank, ++acc) {
-      const int buf = static_cast<int>(acc & 1u);
-      mbar_wait(RL_BAR(kBarAccEmpty + buf), ((acc >> 1) & 1u) ^ 1u);
+      // The accumulator (both halves, 512 columns) is free once the epilogue read it.
+      mbar_wait(RL_BAR(kBarAccEmpty), (acc & 1u) ^ 1u);
       tc_fence_after();
-      const uint32_t d = tmem + static_cast<uint32_t>(buf * kBN);
       for (int kb = 0; kb < k_blocks; ++kb, ++r) {
         const int s = static_cast<int>(r % kStages);
         mbar_wait(RL_BAR(kBarFull + s), (r / kStages) & 1u);
@@ -350,11 +352,15 @@ __global__ void __launch_bounds__(kThreads, 1)
         const uint64_t ad = adesc0 + static_cast<uint64_t>((s * kATileBytes) >> 4);
         const uint64_t bd = bdesc0 + static_cast<uint64_t>((s * kBTileBytes) >> 4);
 #pragma unroll
-        for (int kk = 0; kk < kBK / 16; ++kk)  // 16 K elements = 32 bytes along the row
-          mma_ss_warp(d, ad + 2 * kk, bd + 2 * kk, kIdesc, (kb > 0 || kk > 0) ? 1u : 0u);
+        for (int kk = 0; kk < kBK / 16; ++kk) {  // 16 K elements = 32 bytes along the row
+          const uint32_t accumulate = (kb > 0 || kk > 0) ? 1u : 0u;
+          mma_ss_warp(tmem, ad + 2 * kk, bd + 2 * kk, kIdesc, accumulate);
+          mma_ss_warp(tmem + static_cast<uint32_t>(kBN), ad + (kAHalfBytes >> 4) + 2 * kk,
+                      bd + 2 * kk, kIdesc, accumulate);
+        }
         tc_commit_warp(RL_BAR(kBarEmpty + s));
       }
-      tc_commit_warp(RL_BAR(kBarAccFull + buf));
+      tc_commit_warp(RL_BAR(kBarAccFull));
     }
     // Drain: every MMA this warp issued has completed before TMEM is released.
     tc_commit_warp(RL_BAR(kBarDrain));
@@ -362,25 +368,24 @@ __global__ void __launch_bounds__(kThreads, 1)
   } else if (warp < 6) {
     // ---------------------------------------------------------------- epilogue
     const int q = warp & 3;  // TMEM lane quadrant this warp may read
-    const int row = q * 32 + lane;
     const uint16_t* bias = static_cast<const uint16_t*>(a.bias[lr]);
     uint32_t acc = 0;
     for (int t = cta; t < a.tiles; t += a.grid_per_rank, ++acc) {
-      const int buf = static_cast<int>(acc & 1u);
       const int m0 = (t % a.m_tiles) * kBM, n0 = (t / a.m_tiles) * kBN;
       const int owner = t % world, j = t / world;
-      mbar_wait(RL_BAR(kBarAccFull + buf), (acc >> 1) & 1u);
+      mbar_wait(RL_BAR(kBarAccFull), acc & 1u);
       tc_fence_after();
-      const int64_t m = m0 + row;
       unsigned char* slot =
           world == 1 ? nullptr
                      : a.ws[owner] + ws_recv_offset(a.tiles, world) +
                            (static_cast<int64_t>(j) * world + rank) * kTileElems * 2;
 #pragma unroll 1
-      for (int c = 0; c < kBN / 32; ++c) {
+      for (int hc = 0; hc < 2 * (kBN / 32); ++hc) {  // (half, 32-column group)
+        const int h = hc >> 3, c = hc & 7;
+        const int64_t m = m0 + h * 128 + q * 32 + lane;
         uint32_t v[32];
         tmem_ld32(tmem + (static_cast<uint32_t>(q * 32) << 16) +
-                      static_cast<uint32_t>(buf * kBN + c * 32),
+                      static_cast<uint32_t>(h * kBN + c * 32),
                   v);
         tmem_wait_ld();
         const int64_t n = n0 + c * 32;
@@ -405,7 +410,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                                 packed[4 * i + 3]);
           }
         } else {
-          uint4* o = reinterpret_cast<uint4*>(slot) + (q * 8 + c) * 128 + lane;
+          uint4* o = reinterpret_cast<uint4*>(slot) + h * 4096 + (q * 8 + c) * 128 + lane;
 #pragma unroll
           for (int i = 0; i < 4; ++i)
             o[32 * i] = make_uint4(packed[4 * i], packed[4 * i + 1], packed[4 * i + 2],
@@ -414,7 +419,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(RL_BAR(kBarAccEmpty + buf));
+      if (lane == 0) mbar_arrive(RL_BAR(kBarAccEmpty));
       if (world > 1) {
         // Every epilogue thread's stores of this partial are visible system-wide before
         // the owner's ready flag for (tile, this rank) is raised.
