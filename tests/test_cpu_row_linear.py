@@ -64,3 +64,32 @@ def test_workspace_rule():
         flags = 256 + -(-tiles * (world + 1) * 4 // 256) * 256  # control block + flags
         expect = flags + owned * world * 131072 + tiles * 131072
         assert lib.jt_row_linear_workspace_size(2048, 4096, world) == expect
+
+
+def test_c_abi_rejects_bad_arguments_before_any_cuda_call():
+    """jt_row_linear_launch validates its parameters on the host and answers
+    JT_ERR_INVALID with a message; these checks need no GPU."""
+    import ctypes
+
+    from jetspec_b200 import _lib
+
+    lib = _lib.load_library()
+
+    def launch(**fields):
+        p = _lib.JtRowLinearParams()
+        p.x, p.weight, p.out = 4096, 8192, 12288  # never dereferenced: rejected first
+        p.m, p.n, p.k, p.x_stride, p.w_stride = 64, 256, 128, 128, 128
+        p.dtype, p.rank, p.world, p.epoch = _lib.JT_BF16, 0, 1, 0
+        for key, value in fields.items():
+            setattr(p, key, value)
+        status = lib.jt_row_linear_launch(ctypes.byref(p), None)
+        return status, lib.jt_last_error().decode()
+
+    assert lib.jt_row_linear_launch(None, None) == -1
+    cases = [({"dtype": _lib.JT_F32}, "bf16 or f16"), ({"n": 40}, "multiple of 32"),
+             ({"k": 12}, "multiple of 8"), ({"world": 9}, "world"), ({"rank": 2, "world": 2},
+             "rank"), ({"out": None}, "null"), ({"x": 4100}, "alignment"),
+             ({"x_stride": 100}, "strides"), ({"world": 2}, "workspaces")]
+    for fields, text in cases:
+        status, message = launch(**fields)
+        assert status == -1 and text in message, (fields, message)
