@@ -48,6 +48,31 @@ def test_null_parameters_are_rejected(lib):
     assert lib.jt_tree_attn_launch_noalloc(None, None) == _lib.JT_ERR_INVALID
     assert lib.jt_kv_store_launch(None, None) == _lib.JT_ERR_INVALID
     assert lib.jt_kv_commit_launch(None, None) == _lib.JT_ERR_INVALID
+    assert lib.jt_rope_scatter_launch(None, None) == _lib.JT_ERR_INVALID
+    assert lib.jt_accept_walk_launch(None, None) == _lib.JT_ERR_INVALID
+    assert lib.jt_metadata_build_launch(None, None) == _lib.JT_ERR_INVALID
+    assert lib.jt_row_linear_launch(None, None) == _lib.JT_ERR_INVALID
+
+
+def test_accept_and_metadata_geometry_checks_precede_the_device(lib):
+    import ctypes
+
+    walk = _lib.JtAcceptWalkParams()
+    walk.num_requests, walk.vocab, walk.max_depth, walk.num_nodes = 2, 100, 4, 10
+    walk.path_stride, walk.logits_stride0 = 4, 100  # path_stride < max_depth + 1
+    assert lib.jt_accept_walk_launch(ctypes.byref(walk), None) == _lib.JT_ERR_INVALID
+    assert b"geometry" in lib.jt_last_error()
+    walk.path_stride = 5  # geometry valid, tensors missing
+    assert lib.jt_accept_walk_launch(ctypes.byref(walk), None) == _lib.JT_ERR_INVALID
+    assert b"null" in lib.jt_last_error()
+    meta = _lib.JtMetadataBuildParams()
+    meta.num_requests, meta.block_size, meta.num_nodes, meta.num_pages = 2, 256, 10, 1
+    meta.max_nodes = 2048  # above the 1024-node limit
+    assert lib.jt_metadata_build_launch(ctypes.byref(meta), None) == _lib.JT_ERR_INVALID
+    assert b"max_nodes" in lib.jt_last_error()
+    meta.max_nodes = 64
+    assert lib.jt_metadata_build_launch(ctypes.byref(meta), None) == _lib.JT_ERR_INVALID
+    assert b"null" in lib.jt_last_error()
 
 
 def test_workspace_size_geometry(lib):
