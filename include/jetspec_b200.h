@@ -115,11 +115,13 @@ int jt_tree_attn_launch(const JtTreeAttnParams* params, cudaStream_t stream);
  * coarser splits than jt_tree_attn_launch.  Geometries whose scratch exceeds 32 MiB
  * are rejected with JT_ERR_WORKSPACE.  `workspace` / `workspace_bytes` are ignored.
  *
- * The first call on a device looks up the array's device address
- * (cudaGetSymbolAddress with that device current); make that first call before any
- * stream capture.  All calls share the array and the plan kernel re-initialises what
- * must start at zero on every call, but calls that overlap on the GPU (different
- * streams, or concurrent graph replays) race on it: serialise them.
+ * Every call made outside stream capture looks up the array's device address
+ * (cudaGetSymbolAddress, in the current device and context) and records it for that
+ * context; a call made during capture uses the record and is refused (JT_ERR_INVALID)
+ * when no call has been made in the current context yet, so make the first call on a
+ * device before any stream capture.  All calls share the array and the plan kernel
+ * re-initialises what must start at zero on every call, but calls that overlap on the
+ * GPU (different streams, or concurrent graph replays) race on it: serialise them.
  */
 int jt_tree_attn_launch_noalloc(const JtTreeAttnParams* params, cudaStream_t stream);
 
@@ -156,10 +158,13 @@ int jt_kv_store_launch(const JtKvStoreParams* params, cudaStream_t stream);
  * [2, layers, num_blocks, block_size, kv_heads, head_dim]:
  *   pool[:, :, dst//bs, dst%bs] = pool[:, :, src//bs, src%bs]   (gather before scatter)
  *
- * Replaces copy_accepted_kv (nanovllm/speculative/jetspec/state.py:64-86).  The whole
- * gather completes before any write of the same (axis, layer, head) plane, so
- * overlapping source/destination sets behave like the reference's materialised copy.
- * Supports up to jt_kv_commit_max_slots() slots per call.
+ * Replaces copy_accepted_kv (nanovllm/speculative/jetspec/state.py:64-86).  Every read
+ * of an (axis, layer) plane completes before any write to it (a cooperative launch with a
+ * grid barrier between the gather and the scatter, the planes taken in groups that fit
+ * the grid's shared memory), so overlapping source/destination sets behave like the
+ * reference's materialised copy.  jt_kv_commit_max_slots() is the largest slot count one
+ * call accepts on the current device (one 16-byte word per slot staged per SM x 12288:
+ * about 1.8 million slots on a 148-SM B200; 12288 when no device is visible).
  */
 typedef struct JtKvCommitParams {
   void* kv_pool;

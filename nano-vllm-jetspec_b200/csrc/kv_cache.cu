@@ -5,14 +5,21 @@
 //   * jt_kv_commit_launch - accepted-only commit across K/V and every layer
 //     (copy_accepted_kv, nanovllm/speculative/jetspec/state.py:64-86).
 // Both are pure byte movers: results are bit-identical to the reference's copies.
+#include <cooperative_groups.h>
+
+#include <algorithm>
+
 #include "common.cuh"
+
+namespace cg = cooperative_groups;
 
 namespace {
 
 __device__ uint32_t g_kv_errors;
 
 constexpr int kStoreThreads = 256;
-constexpr int kCommitThreads = 256;
+constexpr int kCommitThreads = 512;
+constexpr int kCommitUnroll = 4;
 constexpr int kCommitSmemCap = 192 * 1024;  // bytes of staging per commit CTA
 
 __device__ __forceinline__ int64_t load_slot(const void* base, int is64, int64_t i) {
@@ -64,70 +71,125 @@ __global__ void __launch_bounds__(kStoreThreads) kv_store_kernel(JtKvStoreParams
   }
 }
 
-// One CTA per (axis, layer, kv head, chunk of the head's row).  The CTA first gathers
-// its chunk of every accepted source slot into shared memory, then scatters to the
-// destinations: no write of a plane can precede a read of the same plane, so the
-// copy is overlap-safe like the reference's materialised gather + scatter.
-__global__ void __launch_bounds__(kCommitThreads)
-    kv_commit_kernel(JtKvCommitParams p, int chunk_bytes, int chunks_per_head) {
-  extern __shared__ __align__(16) unsigned char staging[];
-  int plane = blockIdx.x;
-  const int chunk = plane % chunks_per_head;
-  plane /= chunks_per_head;
-  const int head = plane % p.num_kv_heads;
-  plane /= p.num_kv_heads;
-  const int layer = plane % p.num_layers;
-  const int axis = plane / p.num_layers;
-  const int eb = p.elem_bytes;
-  char* base = static_cast<char*>(p.kv_pool) +
-               (axis * p.stride_axis + layer * p.stride_layer + head * p.stride_head) * eb +
-               chunk * chunk_bytes;
-  const int words = chunk_bytes / 16;
-  const int total = p.num_slots * words;
+// Accepted-only commit over the whole GPU.  The copy is cut into 16-byte units, one per
+// (K/V axis, layer, slot, kv head, 16-byte word of the head row), ordered so that
+// neighbouring threads move neighbouring bytes of one slot's rows.  A "plane" is the
+// set of units of one (axis, layer, head chunk, word chunk) over EVERY slot: a write to
+// a plane can only clobber a source row of the same plane, so the reference's
+// gather-before-scatter semantics hold if every unit of a plane is read before any unit
+// of that plane is written.  Planes are processed in groups that fit the shared memory of
+// the whole grid: each CTA gathers its share of the group's units into shared memory,
+// the grid synchronises (cooperative launch: every CTA is resident), and each CTA
+// scatters the units it gathered; the next group starts after a second grid barrier.
+// The grid spans the GPU whatever the number of layers and heads, so a commit of many
+// slots on a single KV head (one GPU of a KV-head-sharded group) is as parallel as one
+// over all heads.
+struct CommitGeom {
+  int heads_per_plane;   // divides num_kv_heads
+  int words_per_plane;   // divides the 16-byte words of a head row
+  int words_per_row;     // 16-byte words of one head row
+  int planes;            // 2 * layers * (heads / heads_per_plane) * (words / words_per_plane)
+  int planes_per_group;
+  int groups;
+  int plane_units;       // num_slots * heads_per_plane * words_per_plane
+};
+
+__device__ __forceinline__ char* commit_unit_address(const JtKvCommitParams& p,
+                                                     const CommitGeom& g, int plane,
+                                                     int rem, const void* slots,
+                                                     int64_t pool_slots, bool* ok) {
+  const int unit_cols = g.heads_per_plane * g.words_per_plane;
+  const int s = rem / unit_cols;
+  const int r2 = rem - s * unit_cols;
+  const int head_in = r2 / g.words_per_plane;
+  const int word_in = r2 - head_in * g.words_per_plane;
+  const int word_chunks = g.words_per_row / g.words_per_plane;
+  const int head_chunks = p.num_kv_heads / g.heads_per_plane;
+  const int wchunk = plane % word_chunks;
+  int rest = plane / word_chunks;
+  const int hchunk = rest % head_chunks;
+  rest /= head_chunks;
+  const int layer = rest % p.num_layers;
+  const int axis = rest / p.num_layers;
+  const int head = hchunk * g.heads_per_plane + head_in;
+  const int word = wchunk * g.words_per_plane + word_in;
+  const int64_t slot = load_slot(slots, p.slot_is_int64, s);
+  *ok = slot >= 0 && slot < pool_slots;
+  if (!*ok) return nullptr;
+  const int64_t page = slot / p.block_size;
+  const int64_t off = slot - page * p.block_size;
+  return static_cast<char*>(p.kv_pool) +
+         (axis * p.stride_axis + layer * p.stride_layer + page * p.stride_block +
+          off * p.stride_offset + static_cast<int64_t>(head) * p.stride_head) *
+             p.elem_bytes +
+         static_cast<int64_t>(word) * 16;
+}
+
+__global__ void __launch_bounds__(kCommitThreads) kv_commit_kernel(JtKvCommitParams p,
+                                                                   CommitGeom g) {
+  extern __shared__ __align__(16) int4 staging[];
+  cg::grid_group grid = cg::this_grid();
   const int64_t pool_slots = p.num_blocks * p.block_size;
-  for (int i = threadIdx.x; i < total; i += kCommitThreads) {
-    const int s = i / words;
-    const int w = i - s * words;
-    const int64_t slot = load_slot(p.source_slots, p.slot_is_int64, s);
-    int4 value = make_int4(0, 0, 0, 0);
-    if (slot >= 0 && slot < pool_slots) {
-      const int64_t page = slot / p.block_size;
-      const int64_t off = slot - page * p.block_size;
-      value = *reinterpret_cast<const int4*>(
-          base + (page * p.stride_block + off * p.stride_offset) * eb + w * 16);
-    } else if (w == 0) {
-      atomicOr(&g_kv_errors, JT_DEVERR_OUT_OF_RANGE);
+  for (int grp = 0; grp < g.groups; ++grp) {
+    const int plane0 = grp * g.planes_per_group;
+    const int planes_here = min(g.planes_per_group, g.planes - plane0);
+    const int64_t units = static_cast<int64_t>(planes_here) * g.plane_units;
+    const int64_t per = (units + gridDim.x - 1) / gridDim.x;
+    const int64_t u0 = min(units, static_cast<int64_t>(blockIdx.x) * per);
+    const int n = static_cast<int>(min(units, u0 + per) - u0);
+    // Gather: kCommitUnroll loads in flight per thread before they are staged.
+    for (int base = threadIdx.x; base < n; base += kCommitThreads * kCommitUnroll) {
+      int4 v[kCommitUnroll];
+#pragma unroll
+      for (int k = 0; k < kCommitUnroll; ++k) {
+        const int i = base + k * kCommitThreads;
+        v[k] = make_int4(0, 0, 0, 0);
+        if (i < n) {
+          const int64_t u = u0 + i;
+          const int plane = plane0 + static_cast<int>(u / g.plane_units);
+          const int rem = static_cast<int>(u % g.plane_units);
+          bool ok = false;
+          const char* src =
+              commit_unit_address(p, g, plane, rem, p.source_slots, pool_slots, &ok);
+          if (ok) v[k] = *reinterpret_cast<const int4*>(src);
+          else atomicOr(&g_kv_errors, JT_DEVERR_OUT_OF_RANGE);
+        }
+      }
+#pragma unroll
+      for (int k = 0; k < kCommitUnroll; ++k) {
+        const int i = base + k * kCommitThreads;
+        if (i < n) staging[i] = v[k];
+      }
     }
-    reinterpret_cast<int4*>(staging)[i] = value;
-  }
-  __syncthreads();
-  for (int i = threadIdx.x; i < total; i += kCommitThreads) {
-    const int s = i / words;
-    const int w = i - s * words;
-    const int64_t slot = load_slot(p.destination_slots, p.slot_is_int64, s);
-    const int64_t src = load_slot(p.source_slots, p.slot_is_int64, s);
-    if (slot < 0 || slot >= pool_slots || src < 0 || src >= pool_slots) {
-      if (w == 0) atomicOr(&g_kv_errors, JT_DEVERR_OUT_OF_RANGE);
-      continue;
+    grid.sync();  // every read of this group's planes precedes every write to them
+    for (int i = threadIdx.x; i < n; i += kCommitThreads) {
+      const int64_t u = u0 + i;
+      const int plane = plane0 + static_cast<int>(u / g.plane_units);
+      const int rem = static_cast<int>(u % g.plane_units);
+      bool src_ok = false, dst_ok = false;
+      commit_unit_address(p, g, plane, rem, p.source_slots, pool_slots, &src_ok);
+      char* dst = commit_unit_address(p, g, plane, rem, p.destination_slots, pool_slots, &dst_ok);
+      if (src_ok && dst_ok) *reinterpret_cast<int4*>(dst) = staging[i];
+      else if (!dst_ok) atomicOr(&g_kv_errors, JT_DEVERR_OUT_OF_RANGE);
     }
-    const int64_t page = slot / p.block_size;
-    const int64_t off = slot - page * p.block_size;
-    *reinterpret_cast<int4*>(base + (page * p.stride_block + off * p.stride_offset) * eb +
-                             w * 16) = reinterpret_cast<const int4*>(staging)[i];
+    if (grp + 1 < g.groups) grid.sync();  // this group's writes precede the next reads
   }
 }
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 bool stride16(int64_t stride, int eb) { return ((stride * eb) & 15) == 0; }
 
-// Largest staging chunk (64, 32 or 16 bytes of each head row) that keeps all
-// num_slots rows of one plane within the shared-memory budget; 0 if none fits.
-int commit_chunk_bytes(int row_bytes, int num_slots) {
-  for (int cb = 64; cb >= 16; cb >>= 1) {
-    if (row_bytes % cb != 0) continue;
-    if (static_cast<int64_t>(num_slots) * cb <= kCommitSmemCap) return cb;
-  }
-  return 0;
+// SM count of the current device (0 when there is none).
+int commit_sms() {
+  int dev = 0, sms = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return 0;
+  if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) return 0;
+  return sms;
+}
+
+// Units one launch can stage at once: one CTA per SM, kCommitSmemCap bytes each.
+int64_t commit_capacity_units(int sms) {
+  return static_cast<int64_t>(std::max(sms, 1)) * (kCommitSmemCap / 16);
 }
 
 }  // namespace
@@ -170,7 +232,11 @@ extern "C" int jt_kv_store_launch(const JtKvStoreParams* p, cudaStream_t stream)
   return jt_cuda_check(cudaGetLastError(), "kv_store launch");
 }
 
-extern "C" int32_t jt_kv_commit_max_slots(void) { return kCommitSmemCap / 16; }
+extern "C" int32_t jt_kv_commit_max_slots(void) {
+  // One plane of one head-row word per slot must fit the grid's staging.
+  const int64_t cap = commit_capacity_units(commit_sms());
+  return static_cast<int32_t>(std::min<int64_t>(cap, 0x7fffffff));
+}
 
 extern "C" int jt_kv_commit_launch(const JtKvCommitParams* p, cudaStream_t stream) {
   if (p == nullptr) return jt_fail(JT_ERR_INVALID, "kv_commit: null params");
@@ -189,20 +255,59 @@ extern "C" int jt_kv_commit_launch(const JtKvCommitParams* p, cudaStream_t strea
       !stride16(p->stride_offset, eb) || !stride16(p->stride_head, eb))
     return jt_fail(JT_ERR_INVALID,
                    "kv_commit: pool rows must be 16-byte aligned with 16-byte multiple strides");
-  const int cb = commit_chunk_bytes(row_bytes, p->num_slots);
-  if (cb == 0)
+  const int sms = commit_sms();
+  if (sms <= 0) return jt_fail(JT_ERR_CUDA, "kv_commit: no CUDA device");
+  const int64_t capacity = commit_capacity_units(sms);
+  const int words = row_bytes / 16;
+  const int64_t n = p->num_slots;
+  // Largest planes that fit the grid's staging: all heads and words of a slot, else one
+  // head's row, else one 16-byte word of it.
+  CommitGeom g{};
+  if (n * p->num_kv_heads * words <= capacity) {
+    g.heads_per_plane = p->num_kv_heads;
+    g.words_per_plane = words;
+  } else if (n * words <= capacity) {
+    g.heads_per_plane = 1;
+    g.words_per_plane = words;
+  } else if (n <= capacity) {
+    g.heads_per_plane = 1;
+    g.words_per_plane = 1;
+  } else {
     return jt_fail(JT_ERR_UNSUPPORTED, "kv_commit: %d slots exceed the per-call limit of %d",
                    p->num_slots, jt_kv_commit_max_slots());
-  const int chunks = row_bytes / cb;
-  const int64_t planes = 2LL * p->num_layers * p->num_kv_heads * chunks;
+  }
+  g.words_per_row = words;
+  const int64_t planes = 2LL * p->num_layers * (p->num_kv_heads / g.heads_per_plane) *
+                         (words / g.words_per_plane);
   if (planes > 0x7fffffff) return jt_fail(JT_ERR_INVALID, "kv_commit: too many planes");
-  const int smem = p->num_slots * cb;
+  g.planes = static_cast<int>(planes);
+  g.plane_units = static_cast<int>(n * g.heads_per_plane * g.words_per_plane);
+  g.planes_per_group = static_cast<int>(std::min<int64_t>(planes, capacity / g.plane_units));
+  g.groups = (g.planes + g.planes_per_group - 1) / g.planes_per_group;
+  const int64_t group_units = static_cast<int64_t>(g.planes_per_group) * g.plane_units;
+  // Enough CTAs for about kCommitThreads * kCommitUnroll units each, at most one per SM
+  // (every CTA must be resident for the grid barrier).
+  const int64_t want = (group_units + kCommitThreads * kCommitUnroll - 1) /
+                       (kCommitThreads * kCommitUnroll);
+  const int grid = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(sms, want)));
+  const int64_t per_cta = (group_units + grid - 1) / grid;
+  const int smem = static_cast<int>(per_cta * 16);
+  if (smem > kCommitSmemCap)
+    return jt_fail(JT_ERR_UNSUPPORTED, "kv_commit: staging of %d bytes per CTA", smem);
   int rc = jt_cuda_check(cudaFuncSetAttribute(kv_commit_kernel,
                                               cudaFuncAttributeMaxDynamicSharedMemorySize,
                                               kCommitSmemCap),
                          "kv_commit smem attribute");
   if (rc != JT_OK) return rc;
-  kv_commit_kernel<<<static_cast<unsigned>(planes), kCommitThreads, smem, stream>>>(*p, cb,
-                                                                                     chunks);
-  return jt_cuda_check(cudaGetLastError(), "kv_commit launch");
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = dim3(static_cast<unsigned>(grid));
+  cfg.blockDim = dim3(kCommitThreads);
+  cfg.dynamicSmemBytes = static_cast<size_t>(smem);
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeCooperative;
+  attr[0].val.cooperative = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return jt_cuda_check(cudaLaunchKernelEx(&cfg, kv_commit_kernel, *p, g), "kv_commit launch");
 }

@@ -24,6 +24,7 @@
 #include <cudaTypedefs.h>
 
 #include <algorithm>
+#include <mutex>
 #include <type_traits>
 
 #include "common.cuh"
@@ -1002,24 +1003,70 @@ constexpr int64_t kStaticPartialBudget = 16ll << 20;    // split-KV partials wit
 
 __device__ __align__(256) unsigned char g_static_workspace[kStaticWorkspaceBytes];
 
-// Device address of g_static_workspace on each device.  In host code the symbol names
-// a host-side stand-in, not device memory, so the address comes from
-// cudaGetSymbolAddress with that device current.
-void* g_static_workspace_ptr[64];
+// Device address of g_static_workspace.  In host code the symbol names a host-side
+// stand-in, not device memory, so the address comes from cudaGetSymbolAddress with the
+// device current.  The address belongs to the module loaded in the CURRENT context: a
+// host that switches contexts (cuCtxCreate / cuCtxSetCurrent) or resets the device
+// (cudaDeviceReset, after which the module is loaded again) sees another address.  So
+// outside stream capture every call looks the address up afresh (a table lookup in the
+// runtime once the module is loaded) and records it with the context it belongs to;
+// during capture, where lookups are best avoided, the recorded address is used only if it
+// was recorded in the same context, and the call is refused otherwise.  The record is
+// guarded by a mutex: several host threads may call at once.
+struct StaticWorkspaceRecord {
+  CUcontext ctx;
+  void* ptr;
+};
+StaticWorkspaceRecord g_static_workspace_rec[64];
+std::mutex g_static_workspace_mutex;
 
-int static_workspace(void** out) {
+using CtxGetCurrentFn = CUresult (*)(CUcontext*);
+CtxGetCurrentFn ctx_get_current() {
+  static CtxGetCurrentFn fn = [] {
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult query{};
+    if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &ptr, cudaEnableDefault, &query) ==
+            cudaSuccess &&
+        query == cudaDriverEntryPointSuccess)
+      return reinterpret_cast<CtxGetCurrentFn>(ptr);
+    return static_cast<CtxGetCurrentFn>(nullptr);
+  }();
+  return fn;
+}
+
+int static_workspace(cudaStream_t stream, void** out) {
   int dev = 0;
   int rc = jt_cuda_check(cudaGetDevice(&dev), "cudaGetDevice");
   if (rc != JT_OK) return rc;
   if (dev < 0 || dev >= 64) return jt_fail(JT_ERR_UNSUPPORTED, "device index %d >= 64", dev);
-  if (g_static_workspace_ptr[dev] == nullptr) {
-    void* ptr = nullptr;
-    rc = jt_cuda_check(cudaGetSymbolAddress(&ptr, g_static_workspace),
+  // The capture query is a runtime call on the stream: it also makes the runtime's
+  // context current in this thread, so the context can be named afterwards.  Nothing
+  // below may synchronise or allocate while a stream is being captured.
+  cudaStreamCaptureStatus status = cudaStreamCaptureStatusNone;
+  const bool capturing = cudaStreamIsCapturing(stream, &status) != cudaSuccess ||
+                         status != cudaStreamCaptureStatusNone;
+  if (capturing) (void)cudaGetLastError();  // clear a refused query's (non-sticky) error
+  void* fresh = nullptr;
+  if (!capturing) {
+    rc = jt_cuda_check(cudaGetSymbolAddress(&fresh, g_static_workspace),
                        "cudaGetSymbolAddress(static workspace)");
     if (rc != JT_OK) return rc;
-    g_static_workspace_ptr[dev] = ptr;
   }
-  *out = g_static_workspace_ptr[dev];
+  CUcontext ctx = nullptr;
+  const CtxGetCurrentFn get_ctx = ctx_get_current();
+  if (get_ctx == nullptr || get_ctx(&ctx) != CUDA_SUCCESS || ctx == nullptr)
+    return jt_fail(JT_ERR_CUDA, "tree_attn_noalloc: cannot read the current CUDA context");
+  std::lock_guard<std::mutex> lock(g_static_workspace_mutex);
+  StaticWorkspaceRecord& rec = g_static_workspace_rec[dev];
+  if (!capturing) {
+    rec.ctx = ctx;
+    rec.ptr = fresh;
+  } else if (rec.ptr == nullptr || rec.ctx != ctx) {
+    return jt_fail(JT_ERR_INVALID,
+                   "tree_attn_noalloc: under stream capture before any call in this CUDA "
+                   "context; make one call outside capture first");
+  }
+  *out = rec.ptr;
   return JT_OK;
 }
 
@@ -1039,7 +1086,7 @@ extern "C" int jt_tree_attn_launch_noalloc(const JtTreeAttnParams* pp, cudaStrea
                    "static capacity of %zu bytes; use jt_tree_attn_launch with a workspace",
                    L.total, kStaticWorkspaceBytes);
   void* scratch = nullptr;
-  rc = static_workspace(&scratch);
+  rc = static_workspace(stream, &scratch);
   if (rc != JT_OK) return rc;
   JtTreeAttnParams p = *pp;
   p.workspace = scratch;

@@ -132,3 +132,25 @@ def test_status_translation():
     with pytest.raises(_lib.KernelLaunchError):
         _lib.check(_lib.JT_ERR_CUDA)
     _lib.check(_lib.JT_OK)
+
+
+def test_noalloc_rejects_geometry_above_the_static_capacity(lib):
+    """A valid launch whose scratch exceeds the 32 MiB static array returns
+    JT_ERR_WORKSPACE, naming the capacity, before any CUDA work (no device needed)."""
+    p = _params(total_queries=1 << 22, num_kv_heads=8)
+    assert lib.jt_tree_attn_launch_noalloc(ctypes.byref(p), None) == _lib.JT_ERR_WORKSPACE
+    message = lib.jt_last_error()
+    assert b"static capacity" in message and str(32 << 20).encode() in message
+
+
+def test_commit_slot_limit_without_a_device(lib):
+    """Without a visible GPU the per-call commit limit is one CTA's staging (12288
+    slots); with one it is that times the SM count."""
+    import torch
+
+    limit = lib.jt_kv_commit_max_slots()
+    if torch.cuda.is_available():
+        sms = torch.cuda.get_device_properties(0).multi_processor_count
+        assert limit == 12288 * sms
+    else:
+        assert limit == 12288
