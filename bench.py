@@ -54,14 +54,16 @@ def parse():
     parser.add_argument("--steps", type=int, default=200)
     parser.add_argument("--warmup", type=int, default=10)
     parser.add_argument("--impl", choices=("ours", "reference", "reference-triton", "accept-walk",
-                                           "metadata-build", "row-linear"),
+                                           "metadata-build", "row-linear", "verify-step"),
                         default="ours",
                         help="reference-triton: the reference's own Triton kernels (installed "
                              "under baseline/_ref) beside ours on configs 1-4, one GPU; "
                              "accept-walk: the round's acceptance step, reference vs device walk; "
                              "metadata-build: round metadata, reference host build vs device build; "
                              "row-linear: the model's o_proj / down_proj (GEMM + all-reduce over "
-                             "the GPUs), reference F.linear + NCCL all_reduce vs the fused kernel")
+                             "the GPUs), reference F.linear + NCCL all_reduce vs the fused kernel; "
+                             "verify-step: config 5, the full Qwen3-8B verify step through the "
+                             "reference's verifier, as shipped vs with this package patched in")
     parser.add_argument("--requests-per-gpu", type=int, default=64)
     parser.add_argument("--no-cpu-baseline", action="store_true")
     parser.add_argument("--skip-extras", action="store_true",
@@ -91,15 +93,19 @@ def global_batch(world: int, requests_per_gpu: int, pool_blocks=None):
 
 # ---- clocks ---------------------------------------------------------------------------
 class ClockSampler:
-    """NVML sampling of SM clock and throttle reasons on a background thread (read-only)."""
+    """NVML sampling of SM clock and throttle reasons on a background thread (read-only).
+
+    Samples carry host timestamps; the sampler starts before the warm-up so that it is
+    already running when the timed region opens, and ``report(t0, t1)`` keeps the samples
+    taken inside [t0, t1] (the timed region by the host clock)."""
 
     REASONS = {0x1: "gpu_idle", 0x2: "applications_clocks_setting", 0x4: "sw_power_cap",
                0x8: "hw_slowdown", 0x10: "sync_boost", 0x20: "sw_thermal_slowdown",
                0x40: "hw_thermal_slowdown", 0x80: "hw_power_brake_slowdown",
                0x100: "display_clock_setting"}
 
-    def __init__(self, index: int, period: float = 0.001):
-        self.samples, self.reasons, self.ok = [], 0, False
+    def __init__(self, index: int, period: float = 0.0005):
+        self.samples = []  # (time, sm_mhz, reasons bitmask)
         self.max_mhz = None
         self._stop = threading.Event()
         try:
@@ -118,8 +124,9 @@ class ClockSampler:
         nv = self._nvml
         while not self._stop.is_set():
             try:
-                self.samples.append(nv.nvmlDeviceGetClockInfo(self._handle, nv.NVML_CLOCK_SM))
-                self.reasons |= int(nv.nvmlDeviceGetCurrentClocksEventReasons(self._handle))
+                mhz = nv.nvmlDeviceGetClockInfo(self._handle, nv.NVML_CLOCK_SM)
+                reasons = int(nv.nvmlDeviceGetCurrentClocksEventReasons(self._handle))
+                self.samples.append((time.perf_counter(), mhz, reasons))
             except Exception:  # noqa: BLE001
                 pass
             time.sleep(self._period)
@@ -134,12 +141,22 @@ class ClockSampler:
         if self.ok:
             self._thread.join()
 
-    def report(self):
+    def report(self, t0: float | None = None, t1: float | None = None):
         if not self.ok or not self.samples:
             return {"sm_mhz": None, "sm_max_mhz": self.max_mhz, "reasons": ["unavailable"]}
-        names = [name for bit, name in self.REASONS.items() if self.reasons & bit]
-        return {"sm_mhz": statistics.median(self.samples), "sm_max_mhz": self.max_mhz,
-                "reasons": names, "samples": len(self.samples)}
+        inside = [s for s in self.samples
+                  if (t0 is None or s[0] >= t0) and (t1 is None or s[0] <= t1)]
+        window = "timed region"
+        if not inside:  # the region was shorter than one NVML round trip: nearest sample
+            mid = 0.5 * ((t0 or 0.0) + (t1 or 0.0))
+            inside = [min(self.samples, key=lambda s: abs(s[0] - mid))]
+            window = "nearest sample to the timed region"
+        bits = 0
+        for _, _, r in inside:
+            bits |= r
+        names = [name for bit, name in self.REASONS.items() if bits & bit]
+        return {"sm_mhz": statistics.median(s[1] for s in inside), "sm_max_mhz": self.max_mhz,
+                "reasons": names, "samples": len(inside), "window": window}
 
 
 # ---- CPU side -------------------------------------------------------------------------
@@ -619,6 +636,154 @@ def run_row_linear(args, rank: int, world: int, local_rank: int):
             torch.distributed.destroy_process_group()
 
 
+def run_verify_step(args, rank: int, world: int, local_rank: int):
+    """Config 5: the full Qwen3-8B tree-verification step (random bf16 weights; 32
+    requests x 2048-token contexts, 64-node trees) through the reference's own verifier at
+    tensor parallelism = the number of GPUs.  Arms: the reference as shipped
+    (target_kernels "fused_rope_gqa": its Triton RoPE scatter and grouped tree kernel,
+    F.linear + NCCL all-reduce, its accept_batch and copy_accepted_kv) and the same code
+    with integration.ReferencePatch applied.  Both run the verify forward + lm_head as the
+    reference's PackedTargetGraph (a CUDA graph per shape, target_graph.py:94-167), then
+    the acceptance walk (rank 0, results broadcast) and the commit of the accepted nodes'
+    K/V over all 36 layers.  Reports verify-forward device time (CUDA events, max over
+    ranks), step wall time (forward + accept + commit, synchronised) and accepted tokens/s
+    per arm, and whether the greedy accepted paths are identical (divergent requests are
+    checked with the reference's argmax-flip witness, restated in verify_step.py)."""
+    ref_root = ROOT / "baseline" / "_ref"
+    if not (ref_root / "nanovllm").is_dir():
+        if rank == 0:
+            print(json.dumps({"impl": "verify-step",
+                              "unavailable": "reference package not installed under baseline/_ref"}))
+        return
+    sys.path.insert(0, str(ref_root))
+    import torch.distributed as dist
+    from jetspec_b200 import verify_step
+    from jetspec_b200.integration import ReferencePatch
+    from nanovllm.speculative.jetspec.target_graph import PackedTargetGraph
+    device = torch.device("cuda", local_rank)
+    torch.cuda.set_device(device)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=device)
+    else:
+        import socket
+        with socket.socket() as sock:
+            sock.bind(("127.0.0.1", 0))
+            port = sock.getsockname()[1]
+        dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=0,
+                                world_size=1)
+    graphs = []
+    try:
+        config = verify_step.qwen3_8b_config(num_layers=36)
+        model = verify_step.build_reference_model(config, device)
+        verify_step.set_target_kernels(model, "fused_rope_gqa")
+        heads = config.num_key_value_heads // world
+        inputs = verify_step.make_inputs(config, device, kv_heads=heads)
+        rng = np.random.default_rng(55)
+        planted = rng.integers(0, 9, size=32).tolist()
+        verify_step.plant_paths(model, inputs, planted)
+        steps, warmup = max(args.steps, 1), max(args.warmup, 3)
+
+        def share(results):
+            if world == 1:
+                return results
+            box = [results]
+            dist.broadcast_object_list(box, src=0)
+            return box[0]
+
+        def run_arm(name):
+            graph = PackedTargetGraph(model, inputs.kv_pool, (), 4096)
+            graphs.append(graph)
+            execution = "cuda_graph"
+
+            def verify():
+                nonlocal execution
+                try:
+                    logits, _ = graph.verify(inputs.tokens, inputs.positions, inputs.metadata)
+                except Exception as exc:  # noqa: BLE001 - capture refused: eager
+                    execution = f"eager ({type(exc).__name__})"
+                    logits = verify_step.verify_logits(model, inputs)
+                return logits
+
+            def step():
+                logits = verify()
+                results = verify_step.accept(logits, inputs) if rank == 0 else None
+                results = share(results)
+                verify_step.commit(inputs, results)
+                return logits, results
+
+            for _ in range(warmup):
+                logits, results = step()
+            torch.cuda.synchronize(device)
+            if world > 1:
+                dist.barrier()
+            walls, fwd = [], []
+            for _ in range(steps):
+                start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                t0 = time.perf_counter()
+                start.record()
+                logits = verify()
+                end.record()
+                results = verify_step.accept(logits, inputs) if rank == 0 else None
+                results = share(results)
+                verify_step.commit(inputs, results)
+                torch.cuda.synchronize(device)
+                walls.append((time.perf_counter() - t0) * 1e3)
+                fwd.append(start.elapsed_time(end))
+            wall_ms, fwd_ms = max_over_ranks([statistics.median(walls), statistics.median(fwd)],
+                                             world, device)
+            tokens = sum(len(r["outputs"]) for r in results)
+            kept = logits.float().clone() if logits is not None else None
+            return {"verify_forward_ms": fwd_ms, "step_ms": wall_ms,
+                    "accepted_tokens_per_step": tokens,
+                    "accepted_tokens_per_s": tokens / (wall_ms * 1e-3),
+                    "execution": execution}, kept, results
+
+        ref_line, ref_logits, ref_results = run_arm("reference")
+        with ReferencePatch(model):
+            our_line, our_logits, our_results = run_arm("ours")
+        line = {"impl": "verify-step", "n_gpus": world, "steps": steps, "warmup": warmup,
+                "config": {"workload": "config5: Qwen3-8B (36 layers, random bf16 weights), "
+                                       "32 requests x 2048-token contexts, 64-node trees",
+                           "tensor_parallel": world, "kv_heads_per_gpu": heads,
+                           "planted_path_lengths": planted},
+                "reference": ref_line, "ours": our_line,
+                "speedup_verify_forward": ref_line["verify_forward_ms"] / our_line["verify_forward_ms"],
+                "speedup_step": ref_line["step_ms"] / our_line["step_ms"]}
+        if rank == 0:
+            divergent = verify_step.first_divergence(our_results, ref_results)
+            witnesses = []
+            for r, k in enumerate(divergent):
+                if k is None:
+                    continue
+                row = inputs.offsets[r] + ref_results[r]["path"][k - 1]
+                w = verify_step.argmax_flip_witness(our_logits[row:row + 1], ref_logits[row:row + 1])
+                witnesses.append({"request": r, "path_index": k,
+                                  "consistent": w["all_flip_witnesses_consistent"],
+                                  "flipped": w["argmax_flips"] == 1,
+                                  "delta": w["rows"][0]["logits_inf_delta"],
+                                  "margin": w["rows"][0]["reference_top2_margin"]})
+            line.update({
+                "paths_identical": sum(d is None for d in divergent),
+                "requests": len(divergent), "divergent": witnesses,
+                "logits_max_abs_diff": float((our_logits - ref_logits).abs().max()),
+                "accepted_lengths_reference": [r["accepted_length"] for r in ref_results],
+                "accepted_lengths_ours": [r["accepted_length"] for r in our_results],
+                "errors": jb.read_device_errors()})
+            print(json.dumps(line), flush=True)
+    finally:
+        for graph in graphs:
+            graph.close()
+        graphs.clear()
+        from jetspec_b200.row_linear import _GROUPS
+        if world > 1 and _GROUPS:
+            torch.cuda.synchronize(device)
+            dist.barrier()
+        for state in list(_GROUPS.values()):
+            state.close()
+        _GROUPS.clear()
+        dist.destroy_process_group()
+
+
 # ---- GPU side -------------------------------------------------------------------------
 class Step:
     """Device-resident inputs of one verify step on this rank's KV-head shard."""
@@ -700,17 +865,18 @@ def time_device(step: Step, steps: int, warmup: int, world: int, device):
         parts = [g.replay for g in graphs]
     else:
         parts = [step.store, step.attend, step.commit]
-    for _ in range(warmup):
-        for part in parts:
-            part()
-    torch.cuda.synchronize(device)
-    if world > 1:
-        torch.distributed.barrier()
-    stream = torch.cuda.current_stream(device)
-    start = torch.cuda.Event(enable_timing=True)
-    end = torch.cuda.Event(enable_timing=True)
-    marks = [[torch.cuda.Event(enable_timing=True) for _ in range(4)] for _ in range(steps)]
     with ClockSampler(device.index) as clocks:
+        for _ in range(warmup):
+            for part in parts:
+                part()
+        torch.cuda.synchronize(device)
+        if world > 1:
+            torch.distributed.barrier()
+        stream = torch.cuda.current_stream(device)
+        start = torch.cuda.Event(enable_timing=True)
+        end = torch.cuda.Event(enable_timing=True)
+        marks = [[torch.cuda.Event(enable_timing=True) for _ in range(4)] for _ in range(steps)]
+        t0 = time.perf_counter()
         start.record(stream)
         for i in range(steps):
             marks[i][0].record(stream)
@@ -718,13 +884,18 @@ def time_device(step: Step, steps: int, warmup: int, world: int, device):
                 part()
                 marks[i][k + 1].record(stream)
         end.record(stream)
+        # Poll (GIL released while sleeping) rather than block, so the sampler thread
+        # keeps sampling while the GPU drains the queued steps.
+        while not end.query():
+            time.sleep(0.0002)
+        t1 = time.perf_counter()
         torch.cuda.synchronize(device)
     if world > 1:
         torch.distributed.barrier()
     total_ms = start.elapsed_time(end)
     split = [sum(m[k].elapsed_time(m[k + 1]) for m in marks) / steps for k in range(3)]
     launch = "cuda-graph replay" if graphs is not None else "eager"
-    return total_ms, split, clocks.report(), launch
+    return total_ms, split, clocks.report(t0, t1), launch
 
 
 def time_e2e(step: Step, steps: int, warmup: int, world: int, device):
@@ -907,6 +1078,8 @@ def main():
         return run_metadata_build(args, rank)
     if args.impl == "row-linear":
         return run_row_linear(args, rank, world, local_rank)
+    if args.impl == "verify-step":
+        return run_verify_step(args, rank, world, local_rank)
     if world != args.gpus and "WORLD_SIZE" in os.environ:
         args.gpus = world
     device = torch.device("cuda", local_rank)

@@ -42,6 +42,9 @@ extern "C" int jt_read_device_errors(uint32_t* errors) {
   uint32_t f = 0;
   rc = jt_read_errors_rowlin(&f);
   if (rc != JT_OK) return rc;
-  *errors = a | b | c | d | e | f;
+  uint32_t g = 0;
+  rc = jt_read_errors_f32(&g);
+  if (rc != JT_OK) return rc;
+  *errors = a | b | c | d | e | f | g;
   return JT_OK;
 }

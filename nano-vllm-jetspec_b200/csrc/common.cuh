@@ -22,6 +22,10 @@ int jt_read_errors_rope(uint32_t* bits);
 int jt_read_errors_accept(uint32_t* bits);
 int jt_read_errors_meta(uint32_t* bits);
 int jt_read_errors_rowlin(uint32_t* bits);
+int jt_read_errors_f32(uint32_t* bits);
+
+// fp32-operand tree attention (tree_attn_f32.cu), for parameters the entry point checked.
+int jt_tree_attn_f32_launch(const JtTreeAttnParams& p, cudaStream_t stream);
 
 #define JT_DEVERR_OUT_OF_RANGE 1u
 #define JT_DEVERR_TREE_TOO_LARGE 2u

@@ -939,8 +939,8 @@ int validate_params(const JtTreeAttnParams& p) {
     return jt_fail(JT_ERR_INVALID, "tree_attn: invalid geometry");
   if (p.head_dim != 64 && p.head_dim != 128)
     return jt_fail(JT_ERR_UNSUPPORTED, "tree_attn: head_dim %d not in {64, 128}", p.head_dim);
-  if (p.dtype != JT_BF16 && p.dtype != JT_F16)
-    return jt_fail(JT_ERR_UNSUPPORTED, "tree_attn: operands must be bf16 or f16");
+  if (p.dtype != JT_BF16 && p.dtype != JT_F16 && p.dtype != JT_F32)
+    return jt_fail(JT_ERR_UNSUPPORTED, "tree_attn: operands must be bf16, f16 or f32");
   if (p.out_dtype != p.dtype && p.out_dtype != JT_F32)
     return jt_fail(JT_ERR_INVALID, "tree_attn: output dtype must match input or be f32");
   if (!p.out || !p.q || !p.k_pool || !p.v_pool || !p.cu_seqlens_q || !p.query_to_request ||
@@ -986,6 +986,8 @@ extern "C" int jt_tree_attn_launch(const JtTreeAttnParams* pp, cudaStream_t stre
   if (pp == nullptr) return jt_fail(JT_ERR_INVALID, "tree_attn: null params");
   const int rc = validate_params(*pp);
   if (rc != JT_OK) return rc;
+  // fp32 operands: the CUDA-core kernel, which needs no workspace.
+  if (pp->dtype == JT_F32) return jt_tree_attn_f32_launch(*pp, stream);
   return run_tree_attn(*pp, kPartialBudgetBytes, stream);
 }
 
@@ -1076,6 +1078,7 @@ extern "C" int jt_tree_attn_launch_noalloc(const JtTreeAttnParams* pp, cudaStrea
   if (pp == nullptr) return jt_fail(JT_ERR_INVALID, "tree_attn_noalloc: null params");
   int rc = validate_params(*pp);
   if (rc != JT_OK) return rc;
+  if (pp->dtype == JT_F32) return jt_tree_attn_f32_launch(*pp, stream);  // no scratch at all
   const bool tc_core = tcgen05_eligible(*pp);
   const Layout L = make_layout(pp->num_requests, pp->total_queries, pp->num_kv_heads,
                                pp->groups, pp->head_dim, kStaticPartialBudget,

@@ -8,7 +8,9 @@ Every backend runs the sm_100a kernel; they differ only in the probability arith
 * ``"auto"``, ``"reference"``, ``"prefix"`` - near-fp32 probabilities in PV (hi + lo
   split of each probability), the reference's FP32-probability contract for these
   backends (paged_backend.py:1-7).  The reference's sm_120-only prefix specialisation
-  has no separate meaning on B200.
+  has no separate meaning on B200.  These three also take fp32 q / k / v, as the
+  reference's do (paged_backend.py:290-305, tree_attention.py:21-62): fp32 operands run
+  on the CUDA-core fp32 kernel, every product, sum and softmax step in fp32.
 """
 from __future__ import annotations
 

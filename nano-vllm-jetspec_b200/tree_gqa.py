@@ -66,14 +66,16 @@ def launch_tree_attention(out, q, k_pool, v_pool, metadata, scale, groups, *,
                           fp32_probability=False, split_keys=0, portable_core=False):
     """Fill ``out`` through jt_tree_attn_launch on the current stream (validated args).
 
-    ``portable_core`` forces the warp-level mma.sync core instead of the tcgen05 core
-    (used to cross-check the two kernels); head_dim 64 always runs on it.
+    bf16 / f16 operands run on the tensor-core kernels: ``portable_core`` forces the
+    warp-level mma.sync core instead of the tcgen05 core (used to cross-check the two
+    kernels); head_dim 64 always runs on it.  fp32 operands run on the CUDA-core fp32
+    kernel (fp32 products, sums and softmax; no workspace).
     """
     lib = _lib.load_library()
     if q.shape[-1] not in SUPPORTED_HEAD_DIMS:
         raise ValueError(f"head_dim {q.shape[-1]} is not in {SUPPORTED_HEAD_DIMS}")
-    if q.dtype not in (torch.bfloat16, torch.float16):
-        raise ValueError("grouped Tensor Core tree attention requires BF16 or FP16")
+    if q.dtype not in (torch.bfloat16, torch.float16, torch.float32):
+        raise ValueError("tree attention operands must be BF16, FP16 or FP32")
     if k_pool.stride(-1) != 1 or v_pool.stride(-1) != 1 or out.stride(-1) != 1:
         raise ValueError("K/V pools and output need a contiguous head dimension")
     _check_metadata(metadata)
@@ -82,10 +84,12 @@ def launch_tree_attention(out, q, k_pool, v_pool, metadata, scale, groups, *,
     total = int(metadata.total_queries)
     kv_heads = int(k_pool.shape[2])
     head_dim = int(q.shape[-1])
-    size = ctypes.c_size_t(0)
-    _lib.check(lib.jt_tree_attn_workspace_size(num_requests, total, kv_heads, int(groups),
-                                               head_dim, ctypes.byref(size)))
-    scratch = _launch.workspace(device, size.value)
+    scratch = None
+    if q.dtype != torch.float32:
+        size = ctypes.c_size_t(0)
+        _lib.check(lib.jt_tree_attn_workspace_size(num_requests, total, kv_heads, int(groups),
+                                                   head_dim, ctypes.byref(size)))
+        scratch = _launch.workspace(device, size.value)
     p = _lib.JtTreeAttnParams()
     p.out, p.q, p.k_pool, p.v_pool = out.data_ptr(), q.data_ptr(), k_pool.data_ptr(), v_pool.data_ptr()
     p.cu_seqlens_q = metadata.cu_seqlens_q.data_ptr()
@@ -113,8 +117,8 @@ def launch_tree_attention(out, q, k_pool, v_pool, metadata, scale, groups, *,
     p.v_stride0, p.v_stride1, p.v_stride2 = v_pool.stride(0), v_pool.stride(1), v_pool.stride(2)
     p.scale = float(scale)
     p.split_keys = int(split_keys)
-    p.workspace = scratch.data_ptr()
-    p.workspace_bytes = scratch.numel()
+    p.workspace = None if scratch is None else scratch.data_ptr()
+    p.workspace_bytes = 0 if scratch is None else scratch.numel()
     _lib.check(lib.jt_tree_attn_launch(ctypes.byref(p), _launch.stream_handle(device)))
     return out
 

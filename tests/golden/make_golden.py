@@ -19,6 +19,11 @@ Everything here executes the reference's own code on the CPU:
                                                                   -> accept.npz
   * layers/linear.py RowParallelLinear (weight_loader + forward: F.linear on each rank's
     shard, dist.all_reduce over gloo ranks on the CPU, bf16)       -> row_linear.npz
+  * benchmarks/jetspec_numeric_oracles.py argmax_flip_witness (near-tie explanation of a
+    greedy-path difference between two verifiers)                 -> witness.npz
+
+``--only NAME [NAME ...]`` regenerates just the named groups (metadata, kv, rope, accept,
+row_linear, witness, attention).
 
 The fixtures hold only live K/V rows (bf16 bit patterns) plus seeds and shapes, so they
 stay small; the tests rebuild the NaN-poisoned pools from them.  The GPU box never runs
@@ -377,18 +382,59 @@ def row_linear_cases():
     print("row_linear: %d cases" % len(ROW_LINEAR_CASES))
 
 
+def witness_cases():
+    """The reference's argmax_flip_witness on seeded logits pairs: near-tie rows with small
+    perturbations (flips inside the 2-delta envelope), exact ties in the reference
+    (first-index rule), rows where the actual logits promote a far-behind candidate (a
+    flip whose delta is large) and unflipped rows."""
+    sys.path.insert(0, str(REFERENCE / "benchmarks"))
+    from jetspec_numeric_oracles import argmax_flip_witness
+
+    gen = torch.Generator().manual_seed(171)
+    vocab, rows = 512, 24
+    reference = torch.randn((rows, vocab), generator=gen, dtype=torch.float64)
+    actual = reference + 1e-3 * torch.randn((rows, vocab), generator=gen, dtype=torch.float64)
+    for r in range(0, 8):  # near-ties: runner-up within 1e-4 of the winner
+        top = torch.topk(reference[r], 2)
+        reference[r, top.indices[1]] = top.values[0] - 1e-4
+        actual[r] = reference[r] + 1e-3 * torch.randn(vocab, generator=gen, dtype=torch.float64)
+    for r in (8, 9):  # exact tie in the reference: argmax takes the first index
+        top = torch.topk(reference[r], 2)
+        reference[r, top.indices[1]] = top.values[0]
+    for r in (10, 11):  # large-margin flips: actual promotes a far-behind candidate
+        low = int(reference[r].argmin())
+        actual[r, low] = reference[r].max() + 5.0
+    result = argmax_flip_witness(actual, reference)
+    rows_out = result["rows"]
+    np.savez_compressed(
+        HERE / "witness.npz", actual=actual.numpy(), reference=reference.numpy(),
+        argmax_flips=result["argmax_flips"], large_margin_violations=result["large_margin_violations"],
+        flipped=np.array([r["argmax_flipped"] for r in rows_out]),
+        violation=np.array([r["large_margin_violation"] for r in rows_out]),
+        within=np.array([r["flip_within_error_envelope"] is True for r in rows_out]),
+        actual_argmax=np.array([r["actual_argmax"] for r in rows_out]),
+        reference_argmax=np.array([r["reference_argmax"] for r in rows_out]),
+        delta=np.array([r["logits_inf_delta"] for r in rows_out]),
+        margin=np.array([r["reference_top2_margin"] for r in rows_out]))
+
+
 def main():
     parser = argparse.ArgumentParser()
     parser.add_argument("--reference", required=True, help="path of the reference checkout")
+    parser.add_argument("--only", nargs="*", default=None)
     args = parser.parse_args()
     global REFERENCE
     REFERENCE = Path(args.reference).resolve()
     sys.path.insert(0, str(REFERENCE))
-    metadata_case()
-    kv_cases()
-    rope_cases()
-    accept_cases()
-    row_linear_cases()
+    groups = {"metadata": metadata_case, "kv": kv_cases, "rope": rope_cases,
+              "accept": accept_cases, "row_linear": row_linear_cases,
+              "witness": witness_cases}
+    wanted = set(args.only) if args.only else set(groups) | {"attention"}
+    for name, fn in groups.items():
+        if name in wanted:
+            fn()
+    if "attention" not in wanted:
+        return
     rng = np.random.default_rng(7)
     parents = [random_parents(rng, n) for n in (7, 5, 9)]
     attention_case("ragged3", (65, 0, 257), ((2,), (), (4, 0)), parents, 6 * 256, 8,
