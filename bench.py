@@ -749,23 +749,18 @@ def run_verify_step(args, rank: int, world: int, local_rank: int):
                 "reference": ref_line, "ours": our_line,
                 "speedup_verify_forward": ref_line["verify_forward_ms"] / our_line["verify_forward_ms"],
                 "speedup_step": ref_line["step_ms"] / our_line["step_ms"]}
+        # The reference's own spread: its fp32-probability kernels (fused_rope) against the
+        # shipped bf16-probability ones, on the same round (one eager forward).
+        verify_step.set_target_kernels(model, "fused_rope")
+        alt_logits = verify_step.verify_logits(model, inputs)
+        verify_step.set_target_kernels(model, "fused_rope_gqa")
         if rank == 0:
-            divergent = verify_step.first_divergence(our_results, ref_results)
-            witnesses = []
-            for r, k in enumerate(divergent):
-                if k is None:
-                    continue
-                row = inputs.offsets[r] + ref_results[r]["path"][k - 1]
-                w = verify_step.argmax_flip_witness(our_logits[row:row + 1], ref_logits[row:row + 1])
-                witnesses.append({"request": r, "path_index": k,
-                                  "consistent": w["all_flip_witnesses_consistent"],
-                                  "flipped": w["argmax_flips"] == 1,
-                                  "delta": w["rows"][0]["logits_inf_delta"],
-                                  "margin": w["rows"][0]["reference_top2_margin"]})
+            alt_results = verify_step.accept(alt_logits, inputs)
+            line["parity"] = verify_step.divergence_report(our_results, ref_results, our_logits,
+                                                           ref_logits, inputs)
+            line["reference_spread"] = verify_step.divergence_report(
+                alt_results, ref_results, alt_logits.float(), ref_logits, inputs)
             line.update({
-                "paths_identical": sum(d is None for d in divergent),
-                "requests": len(divergent), "divergent": witnesses,
-                "logits_max_abs_diff": float((our_logits - ref_logits).abs().max()),
                 "accepted_lengths_reference": [r["accepted_length"] for r in ref_results],
                 "accepted_lengths_ours": [r["accepted_length"] for r in our_results],
                 "errors": jb.read_device_errors()})

@@ -18,6 +18,7 @@ Importing this module needs the reference package (``nanovllm``) on ``sys.path``
 from __future__ import annotations
 
 from dataclasses import dataclass
+import math
 from types import SimpleNamespace
 import zlib
 
@@ -66,9 +67,13 @@ def _hf_weights(config):
 def build_reference_model(config, device, seed: int = 5, std: float = 0.02):
     """The reference's Qwen3ForCausalLM on ``device`` (bf16), weights loaded through its
     own weight loaders from seeded synthetic checkpoint tensors: dense weights
-    N(0, std^2), norm weights 1.  Every rank generates the same global tensor per name, so
-    tensor-parallel shards agree.  Needs torch.distributed initialised (the reference's
-    layers read the rank and world size when built)."""
+    N(0, std^2), the projections that write into the residual stream (o_proj, down_proj)
+    N(0, (std / sqrt(2 x layers))^2) as in GPT-2's initialisation (so that the residual
+    stream does not grow layer after layer and the random network is not chaotic: a
+    rounding difference early in the stack then stays a rounding difference at the logits,
+    as in a trained model), norm weights 1.  Every rank generates the same global tensor
+    per name, so tensor-parallel shards agree.  Needs torch.distributed initialised (the
+    reference's layers read the rank and world size when built)."""
     from nanovllm.models.qwen3 import Qwen3ForCausalLM
 
     previous = torch.get_default_dtype()
@@ -86,7 +91,10 @@ def build_reference_model(config, device, seed: int = 5, std: float = 0.02):
                 tensor = torch.ones(shape, dtype=torch.bfloat16, device=device)
             else:
                 gen.manual_seed(seed * 1_000_003 + zlib.crc32(name.encode()))
-                tensor = (torch.randn(shape, generator=gen, device=device) * std).bfloat16()
+                scale = std
+                if "o_proj" in name or "down_proj" in name:
+                    scale = std / math.sqrt(2 * config.num_hidden_layers)
+                tensor = (torch.randn(shape, generator=gen, device=device) * scale).bfloat16()
             for key, (target, shard) in mapping.items():
                 if key in name:
                     param = model.get_parameter(name.replace(key, target))
@@ -347,3 +355,23 @@ def argmax_flip_witness(logits_a: torch.Tensor, logits_b: torch.Tensor) -> dict:
     return {"rows_checked": len(rows), "argmax_flips": flips,
             "large_margin_violations": violations,
             "all_flip_witnesses_consistent": violations == 0, "rows": rows}
+
+
+def divergence_report(actual, reference, actual_logits, reference_logits, inputs) -> dict:
+    """Accepted-path agreement of two verifiers on the same round: identical requests, and
+    for each divergent one the argmax-flip witness at the node where the paths part (the
+    last common node, whose greedy token differs)."""
+    divergent = first_divergence(actual, reference)
+    rows = []
+    for r, k in enumerate(divergent):
+        if k is None:
+            continue
+        row = inputs.offsets[r] + reference[r]["path"][k - 1]
+        w = argmax_flip_witness(actual_logits[row:row + 1], reference_logits[row:row + 1])
+        rows.append({"request": r, "path_index": k, "flipped": w["argmax_flips"] == 1,
+                     "consistent": w["all_flip_witnesses_consistent"],
+                     "delta": w["rows"][0]["logits_inf_delta"],
+                     "margin": w["rows"][0]["reference_top2_margin"]})
+    return {"paths_identical": sum(d is None for d in divergent), "requests": len(divergent),
+            "logits_max_abs_diff": float((actual_logits.float() - reference_logits.float()).abs().max()),
+            "divergent": rows}
