@@ -18,6 +18,7 @@ All compute runs in libjetspec_b200.so (hand-written CUDA for sm_100a) through a
 library every operator raises LibraryMissingError.
 """
 from ._lib import KernelLaunchError, LibraryMissingError, load_library, read_device_errors
+from . import ops  # noqa: F401  (registers the jetspec_b200:: custom operators)
 from .accept import accept_batch, accept_walk
 from .attention import store_kvcache
 from .packed_metadata import PackedTreeMetadata, ancestor_mask_from_parents

@@ -21,6 +21,11 @@ def store_kvcache(key: torch.Tensor, value: torch.Tensor, k_cache: torch.Tensor,
     assert key.stride(1) == head_dim and value.stride(1) == head_dim
     assert k_cache.stride(1) == D and v_cache.stride(1) == D
     assert slot_mapping.numel() == N
+    from . import ops
+
+    if ops.compiling():
+        torch.ops.jetspec_b200.kv_store_(key, value, k_cache, v_cache, slot_mapping)
+        return
     _store(key, value, k_cache, v_cache, slot_mapping)
 
 

@@ -1,10 +1,11 @@
 """Accepted-only KV commit: drop-in for ``copy_accepted_kv``.
 
 Same signature, return value and ValueError behaviour as
-nanovllm/speculative/jetspec/state.py:64-86.  The copy runs as one sm_100a kernel over
-every (K/V axis, layer, kv head) plane of the pool; each plane gathers all its source
-rows before scattering, so overlapping source/destination slot sets give the same bytes
-as the reference's materialised advanced-index copy.
+nanovllm/speculative/jetspec/state.py:64-86.  The copy runs as one cooperative sm_100a
+kernel spread over the whole GPU; every source row of a (K/V axis, layer) plane is read
+before any row of that plane is written (a grid barrier between the gather and the
+scatter), so overlapping source/destination slot sets give the same bytes as the
+reference's materialised advanced-index copy.
 """
 from __future__ import annotations
 
@@ -54,7 +55,19 @@ def copy_accepted_kv(kv_pool: torch.Tensor, source_slots: torch.Tensor,
     destination_slots = destination_slots.contiguous()
     if kv_pool.stride(-1) != 1:
         raise ValueError("KV pool needs a contiguous head dimension")
+    from . import ops
+
+    if ops.compiling():
+        torch.ops.jetspec_b200.kv_commit_(kv_pool, source_slots, destination_slots, int(block_size))
+    else:
+        _commit(kv_pool, source_slots, destination_slots, block_size)
+    return int(payload)
+
+
+def _commit(kv_pool, source_slots, destination_slots, block_size) -> None:
+    """jt_kv_commit_launch on the current stream (validated arguments)."""
     lib = _lib.load_library()
+    n = int(source_slots.numel())
     if n > lib.jt_kv_commit_max_slots():
         raise ValueError(f"KV commit of {n} slots exceeds the per-call limit "
                          f"{lib.jt_kv_commit_max_slots()}")
@@ -74,4 +87,3 @@ def copy_accepted_kv(kv_pool: torch.Tensor, source_slots: torch.Tensor,
     p.stride_axis, p.stride_layer, p.stride_block, p.stride_offset, p.stride_head = \
         s[0], s[1], s[2], s[3], s[4]
     _lib.check(lib.jt_kv_commit_launch(ctypes.byref(p), _launch.stream_handle(kv_pool.device)))
-    return int(payload)

@@ -19,6 +19,11 @@ def scatter_tree_kv(k: torch.Tensor, v: torch.Tensor, k_pool: torch.Tensor,
     """Write node K/V rows [Q, kv_heads, dim] to their scratch slots (bit-exact)."""
     if k.ndim != 3 or v.shape != k.shape or node_slots.shape != (k.shape[0],):
         raise ValueError("node K/V must be [rows, kv_heads, dim] with one slot per row")
+    from . import ops
+
+    if ops.compiling():
+        torch.ops.jetspec_b200.kv_store_(k, v, k_pool, v_pool, node_slots.contiguous())
+        return
     _store(k, v, k_pool, v_pool, node_slots.contiguous())
 
 
@@ -119,6 +124,18 @@ def rope_scatter_prevalidated(q, k, v, positions, cos_sin_cache, k_pool, v_pool,
     """Launch-only serving boundary (tree_fusion.py:181-199): one sm_100a kernel, no
     allocation, download or synchronisation; the caller guarantees the invariants that
     ``rope_scatter`` checks."""
+    from . import ops
+
+    if ops.compiling():
+        torch.ops.jetspec_b200.rope_scatter_(q, k, v, positions, cos_sin_cache, k_pool, v_pool,
+                                             node_slots, out)
+        return out
+    return _rope_scatter_launch(q, k, v, positions, cos_sin_cache, k_pool, v_pool, node_slots,
+                                out)
+
+
+def _rope_scatter_launch(q, k, v, positions, cos_sin_cache, k_pool, v_pool, node_slots, out):
+    """jt_rope_scatter_launch on the current stream."""
     import ctypes
 
     from . import _launch, _lib

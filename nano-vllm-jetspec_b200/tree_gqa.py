@@ -64,6 +64,25 @@ def _check_metadata(metadata):
 
 def launch_tree_attention(out, q, k_pool, v_pool, metadata, scale, groups, *,
                           fp32_probability=False, split_keys=0, portable_core=False):
+    """Fill ``out`` on the current stream (validated args): directly, or through the
+    ``jetspec_b200::tree_attention_`` operator while torch.compile traces the caller."""
+    from . import ops
+
+    if ops.compiling():
+        torch.ops.jetspec_b200.tree_attention_(
+            out, q, k_pool, v_pool, metadata.cu_seqlens_q, metadata.query_to_request,
+            metadata.query_local_row, metadata.prefix_lens, metadata.node_counts,
+            metadata.block_tables, metadata.tree_slots, metadata.qq_bias,
+            metadata.qq_bias_offsets, int(metadata.block_size), float(scale), int(groups),
+            bool(fp32_probability), int(split_keys), bool(portable_core))
+        return out
+    return launch_tree_attention_eager(out, q, k_pool, v_pool, metadata, scale, groups,
+                                       fp32_probability=fp32_probability,
+                                       split_keys=split_keys, portable_core=portable_core)
+
+
+def launch_tree_attention_eager(out, q, k_pool, v_pool, metadata, scale, groups, *,
+                                fp32_probability=False, split_keys=0, portable_core=False):
     """Fill ``out`` through jt_tree_attn_launch on the current stream (validated args).
 
     bf16 / f16 operands run on the tensor-core kernels: ``portable_core`` forces the

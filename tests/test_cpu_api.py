@@ -97,3 +97,30 @@ def test_workloads_are_seeded_and_consistent():
     c1 = workloads.config1()
     assert c1.prefix_lens == [512] and c1.block_tables == [[3, 0]] and c1.node_counts == [16]
     assert c1.commit_slots()[1] == [512, 513, 514, 515, 516]
+
+
+def test_custom_operators_are_registered_with_fake_implementations():
+    """The launchers are torch.library operators (what a torch.compile'd caller traces);
+    their fake implementations accept meta tensors and write nothing."""
+    import torch
+
+    import jetspec_b200  # noqa: F401  (registers the operators)
+
+    ops = torch.ops.jetspec_b200
+    for name in ("tree_attention_", "kv_store_", "kv_commit_", "rope_scatter_"):
+        assert hasattr(ops, name), name
+    meta = torch.device("meta")
+    out = torch.empty((8, 4, 128), device=meta)
+    q = torch.empty((8, 4, 128), dtype=torch.bfloat16, device=meta)
+    pool = torch.empty((4, 256, 1, 128), dtype=torch.bfloat16, device=meta)
+    i32 = lambda n: torch.empty(n, dtype=torch.int32, device=meta)  # noqa: E731
+    ops.tree_attention_(out, q, pool, pool, i32(2), i32(8), i32(8), i32(1), i32(1),
+                        torch.empty((1, 1), dtype=torch.int32, device=meta),
+                        torch.empty(8, dtype=torch.int64, device=meta),
+                        torch.empty(64, device=meta), torch.empty(2, dtype=torch.int64, device=meta),
+                        256, 0.1, 4, False, 0, False)
+    kv = torch.empty((2, 1, 4, 256, 1, 128), dtype=torch.bfloat16, device=meta)
+    ops.kv_commit_(kv, torch.empty(3, dtype=torch.int64, device=meta),
+                   torch.empty(3, dtype=torch.int64, device=meta), 256)
+    rows = torch.empty((8, 1, 128), dtype=torch.bfloat16, device=meta)
+    ops.kv_store_(rows, rows, pool, pool, torch.empty(8, dtype=torch.int64, device=meta))
