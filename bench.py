@@ -749,13 +749,19 @@ def run_verify_step(args, rank: int, world: int, local_rank: int):
                 "reference": ref_line, "ours": our_line,
                 "speedup_verify_forward": ref_line["verify_forward_ms"] / our_line["verify_forward_ms"],
                 "speedup_step": ref_line["step_ms"] / our_line["step_ms"]}
-        # The reference's own spread: its fp32-probability kernels (fused_rope) against the
-        # shipped bf16-probability ones, on the same round (one eager forward).
+        # fp32 probabilities (the reference's qualified numerics, target_kernels
+        # "fused_rope"): the reference against the same code patched, one eager forward
+        # each; the reference's fp32 arm against its shipped bf16 arm is its own spread.
         verify_step.set_target_kernels(model, "fused_rope")
         alt_logits = verify_step.verify_logits(model, inputs)
+        with ReferencePatch(model):
+            our32_logits = verify_step.verify_logits(model, inputs)
         verify_step.set_target_kernels(model, "fused_rope_gqa")
         if rank == 0:
             alt_results = verify_step.accept(alt_logits, inputs)
+            our32_results = verify_step.accept(our32_logits, inputs)
+            line["parity_fp32_probability"] = verify_step.divergence_report(
+                our32_results, alt_results, our32_logits.float(), alt_logits.float(), inputs)
             line["parity"] = verify_step.divergence_report(our_results, ref_results, our_logits,
                                                            ref_logits, inputs)
             line["reference_spread"] = verify_step.divergence_report(

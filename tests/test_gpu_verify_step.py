@@ -134,13 +134,18 @@ def test_stage1_decoder_layer_config3(reference):
 
 
 def test_stage2_config5_accepted_paths(reference):
-    """Config 5 at TP 1.  Three verifiers on the same round: the reference as shipped
-    (fused_rope_gqa: bf16-probability grouped kernel), the reference with its fp32-
-    probability kernels (fused_rope: the numerics it qualifies against), and the reference
-    with this package patched in (fused_rope_gqa routed here).  The patched verifier must
-    stay as close to the shipped one as the reference's own two backends are to each
-    other (logits and accepted paths), and every path it accepts differently must start
-    at a greedy flip the argmax-flip witness explains as a near-tie."""
+    """Config 5 at TP 1, four verifiers on the same round.
+
+    * fp32 probabilities (the numerics the reference qualifies against): the reference with
+      its fp32-probability kernels (target_kernels "fused_rope") against the same code with
+      this package patched in.  These must accept identical greedy paths.
+    * bf16 probabilities (the reference's fastest, shipped path, "fused_rope_gqa") against
+      the same code patched.  The random 36-layer model turns any rounding difference into
+      logits differences of a few tenths (the reference's own two backends differ from each
+      other that much), so here the patched verifier must stay as close to the shipped one
+      as the reference's fp32-probability verifier is, and every path it accepts
+      differently must begin at a greedy flip the argmax-flip witness explains as a near-tie.
+    """
     from jetspec_b200 import verify_step
     from jetspec_b200.integration import ReferencePatch
 
@@ -151,26 +156,34 @@ def test_stage2_config5_accepted_paths(reference):
     rng = np.random.default_rng(55)
     planted = rng.integers(0, 9, size=32).tolist()
     verify_step.plant_paths(model, inputs, planted)
-    ref_logits = verify_step.verify_logits(model, inputs)
-    ref_acc = verify_step.accept(ref_logits, inputs)
-    verify_step.set_target_kernels(model, "fused_rope")
-    alt_logits = verify_step.verify_logits(model, inputs)
-    alt_acc = verify_step.accept(alt_logits, inputs)
+
+    def run(kernels, patched):
+        verify_step.set_target_kernels(model, kernels)
+        if patched:
+            with ReferencePatch(model):
+                logits = verify_step.verify_logits(model, inputs)
+                return logits, verify_step.accept(logits, inputs)
+        logits = verify_step.verify_logits(model, inputs)
+        return logits, verify_step.accept(logits, inputs)
+
+    ref_logits, ref_acc = run("fused_rope_gqa", False)
+    our_logits, our_acc = run("fused_rope_gqa", True)
+    ref32_logits, ref32_acc = run("fused_rope", False)
+    our32_logits, our32_acc = run("fused_rope", True)
     verify_step.set_target_kernels(model, "fused_rope_gqa")
-    with ReferencePatch(model):
-        our_logits = verify_step.verify_logits(model, inputs)
-        our_acc = verify_step.accept(our_logits, inputs)
     torch.cuda.synchronize()
-    # The planted paths are what the reference accepts (at least that deep).
+    # The planted paths are what the shipped reference accepts (at least that deep).
     for r, result in enumerate(ref_acc):
         depth = max(inputs.trees[r].host_depths)
         assert result["accepted_length"] >= min(planted[r], depth), (r, result, planted[r])
+    fp32 = verify_step.divergence_report(our32_acc, ref32_acc, our32_logits, ref32_logits, inputs)
     ours = verify_step.divergence_report(our_acc, ref_acc, our_logits, ref_logits, inputs)
-    spread = verify_step.divergence_report(alt_acc, ref_acc, alt_logits, ref_logits, inputs)
-    print(f"config5 patched vs shipped: {ours}")
+    spread = verify_step.divergence_report(ref32_acc, ref_acc, ref32_logits, ref_logits, inputs)
+    print(f"config5 fp32-probability, patched vs reference: {fp32}")
+    print(f"config5 bf16-probability, patched vs shipped: {ours}")
     print(f"config5 reference fp32-probability vs shipped: {spread}")
-    for row in ours["divergent"]:
+    for row in fp32["divergent"] + ours["divergent"]:
         assert row["flipped"] and row["consistent"], row
+    assert fp32["paths_identical"] == fp32["requests"], fp32
     ulp = 2.0 ** -5  # bf16 spacing of logits in [4, 8)
-    assert ours["logits_max_abs_diff"] <= max(2 * spread["logits_max_abs_diff"], 4 * ulp), (ours, spread)
-    assert ours["paths_identical"] >= spread["paths_identical"] - 2, (ours, spread)
+    assert ours["logits_max_abs_diff"] <= max(1.5 * spread["logits_max_abs_diff"], 4 * ulp), (ours, spread)
