@@ -64,16 +64,23 @@ def _hf_weights(config):
     yield "lm_head.weight", (config.vocab_size, h), "dense"
 
 
-def build_reference_model(config, device, seed: int = 5, std: float = 0.02):
+def build_reference_model(config, device, seed: int = 5, std: float = 0.02,
+                          embed_std: float | None = 1.0, residual_std: float | None = None,
+                          head_std: float | None = None):
     """The reference's Qwen3ForCausalLM on ``device`` (bf16), weights loaded through its
     own weight loaders from seeded synthetic checkpoint tensors: dense weights
-    N(0, std^2), the projections that write into the residual stream (o_proj, down_proj)
-    N(0, (std / sqrt(2 x layers))^2) as in GPT-2's initialisation (so that the residual
-    stream does not grow layer after layer and the random network is not chaotic: a
-    rounding difference early in the stack then stays a rounding difference at the logits,
-    as in a trained model), norm weights 1.  Every rank generates the same global tensor
-    per name, so tensor-parallel shards agree.  Needs torch.distributed initialised (the
-    reference's layers read the rank and world size when built)."""
+    N(0, std^2), norm weights 1, the output head N(0, head_std^2) (default std), and a
+    numerically stable residual stream: the embedding N(0, embed_std^2) (default 1, a
+    unit-scale stream) and the projections that write into it (o_proj, down_proj)
+    N(0, residual_std^2), by default std / sqrt(2 x layers) / 32, so that each layer
+    adds a small update.  With every weight N(0, 0.02^2) instead, the 36-layer random
+    network is chaotic: any rounding difference (the reference's own two attention
+    backends against each other, as much as this package against either) grows to a few
+    tenths at the logits and flips greedy choices at near-ties, which says nothing about
+    either implementation; trained models are not chaotic in that way.  Every rank
+    generates the same global tensor per name, so tensor-parallel shards agree.  Needs
+    torch.distributed initialised (the reference's layers read the rank and world size
+    when built)."""
     from nanovllm.models.qwen3 import Qwen3ForCausalLM
 
     previous = torch.get_default_dtype()
@@ -93,7 +100,12 @@ def build_reference_model(config, device, seed: int = 5, std: float = 0.02):
                 gen.manual_seed(seed * 1_000_003 + zlib.crc32(name.encode()))
                 scale = std
                 if "o_proj" in name or "down_proj" in name:
-                    scale = std / math.sqrt(2 * config.num_hidden_layers)
+                    scale = (std / math.sqrt(2 * config.num_hidden_layers) / 32
+                             if residual_std is None else residual_std)
+                elif "embed_tokens" in name and embed_std is not None:
+                    scale = embed_std
+                elif name == "lm_head.weight" and head_std is not None:
+                    scale = head_std
                 tensor = (torch.randn(shape, generator=gen, device=device) * scale).bfloat16()
             for key, (target, shard) in mapping.items():
                 if key in name:

@@ -134,17 +134,17 @@ def test_stage1_decoder_layer_config3(reference):
 
 
 def test_stage2_config5_accepted_paths(reference):
-    """Config 5 at TP 1, four verifiers on the same round.
+    """Config 5 at TP 1, four verifiers on the same round, on the numerically stable
+    synthetic Qwen3-8B (verify_step.build_reference_model):
 
     * fp32 probabilities (the numerics the reference qualifies against): the reference with
       its fp32-probability kernels (target_kernels "fused_rope") against the same code with
-      this package patched in.  These must accept identical greedy paths.
+      this package patched in;
     * bf16 probabilities (the reference's fastest, shipped path, "fused_rope_gqa") against
-      the same code patched.  The random 36-layer model turns any rounding difference into
-      logits differences of a few tenths (the reference's own two backends differ from each
-      other that much), so here the patched verifier must stay as close to the shipped one
-      as the reference's fp32-probability verifier is, and every path it accepts
-      differently must begin at a greedy flip the argmax-flip witness explains as a near-tie.
+      the same code patched.
+
+    Both pairs must accept identical greedy paths (and corrections) for every request;
+    the reference's own two backends against each other are reported beside them.
     """
     from jetspec_b200 import verify_step
     from jetspec_b200.integration import ReferencePatch
@@ -185,5 +185,4 @@ def test_stage2_config5_accepted_paths(reference):
     for row in fp32["divergent"] + ours["divergent"]:
         assert row["flipped"] and row["consistent"], row
     assert fp32["paths_identical"] == fp32["requests"], fp32
-    ulp = 2.0 ** -5  # bf16 spacing of logits in [4, 8)
-    assert ours["logits_max_abs_diff"] <= max(1.5 * spread["logits_max_abs_diff"], 4 * ulp), (ours, spread)
+    assert ours["paths_identical"] == ours["requests"], ours
