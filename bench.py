@@ -66,6 +66,10 @@ def parse():
                              "reference's verifier, as shipped vs with this package patched in")
     parser.add_argument("--requests-per-gpu", type=int, default=64)
     parser.add_argument("--no-cpu-baseline", action="store_true")
+    parser.add_argument("--model-init", choices=("stable", "uniform"), default="stable",
+                        help="verify-step: the numerically stable synthetic Qwen3-8B (default) "
+                             "or every weight at std 0.02 with GPT-2-scaled residual "
+                             "projections (a chaotic random network)")
     parser.add_argument("--skip-extras", action="store_true",
                         help="omit the config-4 strong-scaling and row-linear records")
     parser.add_argument("--cpu-seconds", type=float, default=12.0,
@@ -674,7 +678,9 @@ def run_verify_step(args, rank: int, world: int, local_rank: int):
     graphs = []
     try:
         config = verify_step.qwen3_8b_config(num_layers=36)
-        model = verify_step.build_reference_model(config, device)
+        init = {} if args.model_init == "stable" else {"embed_std": None,
+                                                       "residual_std": 0.02 / 72 ** 0.5}
+        model = verify_step.build_reference_model(config, device, **init)
         verify_step.set_target_kernels(model, "fused_rope_gqa")
         heads = config.num_key_value_heads // world
         inputs = verify_step.make_inputs(config, device, kv_heads=heads)
@@ -745,6 +751,7 @@ def run_verify_step(args, rank: int, world: int, local_rank: int):
                 "config": {"workload": "config5: Qwen3-8B (36 layers, random bf16 weights), "
                                        "32 requests x 2048-token contexts, 64-node trees",
                            "tensor_parallel": world, "kv_heads_per_gpu": heads,
+                           "model_init": args.model_init,
                            "planted_path_lengths": planted},
                 "reference": ref_line, "ours": our_line,
                 "speedup_verify_forward": ref_line["verify_forward_ms"] / our_line["verify_forward_ms"],

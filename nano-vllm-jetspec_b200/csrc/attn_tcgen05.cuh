@@ -12,23 +12,20 @@
 //   warps 1-3    loaders: TMA for the query tile and for prefix K/V tiles (128 keys inside
 //                one page, 128-byte swizzle), cp.async for tiles that touch the tree
 //                nodes (scattered scratch slots), written in the same swizzled layout
-//   warps 4-11   softmax + epilogue: warp w owns score rows (TMEM lanes) 32 (w % 4) +
-//                16 ((w - 4) / 4) + [0, 16), read and written with the 16-lane TMEM shapes;
-//                each row's 128 keys (and 128 output columns) are spread over the four
-//                threads of one quad, so row maxima and sums are two shuffles and no
-//                softmax warp ever waits for another
+//   warps 4-11   softmax + epilogue: warpgroup c (warps 4+4c..7+4c) owns keys 64c..64c+63
+//                of every key tile and output columns 64c..64c+63; thread t owns score
+//                row t (its TMEM lane)
 //
 // TMEM holds O (128 columns) and three S buffers (128 columns each).  Per key tile t:
 // S = Q K_t^T (tcgen05.mma M128 N128 K16, both operands in shared memory) into buffer
-// t % 3; each softmax warp reads its 16 rows of S, and writes P (rounded to the operand
-// type, in pairs) over the first 64 columns of those rows; O += P V_t (tcgen05.mma with A
-// from TMEM, V MN-major in shared memory).  With three S buffers the QKs run up to three
-// tiles ahead of the softmax, which therefore never waits for the tensor core; it only
-// waits for the previous PV before it rescales O, and the running max moves (O rescaled
-// in TMEM) only when it grows by more than 2^8, so P stays <= 256 and rescales are rare.
-// The epilogue reads O into registers and releases it at once, so the next item's PVs
-// overlap this item's output stores.  K and V tiles share one five-slot ring filled in the
-// MMA's consumption order.
+// t % 3; the softmax reads its half of S, swaps half-row maxima with the other warpgroup,
+// and writes P (rounded to the operand type) over the S columns it read; O += P V_t
+// (tcgen05.mma with A from TMEM, V MN-major in shared memory).  With three S buffers the
+// QKs run up to three tiles ahead of the softmax, which therefore never waits for the
+// tensor core; it only waits for the previous PV before it rescales O, and the running
+// max moves (O rescaled in TMEM) only when it grows by more than 2^8, so P stays <= 256
+// and rescales are rare.  K and V tiles share one five-slot ring filled in the MMA's
+// consumption order.
 //
 // Every mbarrier wait is bounded and every waiter consumes every phase of the barriers it
 // waits on, in order (parity waits are unambiguous only within one phase), except the
@@ -55,7 +52,9 @@ constexpr int kOffQ = 0;
 constexpr int kOffRing = kOffQ + kQTileBytes;
 constexpr int kOffBar = kOffRing + kRing * kKVBytes;
 constexpr int kOffMisc = kOffBar + 8 * 32;
-constexpr int kOffItem = kOffMisc + 64;                 // [2] decoded work items (16 ints)
+constexpr int kOffXl = kOffMisc + 64;                   // [2 halves][128] row sums
+constexpr int kOffXm = kOffXl + 2 * kM * 4;             // [tile parity][2 halves][128] maxima
+constexpr int kOffItem = kOffXm + 4 * kM * 4;           // [2] decoded work items (16 ints)
 constexpr int kMaskWordsMax = 32;                       // tree nodes per request <= 1024
 constexpr int kOffMask = kOffItem + 2 * 64;             // single-launch mode: the item's
                                                         // ancestor bitmasks [128][32] words
@@ -66,12 +65,13 @@ constexpr long long kWaitLimit = 4000000000ll;          // cycles (~2 s) per wai
 // TMEM column map (512 columns x 128 lanes x 32 bit): O, then the S buffers.
 __host__ __device__ constexpr uint32_t col_o() { return 0u; }
 __host__ __device__ constexpr uint32_t col_s(int b) { return 128u + 128u * b; }
-// P of keys 16kk..16kk+15 (operand-type pairs, 8 columns) inside an S buffer: the
-// probabilities of the tile's 128 keys, packed in pairs, over the buffer's first 64 columns
-// (each softmax warp overwrites only the rows it owns, after it has read their scores);
-// fp32-probability low parts follow 64 columns later.
-__host__ __device__ constexpr uint32_t col_p(int kk) { return 8u * kk; }
-constexpr uint32_t kColPLow = 64;
+// P of keys 16kk..16kk+15 (operand-type pairs, 8 columns) inside an S buffer: each softmax
+// warpgroup writes the probabilities of its 64 keys inside the S columns it owns (keys
+// 0..63 -> columns 0..31, keys 64..127 -> columns 64..95); fp32-probability low parts
+// follow 32 columns later.
+__host__ __device__ constexpr uint32_t col_p(int kk) {
+  return kk < 4 ? 8u * kk : 64u + 8u * (kk - 4);
+}
 
 // Barrier indices.
 constexpr int kBarFull = 0;                    // [kRing]  loader warps (+ TMA bytes)
@@ -82,7 +82,8 @@ constexpr int kBarSFull = 12;                  // [kSBufs] MMA commit per QK
 constexpr int kBarPFull = 15;                  // [kSBufs] 8 softmax warps
 constexpr int kBarPvDone = 18;                 // [kSBufs] MMA commit per PV (by P's S buffer)
 constexpr int kBarOFree = 21;                  // 8 softmax warps after the epilogue
-// (22, 23: unused)
+constexpr int kBarMx = 22;                     // 8 softmax warps: half maxima swapped
+constexpr int kBarLx = 23;                     // 8 softmax warps: half row sums swapped
 constexpr int kSoftmaxWarps = 8;
 constexpr int kBarDrain = 24;
 constexpr int kBarItemFull = 25;               // [2] work-item ring
@@ -284,28 +285,6 @@ __device__ __forceinline__ void tmem_st8(uint32_t taddr, const uint32_t (&v)[8])
                "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]),
                "r"(v[7]));
 }
-// 16-lane shapes (the softmax's layout).  For a warp whose TMEM lane base is L, thread t
-// (quad = t / 4, t0 = t % 4) holds rows L + quad (a = 0) and L + quad + 8 (a = 1):
-//   16x256b.x16: register c + 2a + 4b <-> (row a, column 8b + 2 t0 + c), b < 16
-//   16x128b.x16: register a + 2b      <-> (row a, column 4b + t0),        b < 16
-// so a row's 128 columns are spread over the four threads of one quad.
-__device__ __forceinline__ void tmem_ld_16x256b_x16(uint32_t taddr, uint32_t (&v)[64]) {
-  asm volatile(
-      "tcgen05.ld.sync.aligned.16x256b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32,%33,%34,%35,%36,%37,%38,%39,%40,%41,%42,%43,%44,%45,%46,%47,%48,%49,%50,%51,%52,%53,%54,%55,%56,%57,%58,%59,%60,%61,%62,%63}, [%64];\n"
-      : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]), "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15]), "=r"(v[16]), "=r"(v[17]), "=r"(v[18]), "=r"(v[19]), "=r"(v[20]), "=r"(v[21]), "=r"(v[22]), "=r"(v[23]), "=r"(v[24]), "=r"(v[25]), "=r"(v[26]), "=r"(v[27]), "=r"(v[28]), "=r"(v[29]), "=r"(v[30]), "=r"(v[31]), "=r"(v[32]), "=r"(v[33]), "=r"(v[34]), "=r"(v[35]), "=r"(v[36]), "=r"(v[37]), "=r"(v[38]), "=r"(v[39]), "=r"(v[40]), "=r"(v[41]), "=r"(v[42]), "=r"(v[43]), "=r"(v[44]), "=r"(v[45]), "=r"(v[46]), "=r"(v[47]), "=r"(v[48]), "=r"(v[49]), "=r"(v[50]), "=r"(v[51]), "=r"(v[52]), "=r"(v[53]), "=r"(v[54]), "=r"(v[55]), "=r"(v[56]), "=r"(v[57]), "=r"(v[58]), "=r"(v[59]), "=r"(v[60]), "=r"(v[61]), "=r"(v[62]), "=r"(v[63])
-      : "r"(taddr));
-}
-__device__ __forceinline__ void tmem_st_16x256b_x16(uint32_t taddr, const uint32_t (&v)[64]) {
-  asm volatile(
-      "tcgen05.st.sync.aligned.16x256b.x16.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32,%33,%34,%35,%36,%37,%38,%39,%40,%41,%42,%43,%44,%45,%46,%47,%48,%49,%50,%51,%52,%53,%54,%55,%56,%57,%58,%59,%60,%61,%62,%63,%64};\n" ::"r"(taddr),
-      "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]), "r"(v[8]), "r"(v[9]), "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15]), "r"(v[16]), "r"(v[17]), "r"(v[18]), "r"(v[19]), "r"(v[20]), "r"(v[21]), "r"(v[22]), "r"(v[23]), "r"(v[24]), "r"(v[25]), "r"(v[26]), "r"(v[27]), "r"(v[28]), "r"(v[29]), "r"(v[30]), "r"(v[31]), "r"(v[32]), "r"(v[33]), "r"(v[34]), "r"(v[35]), "r"(v[36]), "r"(v[37]), "r"(v[38]), "r"(v[39]), "r"(v[40]), "r"(v[41]), "r"(v[42]), "r"(v[43]), "r"(v[44]), "r"(v[45]), "r"(v[46]), "r"(v[47]), "r"(v[48]), "r"(v[49]), "r"(v[50]), "r"(v[51]), "r"(v[52]), "r"(v[53]), "r"(v[54]), "r"(v[55]), "r"(v[56]), "r"(v[57]), "r"(v[58]), "r"(v[59]), "r"(v[60]), "r"(v[61]), "r"(v[62]), "r"(v[63]));
-}
-__device__ __forceinline__ void tmem_st_16x128b_x16(uint32_t taddr, const uint32_t (&v)[32]) {
-  asm volatile(
-      "tcgen05.st.sync.aligned.16x128b.x16.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};\n" ::"r"(taddr),
-      "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]), "r"(v[8]), "r"(v[9]), "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15]), "r"(v[16]), "r"(v[17]), "r"(v[18]), "r"(v[19]), "r"(v[20]), "r"(v[21]), "r"(v[22]), "r"(v[23]), "r"(v[24]), "r"(v[25]), "r"(v[26]), "r"(v[27]), "r"(v[28]), "r"(v[29]), "r"(v[30]), "r"(v[31]));
-}
-
 __device__ __forceinline__ void tmem_wait_ld() {
   asm volatile("tcgen05.wait::ld.sync.aligned;\n" ::: "memory");
 }
@@ -466,12 +445,20 @@ __device__ __forceinline__ void gather_kv_tile(const JtTreeAttnParams& p, const 
   asm volatile("cp.async.wait_all;\n" ::: "memory");
   fence_proxy_async();
 }
-// Softmax of one 128-key tile for the two score rows a thread holds (see the 16-lane TMEM
-// shapes above: rows `lane base + quad` and `+ 8`, keys 8b + 2 t0 + c).  `vk` describes the
-// tile for masked tiles: keys kb..kb+127, prefix P, range end and nodes T.
+// Softmax helpers for one score row (the calling thread's TMEM lane) of one 128-key tile.
+// `vk` describes the tile for masked tiles: keys kb..kb+127, prefix P, range end, nodes T
+// and the row's ancestor bitmask (row_ok false masks the whole row).
 struct TileKeys {
   int kb, P, key_end, T;
+  const uint32_t* mask_row;
+  bool row_ok;
 };
+
+template <bool kMasked>
+__device__ __forceinline__ uint32_t chunk_visibility(const TileKeys& vk, int h) {
+  if constexpr (!kMasked) return 0xffffffffu;
+  return vk.row_ok ? visible_bits(vk.kb + 32 * h, vk.P, vk.key_end, vk.T, vk.mask_row) : 0u;
+}
 
 // Exponentials of score pairs on the FMA pipe, relieving the MUFU unit (16 results per
 // clock per SM) that otherwise bounds the softmax.  2^x = 2^j * 2^f with j = rint(x) taken
@@ -506,157 +493,103 @@ __host__ __device__ constexpr bool poly_pair(int c) {
   return kPolyPairs > 0 && (c % (16 / (kPolyPairs > 0 ? kPolyPairs : 1))) ==
                                (16 / (kPolyPairs > 0 ? kPolyPairs : 1)) - 1;
 }
-// One tile for the calling thread's two rows: load their 64 scores (16x256b), mask (tiles
-// that touch tree nodes), take each row's max over the quad (two shuffles: every row's 128
-// keys are spread over the four threads of one quad, so no other warp is involved), move
-// the lazy running max (log2 units; it moves only when the tile max exceeds it by more than
-// 8, and `alpha` is then the factor the older O and partial sum must take), and write
-// P = exp2(s * scale_log2 - m), rounded to the operand type, in pairs (16x128b) over the
-// first 64 columns of the S buffer.  `rsum` gets this thread's fp32 sum of P per row.
+// Softmax of one score row for one key half.  The two softmax warpgroups share every
+// 128-key tile: warpgroup `c` owns keys 64c..64c+63, i.e. S columns 64c..64c+63, and only
+// ever reads or writes those.  Each thread loads its 64 scores (two 32-column TMEM loads,
+// one wait), publishes its half's max in `xm` and meets the other warpgroup on `mx_bar`
+// (a rendezvous of the eight softmax warps), so both derive the same running max.  The running max is
+// lazy: it moves only when the tile max exceeds it by more than 8 (log2 units).  P =
+// exp2(s * scale_log2 - m), rounded to the operand type, goes to this half's columns
+// (col_p).  Returns the fp32 sum of this half's P; `alpha` is the factor the older O and
+// partial sum must take.
 template <typename Elem, bool FP32P, bool kMasked>
-__device__ __forceinline__ void softmax_tile(uint32_t s_addr, const TileKeys& vk,
-                                             const uint32_t* const (&mask_row)[2],
-                                             const bool (&row_ok)[2], int t0,
-                                             float scale_log2, float (&m_run)[2],
-                                             float (&alpha)[2], float (&rsum)[2]) {
+__device__ __forceinline__ float softmax_half(uint32_t s_addr, int c, const TileKeys& vk,
+                                              float scale_log2, float& m_run, float& alpha,
+                                              float* xm_mine, const float* xm_other,
+                                              uint32_t mx_bar, uint32_t mx_parity,
+                                              volatile int* abort) {
   using Mma = jt::MmaOp<Elem>;
+  const int own = 64 * c;
   uint32_t v[64];
-  tmem_ld_16x256b_x16(s_addr, v);
-  uint32_t vis[2][4];
+#pragma unroll
+  for (int h = 0; h < 2; ++h)
+    tmem_ld32(s_addr + own + 32 * h, *reinterpret_cast<uint32_t(*)[32]>(v + 32 * h));
+  uint32_t vw[2];
   if constexpr (kMasked) {
-    // Word i holds keys 32i..32i+31, shifted so that bit 8 (b & 3) + c is key 8b + 2 t0 + c.
 #pragma unroll
-    for (int a = 0; a < 2; ++a)
-#pragma unroll
-      for (int i = 0; i < 4; ++i)
-        vis[a][i] = row_ok[a] ? visible_bits(vk.kb + 32 * i, vk.P, vk.key_end, vk.T, mask_row[a]) >>
-                                    (2 * t0)
-                              : 0u;
+    for (int h = 0; h < 2; ++h) vw[h] = chunk_visibility<true>(vk, 2 * c + h);
   }
   tmem_wait_ld();
   if constexpr (kMasked) {
 #pragma unroll
-    for (int a = 0; a < 2; ++a)
-#pragma unroll
-      for (int b = 0; b < 16; ++b)
-#pragma unroll
-        for (int c = 0; c < 2; ++c)
-          if (!((vis[a][b >> 2] >> (8 * (b & 3) + c)) & 1u))
-            v[c + 2 * a + 4 * b] = __float_as_uint(-INFINITY);
+    for (int k = 0; k < 64; ++k)
+      if (!((vw[k >> 5] >> (k & 31)) & 1u)) v[k] = __float_as_uint(-INFINITY);
   }
-  float neg[2];
+  float m8[8];
 #pragma unroll
-  for (int a = 0; a < 2; ++a) {
-    float m0 = fmaxf(__uint_as_float(v[2 * a]), __uint_as_float(v[1 + 2 * a]));
-    float m1 = fmaxf(__uint_as_float(v[2 * a + 4]), __uint_as_float(v[1 + 2 * a + 4]));
+  for (int k = 0; k < 8; ++k) m8[k] = fmaxf(__uint_as_float(v[k]), __uint_as_float(v[k + 8]));
 #pragma unroll
-    for (int b = 2; b < 16; b += 2) {
-      m0 = max3f(m0, __uint_as_float(v[2 * a + 4 * b]), __uint_as_float(v[1 + 2 * a + 4 * b]));
-      m1 = max3f(m1, __uint_as_float(v[2 * a + 4 * b + 4]),
-                 __uint_as_float(v[1 + 2 * a + 4 * b + 4]));
-    }
-    float m = fmaxf(m0, m1);
-    m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 1));
-    m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 2));
-    // Raw max; scale > 0 keeps the order.
-    const float mx = m * scale_log2;
-    alpha[a] = 1.f;
-    if (mx > m_run[a] + 8.f) {
-      if (m_run[a] != -INFINITY) alpha[a] = jt::fast_exp2(m_run[a] - mx);
-      m_run[a] = mx;
-    }
-    neg[a] = m_run[a] == -INFINITY ? 0.f : -m_run[a];
+  for (int k0 = 16; k0 < 64; k0 += 16)
+#pragma unroll
+    for (int k = 0; k < 8; ++k)
+      m8[k] = max3f(m8[k], __uint_as_float(v[k0 + k]), __uint_as_float(v[k0 + k + 8]));
+  const float half_max = max3f(max3f(m8[0], m8[1], m8[2]), max3f(m8[3], m8[4], m8[5]),
+                               fmaxf(m8[6], m8[7]));
+  *xm_mine = half_max;
+  warp_arrive(mx_bar);
+  warp_wait(mx_bar, mx_parity, abort);
+  // Raw max; scale > 0 keeps the order.
+  const float mx = fmaxf(half_max, *xm_other) * scale_log2;
+  alpha = 1.f;
+  if (mx > m_run + 8.f) {
+    if (m_run != -INFINITY) alpha = jt::fast_exp2(m_run - mx);
+    m_run = mx;
   }
+  const float neg_m = m_run == -INFINITY ? 0.f : -m_run;
   const float2 scale2 = make_float2(scale_log2, scale_log2);
-  uint32_t ph[32];
-  uint32_t pl[FP32P ? 32 : 1];
+  const float2 neg2 = make_float2(neg_m, neg_m);
+  float2 r2[2] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
+  const uint32_t p_addr = s_addr + col_p(4 * c);
 #pragma unroll
-  for (int a = 0; a < 2; ++a) {
-    const float2 neg2 = make_float2(neg[a], neg[a]);
-    float2 r2[2] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
+  for (int h = 0; h < 2; ++h) {
+    uint32_t ph[16];
+    uint32_t pl[FP32P ? 16 : 1];
 #pragma unroll
-    for (int b = 0; b < 16; ++b) {
+    for (int k = 0; k < 16; ++k) {
       const float2 x = __ffma2_rn(
-          make_float2(__uint_as_float(v[2 * a + 4 * b]), __uint_as_float(v[1 + 2 * a + 4 * b])),
+          make_float2(__uint_as_float(v[32 * h + 2 * k]), __uint_as_float(v[32 * h + 2 * k + 1])),
           scale2, neg2);
       float2 e;
-      if (!kMasked && !FP32P && poly_pair(b))
+      if (!kMasked && !FP32P && poly_pair(k))
         e = exp2_poly2(x);
       else
         e = make_float2(jt::fast_exp2(x.x), jt::fast_exp2(x.y));
-      r2[b & 1] = __fadd2_rn(r2[b & 1], e);
-      ph[a + 2 * b] = Mma::pack(e.x, e.y);
+      r2[k & 1] = __fadd2_rn(r2[k & 1], e);
+      ph[k] = Mma::pack(e.x, e.y);
       if constexpr (FP32P) {
-        const float2 r = Mma::unpack(ph[a + 2 * b]);
-        pl[a + 2 * b] = Mma::pack(e.x - r.x, e.y - r.y);
+        const float2 r = Mma::unpack(ph[k]);
+        pl[k] = Mma::pack(e.x - r.x, e.y - r.y);
       }
     }
-    rsum[a] = (r2[0].x + r2[1].x) + (r2[0].y + r2[1].y);
+    tmem_st16(p_addr + 16 * h, ph);
+    if constexpr (FP32P) tmem_st16(p_addr + 32 + 16 * h, pl);
   }
-  tmem_st_16x128b_x16(s_addr + col_p(0), ph);
-  if constexpr (FP32P) tmem_st_16x128b_x16(s_addr + col_p(0) + kColPLow, pl);
+  return (r2[0].x + r2[1].x) + (r2[0].y + r2[1].y);
 }
 
-// Zero P for the rows of a warp with no live row.
+// Zero P for this warpgroup's 64 keys (rows of a warp with no live row).
 template <bool FP32P>
-__device__ __forceinline__ void write_zero_tile(uint32_t s_addr) {
-  uint32_t z[32];
+__device__ __forceinline__ void write_zero_half(uint32_t s_addr, int c) {
+  uint32_t z[16];
 #pragma unroll
-  for (int k = 0; k < 32; ++k) z[k] = 0u;
-  tmem_st_16x128b_x16(s_addr + col_p(0), z);
-  if constexpr (FP32P) tmem_st_16x128b_x16(s_addr + col_p(0) + kColPLow, z);
-}
-
-// Four 32-bit values per quad lane, transposed within the quad: y[s] = x[t0] of quad lane s.
-// After it, lane t0 holds the four column pairs (8B..8B+7) of block B = 4g + t0 that lanes
-// 0..3 held for it, i.e. 16 contiguous output bytes.  `mask` names the quad's lanes.
-__device__ __forceinline__ void quad_transpose(const uint32_t (&x)[4], uint32_t (&y)[4], int t0,
-                                               uint32_t mask) {
+  for (int k = 0; k < 16; ++k) z[k] = 0u;
+  const uint32_t p_addr = s_addr + col_p(4 * c);
 #pragma unroll
-  for (int k = 0; k < 4; ++k) {
-    const int idx = t0 ^ k;
-    uint32_t send = x[0];
-    send = idx == 1 ? x[1] : send;
-    send = idx == 2 ? x[2] : send;
-    send = idx == 3 ? x[3] : send;
-    const uint32_t recv = k == 0 ? send : __shfl_xor_sync(mask, send, k);
-#pragma unroll
-    for (int i = 0; i < 4; ++i) y[i] = idx == i ? recv : y[i];
+  for (int h = 0; h < 2; ++h) {
+    tmem_st16(p_addr + 16 * h, z);
+    if constexpr (FP32P) tmem_st16(p_addr + 32 + 16 * h, z);
   }
 }
-
-// Stores one score row's 128 outputs (this thread's 32 of them, o[c + 2a + 4b] for row a)
-// scaled by `inv`: operand-type rows as 16-byte pieces after a quad transpose, fp32 rows as
-// 8-byte pairs.  Every lane of the quad must call it (the transpose), `store` decides
-// whether the row is written.
-template <typename Elem>
-__device__ __forceinline__ void store_row(const JtTreeAttnParams& p, int64_t off, const float* o,
-                                          int a, float inv, int t0, uint32_t mask, bool store) {
-  using Mma = jt::MmaOp<Elem>;
-  if (p.out_dtype == JT_F32) {
-    if (!store) return;
-    float* dst = static_cast<float*>(p.out) + off + 2 * t0;
-#pragma unroll
-    for (int b = 0; b < 16; ++b)
-      *reinterpret_cast<float2*>(dst + 8 * b) =
-          make_float2(o[2 * a + 4 * b] * inv, o[1 + 2 * a + 4 * b] * inv);
-    return;
-  }
-  Elem* dst = static_cast<Elem*>(p.out) + off;
-#pragma unroll
-  for (int g = 0; g < 4; ++g) {
-    uint32_t x[4], y[4] = {0u, 0u, 0u, 0u};
-#pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      const int b = 4 * g + j;
-      x[j] = Mma::pack(o[2 * a + 4 * b] * inv, o[1 + 2 * a + 4 * b] * inv);
-    }
-    quad_transpose(x, y, t0, mask);
-    if (store)
-      *reinterpret_cast<uint4*>(dst + 8 * (4 * g + t0)) = make_uint4(y[0], y[1], y[2], y[3]);
-  }
-}
-
 template <typename Elem, bool FP32P>
 __global__ void __launch_bounds__(kThreads, 1)
     tree_attn_tc_kernel(const JtTreeAttnParams p, const DevLayout w,
@@ -682,7 +615,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (tid == 0) {
     for (int i = 0; i < kNumBars; ++i) {
       uint32_t count = 1;
-      if ((i >= kBarPFull && i < kBarPFull + kSBufs) || i == kBarOFree) count = kSoftmaxWarps;
+      if ((i >= kBarPFull && i < kBarPFull + kSBufs) || i == kBarOFree || i == kBarMx ||
+          i == kBarLx)
+        count = kSoftmaxWarps;
       if (i == kBarItemEmpty || i == kBarItemEmpty + 1) count = kItemConsumers;
       if (i >= kBarFull && i < kBarFull + kRing) count = kFullArrivals;
       mbar_init(JT_BAR(i), count);
@@ -846,8 +781,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           mma_ts_warp(tmem + col_o(), pa + col_p(kk), vd + kk * (2048 / 16), kIdescPV,
                       (t > 0 || kk > 0) ? 1u : 0u);
           if constexpr (FP32P)
-            mma_ts_warp(tmem + col_o(), pa + col_p(kk) + kColPLow, vd + kk * (2048 / 16), kIdescPV,
-                        1u);
+            mma_ts_warp(tmem + col_o(), pa + col_p(kk) + 32, vd + kk * (2048 / 16), kIdescPV, 1u);
         }
         tc_commit_warp(JT_BAR(kBarPvDone + b));
         release(slot);
@@ -950,60 +884,61 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else {
     // ------------------------------------------------------------------ softmax + epilogue
-    // Warp w owns TMEM lanes (score rows) 32 (w % 4) + 16 ((w - 4) / 4) + [0, 16); thread t
-    // of it holds rows lane0 + t / 4 and lane0 + t / 4 + 8 (see the 16-lane shapes), each
-    // row's keys and output columns spread over the four threads of one quad.
-    const int quad = lane >> 2, t0 = lane & 3;
-    const int lane0 = 32 * (warp & 3) + 16 * ((warp - 4) >> 2);
-    const uint32_t lane_base = static_cast<uint32_t>(lane0) << 16;
-    const uint32_t qmask = 0xfu << (lane & ~3);
+    const int c = (warp - 4) >> 2;           // key / output column half of this warpgroup
+    const int t128 = tid - 128 - c * 128;    // score row (TMEM lane)
+    const uint32_t lane_base = static_cast<uint32_t>((t128 >> 5) * 32) << 16;
+    float* xl = reinterpret_cast<float*>(sbase + kOffXl);  // [half][row] row sums
+    // [tile parity][half][row] half maxima: alternating buffers, so a warpgroup that runs a
+    // tile ahead never overwrites a value the other warpgroup has yet to read.
+    float* xm = reinterpret_cast<float*>(sbase + kOffXm);
     const float scale_log2 = p.scale * 1.4426950408889634f;
-    uint32_t g0 = 0;
+    // Operand-type rows whose 32-column pieces start on 32-byte boundaries take 32-byte
+    // stores.
+    const bool wide_out = (reinterpret_cast<uintptr_t>(p.out) & 31u) == 0 &&
+                          (p.out_stride0 | p.out_stride1) % 16 == 0;
+    uint32_t g0 = 0, mx_par = 0, lx_par = 0;
     for (uint32_t seq = 0;; ++seq) {
       Item it;
       if (!next_item(seq, it)) break;
       const int n = it.n_tiles;
-      int rr[2], jn[2], gq[2];
-      bool row_ok[2];
-      const uint32_t* mask_row[2];
-#pragma unroll
-      for (int a = 0; a < 2; ++a) {
-        rr[a] = lane0 + quad + 8 * a;
-        const int gm = it.tp * kM + rr[a];
-        jn[a] = gm / G;
-        gq[a] = gm - jn[a] * G;
-        row_ok[a] = jn[a] < it.T;
-        mask_row[a] = single ? smask + (row_ok[a] ? jn[a] - it.tp * (kM / G) : 0) * kMaskWordsMax
-                             : w.masks + static_cast<int64_t>(it.q_start + (row_ok[a] ? jn[a] : 0)) *
-                                             w.mask_words;
-      }
-      const bool warp_live = __any_sync(0xffffffffu, row_ok[0] || row_ok[1]);
-      float m_run[2] = {-INFINITY, -INFINITY};  // running max per row, log2 units
-      float l_run[2] = {0.f, 0.f};              // this thread's partial row sums
+      const int gm = it.tp * kM + t128;
+      const int j = gm / G, g = gm - j * G;
+      const bool row_ok = j < it.T;
+      const bool warp_live = __any_sync(0xffffffffu, row_ok);
+      const uint32_t* mask_row =
+          single ? smask + (row_ok ? j - it.tp * (kM / G) : 0) * kMaskWordsMax
+                 : w.masks + static_cast<int64_t>(it.q_start + (row_ok ? j : 0)) * w.mask_words;
+      float m_run = -INFINITY;  // running max in log2 units (scaled scores)
+      float l_run = 0.f;        // this half's partial row sum
       const uint32_t o_addr = tmem + lane_base + col_o();
       for (int t = 0; t < n; ++t) {
         const int gt = g0 + t;
         const int b = gt % kSBufs;
         const int kb = it.key_begin + t * kN;
         const bool full = kb + kN <= min(it.P, it.key_end);
-        const TileKeys vk{kb, it.P, it.key_end, it.T};
+        const TileKeys vk{kb, it.P, it.key_end, it.T, mask_row, row_ok};
         const uint32_t s_addr = tmem + lane_base + col_s(b);
         warp_wait(JT_BAR(kBarSFull + b), (gt / kSBufs) & 1, abort);
         tc_fence_after();
-        float alpha[2] = {1.f, 1.f}, rsum[2] = {0.f, 0.f};
+        float alpha = 1.f, rsum = 0.f;
+        float* xm_mine = xm + ((gt & 1) * 2 + c) * kM + t128;
+        const float* xm_other = xm + ((gt & 1) * 2 + (c ^ 1)) * kM + t128;
         if (warp_live) {
-          if (full)
-            softmax_tile<Elem, FP32P, false>(s_addr, vk, mask_row, row_ok, t0, scale_log2, m_run,
-                                            alpha, rsum);
-          else
-            softmax_tile<Elem, FP32P, true>(s_addr, vk, mask_row, row_ok, t0, scale_log2, m_run,
-                                           alpha, rsum);
+          rsum = full ? softmax_half<Elem, FP32P, false>(s_addr, c, vk, scale_log2, m_run,
+                                                         alpha, xm_mine, xm_other,
+                                                         JT_BAR(kBarMx), mx_par, abort)
+                      : softmax_half<Elem, FP32P, true>(s_addr, c, vk, scale_log2, m_run,
+                                                        alpha, xm_mine, xm_other,
+                                                        JT_BAR(kBarMx), mx_par, abort);
         } else {
-          write_zero_tile<FP32P>(s_addr);
+          // No live row in this warp: zero P, but still meet the other warpgroup.
+          warp_arrive(JT_BAR(kBarMx));
+          warp_wait(JT_BAR(kBarMx), mx_par, abort);
+          write_zero_half<FP32P>(s_addr, c);
         }
-#pragma unroll
-        for (int a = 0; a < 2; ++a) l_run[a] = l_run[a] * alpha[a] + rsum[a];
-        if (t > 0 && __any_sync(0xffffffffu, alpha[0] != 1.f || alpha[1] != 1.f)) {
+        mx_par ^= 1u;
+        l_run = l_run * alpha + rsum;
+        if (t > 0 && __any_sync(0xffffffffu, alpha != 1.f)) {
           // Rescale this warp's O rows once PV t-1 has completed.  A warp that needs no
           // rescale publishes P t at once, so PV t never waits for PV t-1 in the common
           // case.  The wait is for exactly one phase of PvDone[(gt-1) % 3]: its previous
@@ -1012,102 +947,154 @@ __global__ void __launch_bounds__(kThreads, 1)
           const int gp = gt - 1;
           warp_wait(JT_BAR(kBarPvDone + gp % kSBufs), (gp / kSBufs) & 1, abort);
           tc_fence_after();
-          uint32_t o[64];
-          tmem_ld_16x256b_x16(o_addr, o);
-          tmem_wait_ld();
+#pragma unroll 1
+          for (int chunk = 0; chunk < 2; ++chunk) {
+            uint32_t o[32];
+            tmem_ld32(o_addr + 64 * c + chunk * 32, o);
+            tmem_wait_ld();
 #pragma unroll
-          for (int k = 0; k < 64; ++k)
-            o[k] = __float_as_uint(__uint_as_float(o[k]) * alpha[(k >> 1) & 1]);
-          tmem_st_16x256b_x16(o_addr, o);
+            for (int k = 0; k < 32; ++k) o[k] = __float_as_uint(__uint_as_float(o[k]) * alpha);
+            tmem_st32(o_addr + 64 * c + chunk * 32, o);
+          }
         }
         tmem_wait_st();
         tc_fence_before();
         warp_arrive(JT_BAR(kBarPFull + b));
       }
-      // Epilogue: wait for the item's last PV (same one-phase argument as the rescale
-      // wait), finish the row sums over the quad, read O and write the rows.
+      // Epilogue: wait for the item's last PV, swap the half row sums, then each
+      // warpgroup writes its 64 output columns.
       {
-        const int gl = g0 + n - 1;
+        const int gl = g0 + n - 1;  // same one-phase argument as the rescale wait
         warp_wait(JT_BAR(kBarPvDone + gl % kSBufs), (gl / kSBufs) & 1, abort);
       }
-      float l_fin[2];
-#pragma unroll
-      for (int a = 0; a < 2; ++a) {
-        float l = l_run[a];
-        l += __shfl_xor_sync(0xffffffffu, l, 1);
-        l += __shfl_xor_sync(0xffffffffu, l, 2);
-        l_fin[a] = l;
-      }
+      xl[c * kM + t128] = l_run;
+      warp_arrive(JT_BAR(kBarLx));
+      warp_wait(JT_BAR(kBarLx), lx_par, abort);
+      lx_par ^= 1u;
+      const float l_fin = l_run + xl[(c ^ 1) * kM + t128];
       tc_fence_after();
-      uint32_t ob[64];
-      tmem_ld_16x256b_x16(o_addr, ob);
-      tmem_wait_ld();
-      tc_fence_before();
-      warp_arrive(JT_BAR(kBarOFree));  // O is in registers: the next item's PV may start
-      const float* o = reinterpret_cast<const float*>(ob);
-      int64_t off[2];
-#pragma unroll
-      for (int a = 0; a < 2; ++a)
-        off[a] = static_cast<int64_t>(it.q_start + jn[a]) * p.out_stride0 +
-                 static_cast<int64_t>(it.h * G + gq[a]) * p.out_stride1;
-      if (it.n_split <= 1) {
-#pragma unroll
-        for (int a = 0; a < 2; ++a)
-          store_row<Elem>(p, off[a], o, a, 1.f / l_fin[a], t0, qmask, row_ok[a]);
-      } else {
-        // Split-KV: unnormalised partials and (max, sum) per row; each row's counter counts
-        // the splits that published it, and the quad that completes it merges the row.
-        // Nothing waits: rows finish independently.
-        const int64_t slot0 =
-            it.slot_base + (static_cast<int64_t>(it.h) * it.mblocks + it.tp) * it.n_split;
-        const int64_t slot = slot0 + it.split;
-#pragma unroll
-        for (int a = 0; a < 2; ++a) {
-          float* dst = w.part_o + (slot * kM + rr[a]) * kD + 2 * t0;
-#pragma unroll
-          for (int bb = 0; bb < 16; ++bb)
-            *reinterpret_cast<float2*>(dst + 8 * bb) =
-                make_float2(o[2 * a + 4 * bb], o[1 + 2 * a + 4 * bb]);
-          if (t0 == 0) w.part_ml[slot * kM + rr[a]] = make_float2(m_run[a], l_fin[a]);
-        }
-        __threadfence();
-        __syncwarp();
-#pragma unroll
-        for (int a = 0; a < 2; ++a) {
-          int* counter = w.counters +
-                         (static_cast<int64_t>(it.counter_base) + it.h * it.mblocks + it.tp) * kM +
-                         rr[a];
-          int done = 0;
-          if (t0 == 0) done = atomicAdd(counter, 1);
-          done = __shfl_sync(0xffffffffu, done, lane & ~3);
-          if (done != it.n_split - 1) continue;  // quad-uniform
-          if (t0 == 0) *counter = 0;
-          __threadfence();
-          float mmax = -INFINITY;
-          for (int s2 = 0; s2 < it.n_split; ++s2)
-            mmax = fmaxf(mmax, __ldcg(w.part_ml + (slot0 + s2) * kM + rr[a]).x);
-          const float mref = mmax == -INFINITY ? 0.f : mmax;
-          float acc[64];
-#pragma unroll
-          for (int k = 0; k < 64; ++k) acc[k] = 0.f;
-          float den = 0.f;
+      const bool split_item = it.n_split > 1;
+      const int64_t slot = it.slot_base +
+                           (static_cast<int64_t>(it.h) * it.mblocks + it.tp) * it.n_split + it.split;
+      const float inv = 1.f / l_fin;
 #pragma unroll 1
-          for (int s2 = 0; s2 < it.n_split; ++s2) {
-            const float2 ml = __ldcg(w.part_ml + (slot0 + s2) * kM + rr[a]);
-            const float* src = w.part_o + ((slot0 + s2) * kM + rr[a]) * kD + 2 * t0;
-            float2 v[16];
+      for (int chunk = 0; chunk < 2; ++chunk) {
+        uint32_t o[32];
+        tmem_ld32(o_addr + 64 * c + chunk * 32, o);
+        tmem_wait_ld();
+        const int col = 64 * c + 32 * chunk;
+        if (split_item) {
+          float4* dst = reinterpret_cast<float4*>(w.part_o + (slot * kM + t128) * kD + col);
 #pragma unroll
-            for (int bb = 0; bb < 16; ++bb)
-              v[bb] = __ldcg(reinterpret_cast<const float2*>(src + 8 * bb));
-            const float wv = jt::fast_exp2(ml.x - mref);
-            den += wv * ml.y;
+          for (int k = 0; k < 8; ++k)
+            dst[k] = make_float4(__uint_as_float(o[4 * k]), __uint_as_float(o[4 * k + 1]),
+                                 __uint_as_float(o[4 * k + 2]), __uint_as_float(o[4 * k + 3]));
+        } else if (row_ok) {
+          const int64_t off = static_cast<int64_t>(it.q_start + j) * p.out_stride0 +
+                              static_cast<int64_t>(it.h * G + g) * p.out_stride1 + col;
+          if (p.out_dtype == JT_F32) {
+            float4* dst = reinterpret_cast<float4*>(static_cast<float*>(p.out) + off);
 #pragma unroll
-            for (int bb = 0; bb < 16; ++bb) {
-              acc[2 * a + 4 * bb] += wv * v[bb].x;
-              acc[1 + 2 * a + 4 * bb] += wv * v[bb].y;
+            for (int k = 0; k < 8; ++k)
+              dst[k] = make_float4(__uint_as_float(o[4 * k]) * inv, __uint_as_float(o[4 * k + 1]) * inv,
+                                   __uint_as_float(o[4 * k + 2]) * inv,
+                                   __uint_as_float(o[4 * k + 3]) * inv);
+          } else if (wide_out) {
+            // 32-byte stores: each fills a whole sector, half the store transactions.
+            Elem* dst = static_cast<Elem*>(p.out) + off;
+#pragma unroll
+            for (int k = 0; k < 2; ++k) {
+              uint32_t v8[8];
+#pragma unroll
+              for (int e = 0; e < 8; ++e)
+                v8[e] = Mma::pack(__uint_as_float(o[16 * k + 2 * e]) * inv,
+                                  __uint_as_float(o[16 * k + 2 * e + 1]) * inv);
+              asm volatile("st.global.v8.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8};\n" ::"l"(
+                               dst + 16 * k),
+                           "r"(v8[0]), "r"(v8[1]), "r"(v8[2]), "r"(v8[3]), "r"(v8[4]), "r"(v8[5]),
+                           "r"(v8[6]), "r"(v8[7])
+                           : "memory");
+            }
+          } else {
+            uint4* dst = reinterpret_cast<uint4*>(static_cast<Elem*>(p.out) + off);
+#pragma unroll
+            for (int k = 0; k < 4; ++k)
+              dst[k] = make_uint4(
+                  Mma::pack(__uint_as_float(o[8 * k]) * inv, __uint_as_float(o[8 * k + 1]) * inv),
+                  Mma::pack(__uint_as_float(o[8 * k + 2]) * inv, __uint_as_float(o[8 * k + 3]) * inv),
+                  Mma::pack(__uint_as_float(o[8 * k + 4]) * inv, __uint_as_float(o[8 * k + 5]) * inv),
+                  Mma::pack(__uint_as_float(o[8 * k + 6]) * inv, __uint_as_float(o[8 * k + 7]) * inv));
+          }
+        }
+      }
+      tc_fence_before();
+      warp_arrive(JT_BAR(kBarOFree));
+      if (split_item) {
+        // Per-(row, half) merge: each half publishes its 64 columns and its own copy of the
+        // row's max (log2 units) and sum, then bumps the (row, half) counter; the arrival
+        // that completes it (this half of every split) merges those 64 columns.  Nothing
+        // waits: rows and halves finish independently.  The merge issues each split's
+        // loads together (one load round per split, not one per 4 columns).
+        w.part_ml[(slot * 2 + c) * kM + t128] = make_float2(m_run, l_fin);
+        __threadfence();
+        int* counter = w.counters +
+                       (static_cast<int64_t>(it.counter_base) + it.h * it.mblocks + it.tp) * 2 * kM +
+                       c * kM + t128;
+        const int done = atomicAdd(counter, 1);
+        if (done == it.n_split - 1) {
+          *counter = 0;
+          __threadfence();
+          if (row_ok) {
+            const int64_t slot0 =
+                it.slot_base + (static_cast<int64_t>(it.h) * it.mblocks + it.tp) * it.n_split;
+            float mmax = -INFINITY;
+            for (int s2 = 0; s2 < it.n_split; ++s2)
+              mmax = fmaxf(mmax, __ldcg(w.part_ml + ((slot0 + s2) * 2 + c) * kM + t128).x);
+            const float mref = mmax == -INFINITY ? 0.f : mmax;
+            const int64_t off = static_cast<int64_t>(it.q_start + j) * p.out_stride0 +
+                                static_cast<int64_t>(it.h * G + g) * p.out_stride1 + 64 * c;
+#pragma unroll 1
+            for (int part = 0; part < 2; ++part) {
+              float acc[32];
+#pragma unroll
+              for (int k = 0; k < 32; ++k) acc[k] = 0.f;
+              float den = 0.f;
+#pragma unroll 1
+              for (int s2 = 0; s2 < it.n_split; ++s2) {
+                const float2 ml = __ldcg(w.part_ml + ((slot0 + s2) * 2 + c) * kM + t128);
+                const float4* src = reinterpret_cast<const float4*>(
+                    w.part_o + ((slot0 + s2) * kM + t128) * kD + 64 * c + 32 * part);
+                float4 v[8];
+#pragma unroll
+                for (int k = 0; k < 8; ++k) v[k] = __ldcg(src + k);
+                const float wv = jt::fast_exp2(ml.x - mref);
+                den += wv * ml.y;
+#pragma unroll
+                for (int k = 0; k < 8; ++k) {
+                  acc[4 * k] += wv * v[k].x;
+                  acc[4 * k + 1] += wv * v[k].y;
+                  acc[4 * k + 2] += wv * v[k].z;
+                  acc[4 * k + 3] += wv * v[k].w;
+                }
+              }
+              const float dinv = 1.f / den;
+              if (p.out_dtype == JT_F32) {
+                float4* dst = reinterpret_cast<float4*>(static_cast<float*>(p.out) + off + 32 * part);
+#pragma unroll
+                for (int k = 0; k < 8; ++k)
+                  dst[k] = make_float4(acc[4 * k] * dinv, acc[4 * k + 1] * dinv,
+                                       acc[4 * k + 2] * dinv, acc[4 * k + 3] * dinv);
+              } else {
+                uint4* dst = reinterpret_cast<uint4*>(static_cast<Elem*>(p.out) + off + 32 * part);
+#pragma unroll
+                for (int k = 0; k < 4; ++k)
+                  dst[k] = make_uint4(Mma::pack(acc[8 * k] * dinv, acc[8 * k + 1] * dinv),
+                                      Mma::pack(acc[8 * k + 2] * dinv, acc[8 * k + 3] * dinv),
+                                      Mma::pack(acc[8 * k + 4] * dinv, acc[8 * k + 5] * dinv),
+                                      Mma::pack(acc[8 * k + 6] * dinv, acc[8 * k + 7] * dinv));
+              }
             }
           }
-          store_row<Elem>(p, off[a], acc, a, 1.f / den, t0, qmask, row_ok[a]);
         }
       }
       g0 += n;

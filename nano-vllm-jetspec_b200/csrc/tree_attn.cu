@@ -53,7 +53,7 @@ constexpr int64_t kPartialBudgetBytes = 256ll << 20;
 // ---- workspace layout ---------------------------------------------------------------
 struct Layout {
   int bm;           // score rows per item (64 or 128)
-  int counter_stride;  // split counters per (request, kv head, m-block): 1, or 1 per row
+  int counter_stride;  // split counters per (request, kv head, m-block): 1, or 2 per row
   int mask_words;   // 32-bit words of ancestor bitmask per tree node
   int max_items;
   int max_slots;    // partial-result slots (split items)
@@ -87,16 +87,18 @@ Layout make_layout(int32_t R, int32_t Q, int32_t H, int32_t G, int32_t D,
   L.off_req = o;      o = align_up(o + sizeof(int4) * static_cast<size_t>(R), 256);
   L.off_items = o;    o = align_up(o + sizeof(int4) * static_cast<size_t>(L.max_items), 256);
   // Split counters: one per (request, kv head, m-block) for the portable core, one per
-  // score row for the tcgen05 core (whose rows finish independently).
-  const size_t counter_stride = row_counters ? static_cast<size_t>(L.bm) : 1;
+  // score row and output half for the tcgen05 core (whose rows and halves finish
+  // independently).
+  const size_t counter_stride = row_counters ? 2 * static_cast<size_t>(L.bm) : 1;
   L.counter_stride = static_cast<int>(counter_stride);
   L.off_counters = o;
   o = align_up(o + sizeof(int) * static_cast<size_t>(L.max_slots) * counter_stride, 256);
   L.off_masks = o;
   o = align_up(o + sizeof(uint32_t) * static_cast<size_t>(Q) * L.mask_words, 256);
   L.off_part_o = o;   o = align_up(o + static_cast<size_t>(per_slot) * L.max_slots, 256);
-  L.off_part_ml = o;  // (max, sum) per row
-  o = align_up(o + sizeof(float2) * static_cast<size_t>(L.bm) * L.max_slots, 256);
+  L.off_part_ml = o;  // (max, sum) per row; per row and output half for the tcgen05 core
+  o = align_up(o + sizeof(float2) * static_cast<size_t>(L.bm) * L.max_slots * (row_counters ? 2 : 1),
+               256);
   L.total = o;
   return L;
 }
@@ -110,7 +112,7 @@ struct DevLayout {
   float* part_o;
   float2* part_ml;
   int bm, mask_words, max_items, max_slots;
-  int counter_stride;  // split counters per (request, kv head, m-block): 1, or 1 per row
+  int counter_stride;  // split counters per (request, kv head, m-block): 1, or 2 per row
 };
 
 DevLayout device_layout(const Layout& L, void* ws) {
