@@ -43,8 +43,14 @@ constexpr int kSplitBase = 1024;
 // Planning costs in 128-key tile times, measured: the fixed cost of one work item (query
 // tile load, pipeline fill, epilogue) and the extra cost of a split plan (fp32 partials,
 // the release fence and counter of every split item, the merging loads).
-constexpr int kItemCostTiles = 2;
-constexpr int kMergeCostTiles = 16;
+#ifndef JT_ITEM_COST_TILES
+#define JT_ITEM_COST_TILES 2
+#endif
+constexpr int kItemCostTiles = JT_ITEM_COST_TILES;
+#ifndef JT_MERGE_COST_TILES
+#define JT_MERGE_COST_TILES 16
+#endif
+constexpr int kMergeCostTiles = JT_MERGE_COST_TILES;
 // Longest prefix (block-table capacity) for which a one-item-per-CTA launch without a plan
 // beats a split plan (the plan's estimate gives splits no gain below about 32 tiles).
 constexpr int64_t kSingleLaunchMaxKeys = 4096;
