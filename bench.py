@@ -165,38 +165,55 @@ class ClockSampler:
 
 # ---- CPU side -------------------------------------------------------------------------
 def cpu_oracle_rate(batch, budget_s: float, seed: int = 5):
-    """Reference CPU path (fp32 masked SDPA, all host threads) on a strided request sample.
+    """Reference CPU path of the whole step on a strided request sample: the tree-node K/V
+    store, the fp32 masked-SDPA tree attention (all host threads) and the accepted-only
+    commit, each request on a request-local pool.
 
     Returns (tree tokens/s, sample description, threads).  Inputs are generated on the
     host with the workload's shapes; only the sampled requests' rows are materialised.
     """
+    from oracle import kv_cache as kv_oracle
     from oracle import tree_attention as attn_oracle
 
     threads = os.cpu_count() or 1
     torch.set_num_threads(threads)
     gen = torch.Generator().manual_seed(seed)
     std = batch.head_dim ** -0.5
+    heads, dim = batch.num_kv_heads, batch.head_dim
     order = list(range(0, batch.num_requests, 8)) + [r for r in range(batch.num_requests) if r % 8]
     done, tokens, keys, elapsed = [], 0, 0, 0.0
     for r in order:
         prefix, nodes = batch.prefix_lens[r], len(batch.parents[r])
-        q = (torch.randn((nodes, batch.num_query_heads, batch.head_dim), generator=gen) * std).bfloat16()
-        rows = prefix + nodes
-        k = (torch.randn((1, rows, batch.num_kv_heads, batch.head_dim), generator=gen) * std).bfloat16()
-        v = (torch.randn((1, rows, batch.num_kv_heads, batch.head_dim), generator=gen) * std).bfloat16()
-        # A request-local pool: prefix at positions 0..P-1 of one page-table-free page.
+        path = batch.accepted_paths[r]
+        # One page holding the prefix at 0..P-1, the commit destinations after it and the
+        # tree nodes' scratch slots after those.
+        base = prefix + len(path)
+        rows = base + nodes
+        pool = np.zeros((2, 1, 1, rows, heads, dim), dtype=np.uint16)
+        pool[:, 0, 0, :prefix] = (torch.randn((2, prefix, heads, dim), generator=gen) * std
+                                  ).bfloat16().view(torch.uint16).numpy()
+        q = (torch.randn((nodes, batch.num_query_heads, dim), generator=gen) * std).bfloat16()
+        k_nodes = (torch.randn((nodes, heads, dim), generator=gen) * std).bfloat16()
+        v_nodes = (torch.randn((nodes, heads, dim), generator=gen) * std).bfloat16()
+        node_slots = np.arange(base, rows, dtype=np.int64)
         t0 = time.perf_counter()
+        kv_oracle.store_kvcache(k_nodes.view(torch.uint16).numpy(), v_nodes.view(torch.uint16).numpy(),
+                                pool[0, 0], pool[1, 0], node_slots)
+        k = torch.from_numpy(pool[0, 0]).view(torch.bfloat16)
+        v = torch.from_numpy(pool[1, 0]).view(torch.bfloat16)
         attn_oracle.masked_sdpa(q, k, v, [prefix], [[0] if prefix else []],
-                                [list(range(prefix, rows))], [batch.parents[r]],
-                                batch.head_dim ** -0.5, batch.groups)
+                                [node_slots.tolist()], [batch.parents[r]], std, batch.groups)
+        kv_oracle.copy_accepted_kv(pool, node_slots[list(path)],
+                                   np.arange(prefix, base, dtype=np.int64), rows)
         elapsed += time.perf_counter() - t0
         done.append(r)
         tokens += nodes
-        keys += rows
+        keys += prefix + nodes
         if elapsed >= budget_s:
             break
     sample = (f"{len(done)} of {batch.num_requests} requests (every 8th first), "
-              f"{tokens} tree tokens, {keys} keys x {batch.num_kv_heads} KV heads, fp32 masked SDPA")
+              f"{tokens} tree tokens, {keys} keys x {heads} KV heads: node K/V store, "
+              f"fp32 masked SDPA, accepted-only commit")
     return tokens / elapsed, sample, threads
 
 
@@ -1062,13 +1079,28 @@ def attention_other_bytes(batch, heads: int) -> int:
     return q_o + meta
 
 
-def traffic_from_profiles(workload: str):
+def traffic_from_profiles(world: int, requests_per_gpu: int, bytes_per_launch: float):
+    """DRAM bytes per attention launch from the committed ncu capture of config 3 on one
+    GPU (dram__bytes_read.sum + dram__bytes_write.sum), with where they come from.
+
+    At N > 1 each GPU runs N x the requests at 1/N of the KV heads; the launch's traffic
+    is scaled from the capture by the ratio of algorithmic bytes (the capture read 1.00x
+    its algorithmic bytes, and traffic grows with the K/V streamed).
+    """
     path = ROOT / "profiles" / "traffic.json"
     if not path.exists():
-        return None
-    data = json.loads(path.read_text())
-    entry = data.get(workload)
-    return None if entry is None else entry.get("dram_bytes_per_launch")
+        return None, None
+    entry = json.loads(path.read_text()).get("config3x1")
+    if entry is None:
+        return None, None
+    measured = entry["dram_bytes_per_launch"]
+    if world == 1:
+        return measured, f"ncu capture of this workload ({entry['source']})"
+    one = global_batch(1, requests_per_gpu)
+    algo_one = one.kv_bytes(kv_heads=KV_HEADS) + attention_other_bytes(one, KV_HEADS)
+    scaled = measured * bytes_per_launch / algo_one
+    return scaled, (f"config3x1 ncu capture ({entry['source']}) scaled by algorithmic bytes "
+                    f"{bytes_per_launch / algo_one:.4f}")
 
 
 def main():
@@ -1137,7 +1169,8 @@ def main():
             kv_total = kv_bytes * world
             achieved = (kv_bytes + other_bytes) / (attn_ms * 1e-3) / 1e9
             flops = batch.attention_flops(kv_heads=heads)
-            workload = f"config3x{world}"
+            traffic, traffic_source = traffic_from_profiles(world, args.requests_per_gpu,
+                                                            kv_bytes + other_bytes)
             line = {
                 "metric": METRIC, "value": tokens / (ms * 1e-3), "unit": UNIT, "n_gpus": world,
                 "steps": steps, "warmup": warmup, "ms_per_step": ms, "higher_is_better": True,
@@ -1149,7 +1182,7 @@ def main():
                 "roofline": {"bound": "hbm", "achieved": achieved, "peak": pk["hbm_gbs"],
                              "unit": "GB/s", "frac": achieved / pk["hbm_gbs"],
                              "peak_source": pk["source"],
-                             "traffic": traffic_from_profiles(workload),
+                             "traffic": traffic, "traffic_source": traffic_source,
                              "tensor_tflops": flops / (attn_ms * 1e-3) / 1e12,
                              "tensor_frac": flops / (attn_ms * 1e-3) / 1e12 / pk["bf16_tflops"]},
                 "e2e": {"value": tokens / (e2e_ms / steps * 1e-3), "unit": UNIT,
