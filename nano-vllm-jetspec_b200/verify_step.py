@@ -121,7 +121,29 @@ def build_reference_model(config, device, seed: int = 5, std: float = 0.02,
                     loader(param, tensor)
             del tensor
     model.eval()
+    if dist.is_initialized() and dist.get_world_size() > 1:
+        for layer in model.model.layers:
+            layer.mlp.forward_dense = _dense_mlp_rank_width(layer.mlp)
     return model
+
+
+def _dense_mlp_rank_width(mlp):
+    """``Qwen3MLP.forward_dense`` (qwen3.py:348-355) with the gate / up split at this
+    rank's width.  The reference splits the merged gate_up weight at
+    ``output_sizes[0]``, the global intermediate size, which is right only at tensor
+    parallelism 1 (its packed verifier requires TP 1, llm_engine.py:355-356); a rank holds
+    output_sizes[0] / TP rows of each half, so the split point is half the rank's rows.
+    Applied to both arms of a TP > 1 run; at TP 1 the reference's method runs unchanged."""
+    import torch.nn.functional as F
+
+    def forward_dense(x):
+        weight, bias = mlp.gate_up_proj.weight, mlp.gate_up_proj.bias
+        width = weight.shape[0] // 2
+        gate = F.linear(x, weight[:width], None if bias is None else bias[:width])
+        up = F.linear(x, weight[width:], None if bias is None else bias[width:])
+        return mlp.down_proj(F.silu(gate) * up)
+
+    return forward_dense
 
 
 @dataclass

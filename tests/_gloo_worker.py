@@ -36,3 +36,52 @@ def run(rank: int, world: int, port: int, result_path: str):
             torch.save({"gathered": torch.cat(parts, dim=1), "max": elapsed.item()}, result_path)
     finally:
         dist.destroy_process_group()
+
+
+def run_dense_mlp(rank: int, world: int, port: int, result_path: str):
+    """The reference's Qwen3MLP at tensor parallelism `world`, weights loaded through its
+    own loaders from full seeded tensors; the rank-width forward_dense of verify_step and
+    (recorded, not raised) the reference's own forward_dense."""
+    import datetime
+    import sys
+    from pathlib import Path
+
+    root = Path(__file__).resolve().parents[1]
+    for path in (str(root), str(root / "baseline" / "_ref")):
+        if path not in sys.path:
+            sys.path.insert(0, path)
+    import torch
+    import torch.distributed as dist
+
+    import __graft_entry__
+    __graft_entry__.load_package()
+
+    dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank,
+                            world_size=world, timeout=datetime.timedelta(seconds=60))
+    try:
+        from nanovllm.models.qwen3 import Qwen3MLP
+        from jetspec_b200.verify_step import _dense_mlp_rank_width
+
+        hidden, inter = 64, 96
+        gen = torch.Generator().manual_seed(11)
+        gate = torch.randn((inter, hidden), generator=gen) * 0.1
+        up = torch.randn((inter, hidden), generator=gen) * 0.1
+        down = torch.randn((hidden, inter), generator=gen) * 0.1
+        x = torch.randn((5, hidden), generator=gen)
+        mlp = Qwen3MLP(hidden, inter, "silu")
+        with torch.no_grad():
+            p = mlp.gate_up_proj.weight
+            p.weight_loader(p, gate, 0)
+            p.weight_loader(p, up, 1)
+            p = mlp.down_proj.weight
+            p.weight_loader(p, down)
+            out = _dense_mlp_rank_width(mlp)(x)
+            try:
+                mlp.forward_dense(x)
+                reference_error = None
+            except RuntimeError as exc:
+                reference_error = str(exc)
+        if rank == 0:
+            torch.save({"out": out, "reference_error": reference_error}, result_path)
+    finally:
+        dist.destroy_process_group()
