@@ -21,6 +21,9 @@ constexpr int kStoreThreads = 256;
 constexpr int kCommitThreads = 512;
 constexpr int kCommitUnroll = 4;
 constexpr int kCommitSmemCap = 192 * 1024;  // bytes of staging per commit CTA
+constexpr int kLocalThreads = 256;          // plane-local commit CTAs
+constexpr int kLocalUnroll = 2;
+constexpr int kLocalMinPlanes = 32;         // fewer planes: the grid-wide form spreads wider
 
 __device__ __forceinline__ int64_t load_slot(const void* base, int is64, int64_t i) {
   return is64 ? static_cast<const int64_t*>(base)[i]
@@ -176,6 +179,47 @@ __global__ void __launch_bounds__(kCommitThreads) kv_commit_kernel(JtKvCommitPar
   }
 }
 
+// Plane-local form: when every plane's units fit one CTA's shared memory and there are
+// enough planes to spread over the GPU, each CTA takes whole planes (a grid-stride loop):
+// it gathers a plane's units, synchronises its own threads and scatters them.  Planes
+// cover disjoint bytes, so no CTA waits for another: an ordinary launch, no grid barrier.
+__global__ void __launch_bounds__(kLocalThreads) kv_commit_local_kernel(JtKvCommitParams p,
+                                                                        CommitGeom g) {
+  extern __shared__ __align__(16) int4 staging[];
+  const int64_t pool_slots = p.num_blocks * p.block_size;
+  const int n = g.plane_units;
+  for (int plane = blockIdx.x; plane < g.planes; plane += gridDim.x) {
+    for (int base = threadIdx.x; base < n; base += kLocalThreads * kLocalUnroll) {
+      int4 v[kLocalUnroll];
+#pragma unroll
+      for (int k = 0; k < kLocalUnroll; ++k) {
+        const int i = base + k * kLocalThreads;
+        v[k] = make_int4(0, 0, 0, 0);
+        if (i < n) {
+          bool ok = false;
+          const char* src = commit_unit_address(p, g, plane, i, p.source_slots, pool_slots, &ok);
+          if (ok) v[k] = *reinterpret_cast<const int4*>(src);
+          else atomicOr(&g_kv_errors, JT_DEVERR_OUT_OF_RANGE);
+        }
+      }
+#pragma unroll
+      for (int k = 0; k < kLocalUnroll; ++k) {
+        const int i = base + k * kLocalThreads;
+        if (i < n) staging[i] = v[k];
+      }
+    }
+    __syncthreads();  // every read of this plane precedes every write to it
+    for (int i = threadIdx.x; i < n; i += kLocalThreads) {
+      bool src_ok = false, dst_ok = false;
+      commit_unit_address(p, g, plane, i, p.source_slots, pool_slots, &src_ok);
+      char* dst = commit_unit_address(p, g, plane, i, p.destination_slots, pool_slots, &dst_ok);
+      if (src_ok && dst_ok) *reinterpret_cast<int4*>(dst) = staging[i];
+      else if (!dst_ok) atomicOr(&g_kv_errors, JT_DEVERR_OUT_OF_RANGE);
+    }
+    __syncthreads();  // the staging is free for the next plane
+  }
+}
+
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 bool stride16(int64_t stride, int eb) { return ((stride * eb) & 15) == 0; }
 
@@ -260,8 +304,34 @@ extern "C" int jt_kv_commit_launch(const JtKvCommitParams* p, cudaStream_t strea
   const int64_t capacity = commit_capacity_units(sms);
   const int words = row_bytes / 16;
   const int64_t n = p->num_slots;
-  // Largest planes that fit the grid's staging: all heads and words of a slot, else one
-  // head's row, else one 16-byte word of it.
+  // Plane-local form: planes of one head and one 32-byte sector of its row (one 16-byte
+  // word when that leaves too few planes or too much staging), each gathered and
+  // scattered by one CTA.
+  for (int wp : {2, 1}) {
+    if (words % wp != 0) continue;
+    const int64_t planes = 2LL * p->num_layers * p->num_kv_heads * (words / wp);
+    const int64_t staging = n * wp * 16;
+    if (planes < kLocalMinPlanes || planes > 0x7fffffff || staging > kCommitSmemCap) continue;
+    CommitGeom g{};
+    g.heads_per_plane = 1;
+    g.words_per_plane = wp;
+    g.words_per_row = words;
+    g.planes = static_cast<int>(planes);
+    g.plane_units = static_cast<int>(n * wp);
+    g.planes_per_group = g.planes;
+    g.groups = 1;
+    const int smem = static_cast<int>(staging);
+    int rc = jt_cuda_check(cudaFuncSetAttribute(kv_commit_local_kernel,
+                                                cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                kCommitSmemCap),
+                           "kv_commit smem attribute");
+    if (rc != JT_OK) return rc;
+    const int grid = static_cast<int>(std::min<int64_t>(planes, 8LL * sms));
+    kv_commit_local_kernel<<<grid, kLocalThreads, smem, stream>>>(*p, g);
+    return jt_cuda_check(cudaGetLastError(), "kv_commit launch");
+  }
+  // Grid-wide form: the largest planes that fit the grid's staging (all heads and words
+  // of a slot, else one head's row, else one 16-byte word of it).
   CommitGeom g{};
   if (n * p->num_kv_heads * words <= capacity) {
     g.heads_per_plane = p->num_kv_heads;

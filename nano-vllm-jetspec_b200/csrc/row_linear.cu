@@ -5,11 +5,16 @@
 // the [M, N] result; the Qwen3 o_proj (qwen3.py:59, :97 ... :302) and down_proj (:334,
 // :345) are its callers.  Here one persistent kernel per GPU does both:
 //
-//   warp 0      TMA producer: x [256 rows x 64 K] and W [256 rows x 64 K] tiles, 128-byte
-//               swizzle, into a 3-stage ring (64 KB per stage)
-//   warp 1      tcgen05.mma issuer (kind::f16, M128 N256 K16, two per K step: the two
-//               128-row halves of the x tile share each W tile) and TMEM owner; the
-//               256 x 256 fp32 tile fills all 512 columns
+//   warp 0      TMA producer: x [BM rows x 64 K] and W [256 rows x 64 K] tiles, 128-byte
+//               swizzle, into a ring of stages
+//   warp 1      tcgen05.mma issuer (kind::f16, M128 N256 K16) and TMEM owner
+//
+// Two tile shapes.  Tall (one GPU): 256 x 256 output tiles, two MMAs per K step (the two
+// 128-row halves of the x tile share each W tile, half the W stream per flop), the fp32
+// tile in all 512 TMEM columns, 3 stages of 64 KB.  Short (a group of GPUs): 128 x 256
+// tiles, two 256-column accumulators so the epilogue and exchange of one tile overlap the
+// MMAs of the next, 4 stages of 48 KB: with twice the tiles, the partial and result
+// transfers of the first tiles run while the GEMM of the later ones still does.
 //   warps 2-5   epilogue: TMEM -> registers -> bf16/f16 partial tile, stored straight into
 //               the tile owner's receive slot (a peer GPU's memory over NVLink, or this
 //               GPU's), then a release flag in the owner's memory
@@ -50,31 +55,43 @@ __device__ uint32_t g_rowlin_errors;
 
 namespace rl {
 
-constexpr int kBM = 256, kBN = 256, kBK = 64;  // output tile; MMAs are M128 halves
-constexpr int kStages = 3;
-constexpr int kATileBytes = kBM * kBK * 2;  // 32 KB
+constexpr int kBN = 256, kBK = 64;  // output tile width, K step; MMAs are M128
 constexpr int kBTileBytes = kBN * kBK * 2;  // 32 KB
-constexpr int kAHalfBytes = kATileBytes / 2;  // rows 128..255 of the x tile
-constexpr int kStageBytes = kATileBytes + kBTileBytes;
-constexpr int kOffA = 0;
-constexpr int kOffB = kOffA + kStages * kATileBytes;
-constexpr int kOffBar = kOffB + kStages * kBTileBytes;
-constexpr int kOffMisc = kOffBar + 16 * 8;
-constexpr int kSmemBytes = kOffMisc + 64 + 1024;  // + alignment slack
-static_assert(kSmemBytes <= 227 * 1024, "shared memory per CTA");
 constexpr int kThreads = 448;
 constexpr int kExchangeThreads = 256;  // warps 6-13
-constexpr int kTileElems = kBM * kBN;  // elements per partial / result tile
 constexpr int kMaxRanks = 8;
+// The tall tile (256 rows) on one GPU, the short one (128 rows) in a group of GPUs.
+#ifndef JT_RL_TALL_WORLD_MAX
+#define JT_RL_TALL_WORLD_MAX 1
+#endif
+__host__ __device__ constexpr bool tall_for(int world) { return world <= JT_RL_TALL_WORLD_MAX; }
+
+template <bool kTall>
+struct Shape {
+  static constexpr int kBM = kTall ? 256 : 128;         // output tile rows
+  static constexpr int kStages = kTall ? 3 : 4;
+  static constexpr int kAccBufs = kTall ? 1 : 2;        // fp32 accumulators in TMEM
+  static constexpr int kATileBytes = kBM * kBK * 2;     // 32 / 16 KB
+  static constexpr int kAHalfBytes = kATileBytes / 2;   // rows 128..255 of a tall x tile
+  static constexpr int kStageBytes = kATileBytes + kBTileBytes;
+  static constexpr int kOffA = 0;
+  static constexpr int kOffB = kOffA + kStages * kATileBytes;
+  static constexpr int kOffBar = kOffB + kStages * kBTileBytes;
+  static constexpr int kOffMisc = kOffBar + 16 * 8;
+  static constexpr int kSmemBytes = kOffMisc + 64 + 1024;  // + alignment slack
+  static constexpr int kTileElems = kBM * kBN;          // elements per partial / result tile
+  static_assert(kSmemBytes <= 227 * 1024, "shared memory per CTA");
+};
+__host__ __device__ constexpr int tile_rows(int world) { return tall_for(world) ? 256 : 128; }
 constexpr long long kLocalWaitLimit = 4000000000ll;  // cycles per pipeline wait
 
 // Barriers.
-constexpr int kBarFull = 0;      // [kStages] TMA bytes
-constexpr int kBarEmpty = 3;     // [kStages] MMA commit
-constexpr int kBarAccFull = 6;   // MMA commit after a tile's last K step
-constexpr int kBarAccEmpty = 7;  // 4 epilogue warps
-constexpr int kBarDrain = 8;
-constexpr int kNumBars = 9;
+constexpr int kBarFull = 0;       // [stages] TMA bytes
+constexpr int kBarEmpty = 4;      // [stages] MMA commit
+constexpr int kBarAccFull = 8;    // [accumulators] MMA commit after a tile's last K step
+constexpr int kBarAccEmpty = 10;  // [accumulators] 4 epilogue warps
+constexpr int kBarDrain = 12;
+constexpr int kNumBars = 13;
 
 struct Args {
   int64_t M, N, K;
@@ -98,12 +115,15 @@ __host__ __device__ inline int64_t ws_flag_bytes(int tiles, int world) {
 __host__ __device__ inline int64_t ws_recv_offset(int tiles, int world) {
   return ws_flag_bytes(tiles, world);
 }
-__host__ __device__ inline int64_t ws_result_offset(int tiles, int world, int owned_max) {
+__host__ __device__ inline int64_t ws_result_offset(int tiles, int world, int owned_max,
+                                                    int tile_elems) {
   return ws_recv_offset(tiles, world) +
-         static_cast<int64_t>(owned_max) * world * kTileElems * 2;
+         static_cast<int64_t>(owned_max) * world * tile_elems * 2;
 }
-__host__ __device__ inline int64_t ws_total(int tiles, int world, int owned_max) {
-  return ws_result_offset(tiles, world, owned_max) + static_cast<int64_t>(tiles) * kTileElems * 2;
+__host__ __device__ inline int64_t ws_total(int tiles, int world, int owned_max,
+                                            int tile_elems) {
+  return ws_result_offset(tiles, world, owned_max, tile_elems) +
+         static_cast<int64_t>(tiles) * tile_elems * 2;
 }
 
 // ---- PTX wrappers --------------------------------------------------------------------
@@ -265,28 +285,32 @@ __device__ __forceinline__ uint32_t* done_flags(unsigned char* ws, int tiles, in
   return ready_flags(ws) + static_cast<int64_t>(tiles) * world;
 }
 
-// 16-byte chunk `ch` (0..8191) of a partial / result tile: chunks are stored so that the
-// 32 lanes of an epilogue warp write 512 contiguous bytes (one row per lane, 8 columns per
-// chunk); this maps a chunk back to its row and first column inside the 256 x 256 tile
-// (chunk = half * 4096 + quadrant * 1024 + column group * 128 + i * 32 + lane).
+// 16-byte chunk `ch` (0..8191 of a tall tile, 0..4095 of a short one) of a partial /
+// result tile: chunks are stored so that the 32 lanes of an epilogue warp write 512
+// contiguous bytes (one row per lane, 8 columns per chunk); this maps a chunk back to its
+// row and first column inside the tile (chunk = half * 4096 + quadrant * 1024 + column
+// group * 128 + i * 32 + lane; a short tile has only half 0).
 __device__ __forceinline__ void chunk_coords(int ch, int& row, int& col) {
   const int lane = ch & 31, i = (ch >> 5) & 3, c = (ch >> 7) & 7, q = (ch >> 10) & 3;
   row = (ch >> 12) * 128 + q * 32 + lane;
   col = c * 32 + i * 8;
 }
 
-template <bool kBf16>
+template <bool kBf16, bool kTall>
 __global__ void __launch_bounds__(kThreads, 1)
     row_linear_kernel(const __grid_constant__ Args a, const __grid_constant__ Maps maps) {
   using Cv = Conv<kBf16>;
-  constexpr uint32_t kIdesc = instr_desc(128, kBN, kBf16);  // one 128-row half per MMA
+  using S = Shape<kTall>;
+  constexpr int kBM = S::kBM, kStages = S::kStages, kTileElems = S::kTileElems;
+  constexpr int kATileBytes = S::kATileBytes, kOffA = S::kOffA, kOffB = S::kOffB;
+  constexpr uint32_t kIdesc = instr_desc(128, kBN, kBf16);  // one 128-row block per MMA
   extern __shared__ unsigned char smem_raw[];
   const uint32_t raw = jt::smem_u32(smem_raw);
   const uint32_t base = (raw + 1023u) & ~1023u;
   unsigned char* sbase = smem_raw + (base - raw);
-  const uint32_t bar0 = base + kOffBar;
+  const uint32_t bar0 = base + S::kOffBar;
 #define RL_BAR(i) (bar0 + 8u * static_cast<uint32_t>(i))
-  volatile int* misc = reinterpret_cast<volatile int*>(sbase + kOffMisc);
+  volatile int* misc = reinterpret_cast<volatile int*>(sbase + S::kOffMisc);
   volatile int* abort = misc + 1;  // misc[0]: TMEM base
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int lr = blockIdx.x % a.ranks_in_launch;  // rank of this launch the CTA works for
@@ -297,7 +321,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   if (tid == 0) {
     for (int i = 0; i < kNumBars; ++i)
-      mbar_init(RL_BAR(i), i == kBarAccEmpty ? 4u : 1u);
+      mbar_init(RL_BAR(i), (i == kBarAccEmpty || i == kBarAccEmpty + 1) ? 4u : 1u);
     misc[1] = 0;
     // The call's epoch: given by the host, or (0) one past this rank's call counter, which
     // the last CTA of the previous call advanced (stream order makes it visible here).
@@ -309,7 +333,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
   if (warp == 1) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], 512;\n" ::"r"(
-                     base + kOffMisc)
+                     base + S::kOffMisc)
                  : "memory");
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;\n" ::: "memory");
   }
@@ -328,7 +352,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int kb = 0; kb < k_blocks; ++kb, ++r) {
           const int s = static_cast<int>(r % kStages);
           mbar_wait(RL_BAR(kBarEmpty + s), ((r / kStages) & 1u) ^ 1u);
-          mbar_arrive_tx(RL_BAR(kBarFull + s), kStageBytes);
+          mbar_arrive_tx(RL_BAR(kBarFull + s), S::kStageBytes);
           tma_load_2d(base + kOffA + s * kATileBytes, &maps.x[lr], kb * kBK, m0,
                       RL_BAR(kBarFull + s));
           tma_load_2d(base + kOffB + s * kBTileBytes, &maps.w[lr], kb * kBK, n0,
@@ -342,9 +366,12 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint32_t r = 0, acc = 0;
     const uint64_t adesc0 = smem_desc(base + kOffA), bdesc0 = smem_desc(base + kOffB);
     for (int t = cta; t < a.tiles; t += a.grid_per_rank, ++acc) {
-      // The accumulator (both halves, 512 columns) is free once the epilogue read it.
-      mbar_wait(RL_BAR(kBarAccEmpty), (acc & 1u) ^ 1u);
+      // An accumulator is free once the epilogue read it (tall: the one 512-column
+      // accumulator; short: accumulators alternate, 256 columns each).
+      const uint32_t buf = kTall ? 0u : (acc & 1u), use = kTall ? acc : (acc >> 1);
+      mbar_wait(RL_BAR(kBarAccEmpty + buf), (use & 1u) ^ 1u);
       tc_fence_after();
+      const uint32_t d = tmem + buf * static_cast<uint32_t>(kBN);
       for (int kb = 0; kb < k_blocks; ++kb, ++r) {
         const int s = static_cast<int>(r % kStages);
         mbar_wait(RL_BAR(kBarFull + s), (r / kStages) & 1u);
@@ -354,13 +381,14 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
         for (int kk = 0; kk < kBK / 16; ++kk) {  // 16 K elements = 32 bytes along the row
           const uint32_t accumulate = (kb > 0 || kk > 0) ? 1u : 0u;
-          mma_ss_warp(tmem, ad + 2 * kk, bd + 2 * kk, kIdesc, accumulate);
-          mma_ss_warp(tmem + static_cast<uint32_t>(kBN), ad + (kAHalfBytes >> 4) + 2 * kk,
-                      bd + 2 * kk, kIdesc, accumulate);
+          mma_ss_warp(d, ad + 2 * kk, bd + 2 * kk, kIdesc, accumulate);
+          if constexpr (kTall)
+            mma_ss_warp(tmem + static_cast<uint32_t>(kBN), ad + (S::kAHalfBytes >> 4) + 2 * kk,
+                        bd + 2 * kk, kIdesc, accumulate);
         }
         tc_commit_warp(RL_BAR(kBarEmpty + s));
       }
-      tc_commit_warp(RL_BAR(kBarAccFull));
+      tc_commit_warp(RL_BAR(kBarAccFull + buf));
     }
     // Drain: every MMA this warp issued has completed before TMEM is released.
     tc_commit_warp(RL_BAR(kBarDrain));
@@ -373,19 +401,20 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int t = cta; t < a.tiles; t += a.grid_per_rank, ++acc) {
       const int m0 = (t % a.m_tiles) * kBM, n0 = (t / a.m_tiles) * kBN;
       const int owner = t % world, j = t / world;
-      mbar_wait(RL_BAR(kBarAccFull), acc & 1u);
+      const uint32_t buf = kTall ? 0u : (acc & 1u), use = kTall ? acc : (acc >> 1);
+      mbar_wait(RL_BAR(kBarAccFull + buf), use & 1u);
       tc_fence_after();
       unsigned char* slot =
           world == 1 ? nullptr
                      : a.ws[owner] + ws_recv_offset(a.tiles, world) +
                            (static_cast<int64_t>(j) * world + rank) * kTileElems * 2;
 #pragma unroll 1
-      for (int hc = 0; hc < 2 * (kBN / 32); ++hc) {  // (half, 32-column group)
+      for (int hc = 0; hc < (kBM / 128) * (kBN / 32); ++hc) {  // (half, 32-column group)
         const int h = hc >> 3, c = hc & 7;
         const int64_t m = m0 + h * 128 + q * 32 + lane;
         uint32_t v[32];
         tmem_ld32(tmem + (static_cast<uint32_t>(q * 32) << 16) +
-                      static_cast<uint32_t>(h * kBN + c * 32),
+                      static_cast<uint32_t>((h + static_cast<int>(buf)) * kBN + c * 32),
                   v);
         tmem_wait_ld();
         const int64_t n = n0 + c * 32;
@@ -419,7 +448,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(RL_BAR(kBarAccEmpty));
+      if (lane == 0) mbar_arrive(RL_BAR(kBarAccEmpty + buf));
       if (world > 1) {
         // Every epilogue thread's stores of this partial are visible system-wide before
         // the owner's ready flag for (tile, this rank) is raised.
@@ -434,7 +463,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     // ---------------------------------------------------------------- exchange
     const int et = tid - 192;  // 0..255
     unsigned char* mine = a.ws[rank];
-    const int64_t inbox_off = ws_result_offset(a.tiles, world, a.owned_max);
+    const int64_t inbox_off = ws_result_offset(a.tiles, world, a.owned_max, kTileElems);
     const int owned = (a.tiles - rank + world - 1) / world;  // tiles j * world + rank
     for (int j = cta; j < owned; j += a.grid_per_rank) {
       const int t = j * world + rank;
@@ -579,8 +608,8 @@ bool encode_kmajor(CUtensorMap* map, const void* ptr, int32_t dtype, int64_t row
 
 bool al16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
-int rl_tiles(int64_t m, int64_t n, int* m_tiles, int* n_tiles) {
-  const int64_t mt = (m + rl::kBM - 1) / rl::kBM, nt = (n + rl::kBN - 1) / rl::kBN;
+int rl_tiles(int64_t m, int64_t n, int bm, int* m_tiles, int* n_tiles) {
+  const int64_t mt = (m + bm - 1) / bm, nt = (n + rl::kBN - 1) / rl::kBN;
   if (mt * nt > (1ll << 30)) return jt_fail(JT_ERR_INVALID, "row_linear: output too large");
   *m_tiles = static_cast<int>(mt);
   *n_tiles = static_cast<int>(nt);
@@ -614,7 +643,7 @@ int rl_check_rank(const JtRowLinearParams& p, CUtensorMap* xmap, CUtensorMap* wm
       if (p.workspaces[r] == nullptr || (reinterpret_cast<uintptr_t>(p.workspaces[r]) & 255u))
         return jt_fail(JT_ERR_INVALID, "row_linear: workspace %d null or not 256-byte aligned", r);
   }
-  if (!encode_kmajor(xmap, p.x, p.dtype, p.m, p.k, p.x_stride, rl::kBM) ||
+  if (!encode_kmajor(xmap, p.x, p.dtype, p.m, p.k, p.x_stride, rl::tile_rows(p.world)) ||
       !encode_kmajor(wmap, p.weight, p.dtype, p.n, p.k, p.w_stride, rl::kBN))
     return jt_fail(JT_ERR_CUDA, "row_linear: cuTensorMapEncodeTiled rejected x or weight");
   return JT_OK;
@@ -637,7 +666,8 @@ int rl_launch(const JtRowLinearParams* ranks, int count, cudaStream_t stream) {
     a.out[i] = p.out;
   }
   int m_tiles = 0, n_tiles = 0;
-  int rc = rl_tiles(p0.m, p0.n, &m_tiles, &n_tiles);
+  const bool tall = rl::tall_for(p0.world);
+  int rc = rl_tiles(p0.m, p0.n, rl::tile_rows(p0.world), &m_tiles, &n_tiles);
   if (rc != JT_OK) return rc;
   a.M = p0.m;
   a.N = p0.n;
@@ -659,15 +689,24 @@ int rl_launch(const JtRowLinearParams* ranks, int count, cudaStream_t stream) {
   rc = jt_cuda_check(cudaGetDevice(&dev), "row_linear: device");
   if (rc != JT_OK) return rc;
   if (dev < 0 || dev >= 64) return jt_fail(JT_ERR_INVALID, "row_linear: device index");
-  auto kernel = p0.dtype == JT_BF16 ? rl::row_linear_kernel<true> : rl::row_linear_kernel<false>;
+  const bool bf16 = p0.dtype == JT_BF16;
+  auto kernel = tall ? (bf16 ? rl::row_linear_kernel<true, true> : rl::row_linear_kernel<false, true>)
+                     : (bf16 ? rl::row_linear_kernel<true, false> : rl::row_linear_kernel<false, false>);
+  const int smem = tall ? rl::Shape<true>::kSmemBytes : rl::Shape<false>::kSmemBytes;
   if (sm_count[dev] == 0) {
     int sms = 0;
     rc = jt_cuda_check(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev),
                        "row_linear: SM count");
     if (rc != JT_OK) return rc;
-    for (auto k : {rl::row_linear_kernel<true>, rl::row_linear_kernel<false>}) {
+    for (auto k : {rl::row_linear_kernel<true, true>, rl::row_linear_kernel<false, true>}) {
       rc = jt_cuda_check(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                              rl::kSmemBytes),
+                                              rl::Shape<true>::kSmemBytes),
+                         "row_linear: smem attribute");
+      if (rc != JT_OK) return rc;
+    }
+    for (auto k : {rl::row_linear_kernel<true, false>, rl::row_linear_kernel<false, false>}) {
+      rc = jt_cuda_check(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                              rl::Shape<false>::kSmemBytes),
                          "row_linear: smem attribute");
       if (rc != JT_OK) return rc;
     }
@@ -680,7 +719,7 @@ int rl_launch(const JtRowLinearParams* ranks, int count, cudaStream_t stream) {
   cudaLaunchConfig_t cfg{};
   cfg.gridDim = dim3(static_cast<unsigned>(a.grid_per_rank * count));
   cfg.blockDim = dim3(rl::kThreads);
-  cfg.dynamicSmemBytes = rl::kSmemBytes;
+  cfg.dynamicSmemBytes = smem;
   cfg.stream = stream;
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeCooperative;
@@ -705,9 +744,10 @@ extern "C" int64_t jt_row_linear_workspace_size(int64_t m, int64_t n, int32_t wo
   if (m < 1 || n < 1 || world < 1 || world > rl::kMaxRanks) return -1;
   if (world == 1) return 0;
   int m_tiles = 0, n_tiles = 0;
-  if (rl_tiles(m, n, &m_tiles, &n_tiles) != JT_OK) return -1;
+  const int bm = rl::tile_rows(world);
+  if (rl_tiles(m, n, bm, &m_tiles, &n_tiles) != JT_OK) return -1;
   const int tiles = m_tiles * n_tiles;
-  return rl::ws_total(tiles, world, (tiles + world - 1) / world);
+  return rl::ws_total(tiles, world, (tiles + world - 1) / world, bm * rl::kBN);
 }
 
 extern "C" int jt_row_linear_launch(const JtRowLinearParams* p, cudaStream_t stream) {

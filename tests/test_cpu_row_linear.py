@@ -58,11 +58,11 @@ def test_workspace_rule():
     assert lib.jt_row_linear_workspace_size(2048, 4096, 1) == 0
     assert lib.jt_row_linear_workspace_size(0, 4096, 2) == -1
     assert lib.jt_row_linear_workspace_size(10, 64, 9) == -1
-    tiles = 8 * 16  # 256 x 256 output tiles
+    tiles = 16 * 16  # a group of GPUs uses 128 x 256 output tiles
     for world in (2, 4, 8):
         owned = -(-tiles // world)
         flags = 256 + -(-tiles * (world + 1) * 4 // 256) * 256  # control block + flags
-        expect = flags + owned * world * 131072 + tiles * 131072
+        expect = flags + owned * world * 65536 + tiles * 65536
         assert lib.jt_row_linear_workspace_size(2048, 4096, world) == expect
 
 
