@@ -21,8 +21,8 @@ constexpr int kStoreThreads = 256;
 constexpr int kCommitThreads = 512;
 constexpr int kCommitUnroll = 4;
 constexpr int kCommitSmemCap = 192 * 1024;  // bytes of staging per commit CTA
-constexpr int kLocalThreads = 256;          // plane-local commit CTAs
-constexpr int kLocalUnroll = 2;
+constexpr int kLocalThreads = 512;          // plane-local commit CTAs
+constexpr int kLocalUnroll = 4;             // a plane of up to 2048 units in one round
 constexpr int kLocalMinPlanes = 32;         // fewer planes: the grid-wide form spreads wider
 
 __device__ __forceinline__ int64_t load_slot(const void* base, int is64, int64_t i) {
@@ -304,11 +304,12 @@ extern "C" int jt_kv_commit_launch(const JtKvCommitParams* p, cudaStream_t strea
   const int64_t capacity = commit_capacity_units(sms);
   const int words = row_bytes / 16;
   const int64_t n = p->num_slots;
-  // Plane-local form: planes of one head and one 32-byte sector of its row (one 16-byte
-  // word when that leaves too few planes or too much staging), each gathered and
-  // scattered by one CTA.
+  // Plane-local form: planes of one head and one 32-byte sector of its row while a plane
+  // stays within one round of loads (n <= 1024), else of one 16-byte word (half the
+  // rounds), each gathered and scattered by one CTA; one word when the sector planes are
+  // too few or do not fit.
   for (int wp : {2, 1}) {
-    if (words % wp != 0) continue;
+    if (words % wp != 0 || (wp == 2 && n * 2 > kLocalThreads * kLocalUnroll)) continue;
     const int64_t planes = 2LL * p->num_layers * p->num_kv_heads * (words / wp);
     const int64_t staging = n * wp * 16;
     if (planes < kLocalMinPlanes || planes > 0x7fffffff || staging > kCommitSmemCap) continue;

@@ -24,6 +24,13 @@
 //               a done flag there; then copy the tiles other ranks own from this rank's
 //               inbox into its output as each one is done
 //
+// A pair of GPUs (world == 2) exchanges in one hop instead: every rank's epilogue stores
+// its partial tile into its own and its peer's receive slot (double-buffered by the call's
+// epoch parity), and the exchange warps of both ranks sum the two partials of the tiles
+// their CTA computed, in rank order, and write their own output: the same bytes cross
+// NVLink as with an owner (one partial each way per tile), without the second hop of the
+// results, the owner's done flag and the inbox copy.
+//
 // The all-reduce therefore moves the reduce-scatter + all-gather volume ((world-1)/world of
 // the output out and back per rank), tile by tile while the GEMM is still running, and
 // without a separate collective launch; every transfer over NVLink is a posted store
@@ -108,7 +115,15 @@ struct Args {
 // counter at 4), [ready: tiles x world u32][done: tiles u32] (256-byte aligned), then the
 // receive slots [owned_max][world][tile], then the inbox [tiles][tile] where the owners of
 // the other tiles put the reduced results.
+// A pair (world == 2) uses receive slots [tiles][epoch parity][world][tile] after the
+// flags instead, and no inbox.
 constexpr int kCtrlBytes = 256;
+#ifndef JT_RL_PAIR_EXCHANGE
+#define JT_RL_PAIR_EXCHANGE 1
+#endif
+__host__ __device__ constexpr bool pair_exchange(int world) {
+  return JT_RL_PAIR_EXCHANGE != 0 && world == 2;
+}
 __host__ __device__ inline int64_t ws_flag_bytes(int tiles, int world) {
   return kCtrlBytes + ((static_cast<int64_t>(tiles) * (world + 1) * 4) + 255) / 256 * 256;
 }
@@ -122,8 +137,16 @@ __host__ __device__ inline int64_t ws_result_offset(int tiles, int world, int ow
 }
 __host__ __device__ inline int64_t ws_total(int tiles, int world, int owned_max,
                                             int tile_elems) {
+  if (pair_exchange(world))
+    return ws_recv_offset(tiles, world) + static_cast<int64_t>(tiles) * 2 * world * tile_elems * 2;
   return ws_result_offset(tiles, world, owned_max, tile_elems) +
          static_cast<int64_t>(tiles) * tile_elems * 2;
+}
+// Receive slot of (tile, source rank) in a pair's workspace for the call's epoch parity.
+__host__ __device__ inline int64_t ws_pair_slot(int tiles, int world, int t, uint32_t epoch,
+                                                int src, int tile_elems) {
+  return ws_recv_offset(tiles, world) +
+         ((static_cast<int64_t>(t) * 2 + (epoch & 1u)) * world + src) * tile_elems * 2;
 }
 
 // ---- PTX wrappers --------------------------------------------------------------------
@@ -404,10 +427,17 @@ __global__ void __launch_bounds__(kThreads, 1)
       const uint32_t buf = kTall ? 0u : (acc & 1u), use = kTall ? acc : (acc >> 1);
       mbar_wait(RL_BAR(kBarAccFull + buf), use & 1u);
       tc_fence_after();
-      unsigned char* slot =
-          world == 1 ? nullptr
-                     : a.ws[owner] + ws_recv_offset(a.tiles, world) +
-                           (static_cast<int64_t>(j) * world + rank) * kTileElems * 2;
+      const bool pair = pair_exchange(world);
+      unsigned char* slot = nullptr;
+      unsigned char* slot_peer = nullptr;
+      if (pair) {
+        const int64_t off = ws_pair_slot(a.tiles, world, t, epoch, rank, kTileElems);
+        slot = a.ws[rank] + off;
+        slot_peer = a.ws[rank ^ 1] + off;
+      } else if (world > 1) {
+        slot = a.ws[owner] + ws_recv_offset(a.tiles, world) +
+               (static_cast<int64_t>(j) * world + rank) * kTileElems * 2;
+      }
 #pragma unroll 1
       for (int hc = 0; hc < (kBM / 128) * (kBN / 32); ++hc) {  // (half, 32-column group)
         const int h = hc >> 3, c = hc & 7;
@@ -439,11 +469,19 @@ __global__ void __launch_bounds__(kThreads, 1)
                                 packed[4 * i + 3]);
           }
         } else {
-          uint4* o = reinterpret_cast<uint4*>(slot) + h * 4096 + (q * 8 + c) * 128 + lane;
+          const int64_t ch0 = h * 4096 + (q * 8 + c) * 128 + lane;
+          uint4* o = reinterpret_cast<uint4*>(slot) + ch0;
 #pragma unroll
           for (int i = 0; i < 4; ++i)
             o[32 * i] = make_uint4(packed[4 * i], packed[4 * i + 1], packed[4 * i + 2],
                                    packed[4 * i + 3]);
+          if (pair) {
+            uint4* op = reinterpret_cast<uint4*>(slot_peer) + ch0;
+#pragma unroll
+            for (int i = 0; i < 4; ++i)
+              op[32 * i] = make_uint4(packed[4 * i], packed[4 * i + 1], packed[4 * i + 2],
+                                      packed[4 * i + 3]);
+          }
         }
       }
       tc_fence_before();
@@ -454,9 +492,57 @@ __global__ void __launch_bounds__(kThreads, 1)
         // the owner's ready flag for (tile, this rank) is raised.
         __threadfence_system();
         named_sync(2, 128);
-        if (warp == 2 && lane == 0)
+        if (pair) {
+          if ((warp == 2 || warp == 3) && lane == 0)
+            st_release_sys(ready_flags(a.ws[rank ^ (warp - 2)]) +
+                               static_cast<int64_t>(t) * world + rank,
+                           epoch);
+        } else if (warp == 2 && lane == 0) {
           st_release_sys(ready_flags(a.ws[owner]) + static_cast<int64_t>(t) * world + rank,
                          epoch);
+        }
+      }
+    }
+  } else if (pair_exchange(world)) {
+    // ---------------------------------------------------------------- pair exchange
+    // The tiles this CTA computed: wait for both partials, sum them in rank order (the
+    // same order, hence the same bits, on both ranks), write this rank's output.
+    const int et = tid - 192;  // 0..255
+    unsigned char* mine = a.ws[rank];
+    for (int t = cta; t < a.tiles; t += a.grid_per_rank) {
+      if (et < world)
+        wait_flag(ready_flags(mine) + static_cast<int64_t>(t) * world + et, epoch,
+                  a.wait_limit, abort);
+      named_sync(1, kExchangeThreads);
+      if (*abort) continue;
+      const int m0 = (t % a.m_tiles) * kBM, n0 = (t / a.m_tiles) * kBN;
+      const uint4* slots = reinterpret_cast<const uint4*>(
+          mine + ws_pair_slot(a.tiles, world, t, epoch, 0, kTileElems));
+#pragma unroll 1
+      for (int c0 = et; c0 < kTileElems / 8; c0 += 4 * kExchangeThreads) {
+        uint4 in0[4], in1[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          in0[u] = __ldcg(slots + c0 + kExchangeThreads * u);
+          in1[u] = __ldcg(slots + kTileElems / 8 + c0 + kExchangeThreads * u);
+        }
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          const uint32_t w0[4] = {in0[u].x, in0[u].y, in0[u].z, in0[u].w};
+          const uint32_t w1[4] = {in1[u].x, in1[u].y, in1[u].z, in1[u].w};
+          uint32_t r4[4];
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const float2 f0 = Cv::unpack(w0[e]), f1 = Cv::unpack(w1[e]);
+            r4[e] = Cv::pack(f0.x + f1.x, f0.y + f1.y);
+          }
+          int row, col;
+          chunk_coords(c0 + kExchangeThreads * u, row, col);
+          const int64_t m = m0 + row, n = n0 + col;
+          if (m < a.M && n < a.N)
+            *reinterpret_cast<uint4*>(static_cast<unsigned char*>(a.out[lr]) +
+                                      (m * a.N + n) * 2) = make_uint4(r4[0], r4[1], r4[2], r4[3]);
+        }
       }
     }
   } else if (world > 1) {

@@ -62,7 +62,10 @@ def test_workspace_rule():
     for world in (2, 4, 8):
         owned = -(-tiles // world)
         flags = 256 + -(-tiles * (world + 1) * 4 // 256) * 256  # control block + flags
-        expect = flags + owned * world * 65536 + tiles * 65536
+        if world == 2:  # a pair: receive slots for every tile, both epoch parities
+            expect = flags + tiles * 2 * world * 65536
+        else:  # owners: receive slots for the owned tiles, then the inbox
+            expect = flags + owned * world * 65536 + tiles * 65536
         assert lib.jt_row_linear_workspace_size(2048, 4096, world) == expect
 
 
