@@ -300,8 +300,9 @@ int jt_metadata_build_launch(const JtMetadataBuildParams* params, cudaStream_t s
  * jt_ipc_open_handle).  epoch 0 (the usual value) takes the call's epoch from a counter in
  * the rank's workspace that the kernel advances itself, so a captured launch replays
  * correctly; a nonzero epoch (1, 2, 3, ... on every rank, never mixed with 0 on one
- * workspace) is used as given.  A rank whose peers do not arrive within
- * wait_limit_cycles (0: about ten seconds) flags device error bit 2 and leaves its output
+ * workspace) is used as given (consecutive calls take consecutive epochs: a pair of ranks
+ * alternates its receive slots with the epoch's parity).  A rank whose peers do not arrive
+ * within wait_limit_cycles (0: about ten seconds) flags device error bit 2 and leaves its output
  * incomplete.
  */
 typedef struct JtRowLinearParams {
