@@ -130,6 +130,25 @@ def test_commit_config3_paths_and_empty_commit():
     assert jb.copy_accepted_kv(device_pool, empty, empty, 256) == 0
 
 
+@pytest.mark.parametrize("layers,heads,dim,n", [(1, 1, 64, 300), (1, 1, 128, 13000)])
+def test_commit_grid_wide_form_bit_exact(layers, heads, dim, n):
+    """Commits the plane-local form does not take: too few planes (one layer, one head,
+    64-dim rows: 16 one-word planes) and more slots than one CTA's staging holds (13 000);
+    both go through the cooperative grid-wide kernel.  Sources and destinations overlap
+    (a shifted chain), so the grid barrier between gather and scatter is exercised."""
+    gen = torch.Generator().manual_seed(21)
+    blocks = (2 * n) // 256 + 2
+    pool = torch.randn((2, layers, blocks, 256, heads, dim), generator=gen).bfloat16()
+    perm = torch.randperm(blocks * 256, generator=gen)
+    src = perm[:n]
+    dst = perm[n // 2:n // 2 + n]  # half of the destinations are also sources
+    expected = raw(pool)
+    kv_oracle.copy_accepted_kv(expected, src.numpy(), dst.numpy(), 256)
+    device_pool = pool.to(DEVICE)
+    jb.copy_accepted_kv(device_pool, src.to(DEVICE), dst.to(DEVICE), 256)
+    assert np.array_equal(raw(device_pool), expected)
+
+
 def test_commit_rejects_bad_slot_maps():
     pool = _pool(1, 2).to(DEVICE)
     with pytest.raises(ValueError, match="one-dimensional"):
