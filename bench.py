@@ -924,23 +924,41 @@ def time_device(step: Step, steps: int, warmup: int, world: int, device):
 
 
 def time_e2e(step: Step, steps: int, warmup: int, world: int, device):
-    """The public API with host buffers: every step copies its inputs (metadata, queries,
-    node K/V) from pinned host memory and reads its attention output back.  Three streams
-    and two input / output buffer sets: step i's upload runs while step i-1 computes and
-    step i-2's output downloads, as a serving loop would pipeline rounds.  Returns the
-    time from the first upload to the last download (events on the compute stream after it
-    joined the copy streams), and the bytes copied per step."""
-    meta = step.meta
-    names = ("cu_seqlens_q", "query_to_request", "query_local_row", "prefix_lens",
-             "block_tables", "tree_slots", "qq_bias", "qq_bias_offsets", "node_counts")
-    host_meta = {n: getattr(meta, n).cpu().pin_memory() for n in names}
+    """The public API with host buffers: every step copies its inputs (the round's compact
+    topology, queries, node K/V) from pinned host memory and reads its attention output
+    back.  The metadata is built on the GPU from the uploaded topology
+    (PackedTreeMetadata.stage_topology / from_staged_topology: node counts, prefix lengths,
+    block tables, parents and scratch pages as one int32 buffer, not the dense bias
+    matrices); when the pool has no free pages for the scratch arena, the dense metadata
+    tensors are uploaded instead.  Three streams and two input / output buffer sets: step
+    i's upload runs while step i-1 computes and step i-2's output downloads, as a serving
+    loop would pipeline rounds.  Returns the time from the first upload to the last download
+    (events on the compute stream after it joined the copy streams), and the bytes copied
+    per step."""
+    from jetspec_b200 import PackedTreeMetadata
+
+    batch, meta = step.batch, step.meta
+    used = {p for t in batch.owned_pages for p in t} | {p for t in batch.block_tables for p in t}
+    used |= {s // BLOCK for slots in batch.tree_slots for s in slots}
+    need = -(-batch.total_queries // BLOCK)
+    arena = [p for p in range(batch.num_blocks) if p not in used][:need]
+    topo = None
+    if len(arena) == need:
+        topo = PackedTreeMetadata.stage_topology(batch.prefix_lens, batch.block_tables,
+                                                 batch.parents, arena, BLOCK)
+        host_meta = {"topology": torch.from_numpy(topo.host).pin_memory()}
+    else:
+        names = ("cu_seqlens_q", "query_to_request", "query_local_row", "prefix_lens",
+                 "block_tables", "tree_slots", "qq_bias", "qq_bias_offsets", "node_counts")
+        host_meta = {n: getattr(meta, n).cpu().pin_memory() for n in names}
     host_q = step.q.cpu().pin_memory()
     host_k, host_v = step.k_nodes.cpu().pin_memory(), step.v_nodes.cpu().pin_memory()
     from dataclasses import replace
     sets = []
     for _ in range(2):
-        dev_meta = replace(meta, **{n: torch.empty_like(getattr(meta, n)) for n in names})
-        sets.append({"meta": dev_meta, "q": torch.empty_like(step.q),
+        staged = {n: torch.empty(t.shape, dtype=t.dtype, device=device)
+                  for n, t in host_meta.items()}
+        sets.append({"staged": staged, "q": torch.empty_like(step.q),
                      "k": torch.empty_like(step.k_nodes), "v": torch.empty_like(step.v_nodes),
                      "uploaded": torch.cuda.Event(), "consumed": torch.cuda.Event(),
                      "computed": torch.cuda.Event(), "downloaded": torch.cuda.Event(),
@@ -958,8 +976,8 @@ def time_e2e(step: Step, steps: int, warmup: int, world: int, device):
         with torch.cuda.stream(up):
             if started[i % 2]:
                 up.wait_event(s["consumed"])      # step i-2 finished reading this set
-            for n in names:
-                getattr(s["meta"], n).copy_(host_meta[n], non_blocking=True)
+            for n, t in host_meta.items():
+                s["staged"][n].copy_(t, non_blocking=True)
             s["q"].copy_(host_q, non_blocking=True)
             s["k"].copy_(host_k, non_blocking=True)
             s["v"].copy_(host_v, non_blocking=True)
@@ -967,8 +985,12 @@ def time_e2e(step: Step, steps: int, warmup: int, world: int, device):
         compute.wait_event(s["uploaded"])
         if started[i % 2]:
             compute.wait_event(s["downloaded"])   # step i-2's output has left the GPU
-        jb.scatter_tree_kv(s["k"], s["v"], step.k_pool, step.v_pool, s["meta"].tree_slots)
-        out = jb.packed_tree_attention_gqa(s["q"], step.k_pool, step.v_pool, s["meta"],
+        if topo is not None:
+            round_meta = PackedTreeMetadata.from_staged_topology(s["staged"]["topology"], topo)
+        else:
+            round_meta = replace(meta, **s["staged"])
+        jb.scatter_tree_kv(s["k"], s["v"], step.k_pool, step.v_pool, round_meta.tree_slots)
+        out = jb.packed_tree_attention_gqa(s["q"], step.k_pool, step.v_pool, round_meta,
                                            step.scale, GROUPS)
         jb.copy_accepted_kv(step.kv_pool, step.src, step.dst, BLOCK)
         s["consumed"].record(compute)
@@ -994,7 +1016,7 @@ def time_e2e(step: Step, steps: int, warmup: int, world: int, device):
     compute.wait_stream(down)
     end.record(compute)
     torch.cuda.synchronize(device)
-    return start.elapsed_time(end), h2d, d2h
+    return start.elapsed_time(end), h2d, d2h, "compact topology" if topo is not None else "dense"
 
 
 def config4_record(rank: int, world: int, device, steps: int, warmup: int) -> dict:
@@ -1135,7 +1157,7 @@ def main():
         total_ms, split, clocks, launch = time_device(step, steps, warmup, world, device)
         if not torch.isfinite(step.out).all():
             raise RuntimeError("non-finite attention output: a poisoned KV row was read")
-        e2e_ms, h2d, d2h = time_e2e(step, steps, warmup, world, device)
+        e2e_ms, h2d, d2h, e2e_meta = time_e2e(step, steps, warmup, world, device)
         ref_gpu = None
         if rank == 0 and not args.no_cpu_baseline:
             ref_gpu = reference_gpu_attention(step, device)
@@ -1188,7 +1210,9 @@ def main():
                 "e2e": {"value": tokens / (e2e_ms / steps * 1e-3), "unit": UNIT,
                         "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                         "pipelining": "uploads / compute / downloads on three streams, "
-                                      "double-buffered"},
+                                      "double-buffered",
+                        "metadata": e2e_meta + " upload, metadata built on the device"
+                                    if e2e_meta != "dense" else "dense tensors uploaded"},
                 "gpu_launches": steps * 4,
                 "clocks": clocks,
             }

@@ -47,6 +47,24 @@ def _bias_rows(mask: np.ndarray) -> np.ndarray:
 
 
 @dataclass(frozen=True)
+class StagedTopology:
+    """Compact round topology for the device metadata build (PackedTreeMetadata
+    .stage_topology): ``host`` is the int32 buffer to upload; the rest is what the host keeps
+    (per-request node counts, prefix lengths, tables, the arena pages, request IDs)."""
+    host: np.ndarray
+    counts: tuple
+    prefixes: tuple
+    tables: tuple
+    pages: tuple
+    ids: tuple
+    width: int
+    block_size: int
+    query_offsets: tuple   # cu_seqlens_q on the host
+    bias_offsets: tuple    # qq_bias_offsets on the host
+    slot_ids: tuple        # node j's scratch slot: the j-th slot of the arena pages
+
+
+@dataclass(frozen=True)
 class PackedTreeMetadata:
     cu_seqlens_q: torch.Tensor
     query_to_request: torch.Tensor
@@ -182,9 +200,22 @@ class PackedTreeMetadata:
         Node j's scratch slot is the j-th slot of the packed arena pages, as in
         from_host_trees.  Host-side checks: tight canonical tables, parents in
         topological order, enough arena pages, no arena page inside a prefix.
-        """
-        from . import _launch, _lib
 
+        The two halves are public for callers that stage the upload themselves (pinned
+        memory, a copy stream): ``stage_topology`` (host checks and the int32 buffer) and
+        ``from_staged_topology`` (the device build from that buffer once it is on the GPU).
+        """
+        topo = cls.stage_topology(prefix_lens, block_tables, parents, arena_blocks, block_size,
+                                  request_ids=request_ids)
+        staged = torch.from_numpy(topo.host).to(torch.device(device))   # the one upload
+        return cls.from_staged_topology(staged, topo)
+
+    @staticmethod
+    def stage_topology(prefix_lens, block_tables, parents, arena_blocks, block_size, *,
+                       request_ids=None) -> "StagedTopology":
+        """Host half of from_parents_device: the checks and the compact int32 buffer
+        (``StagedTopology.host``: node counts, prefix lengths, padded block tables, parents,
+        arena pages)."""
         prefixes = tuple(int(v) for v in prefix_lens)
         tables = tuple(tuple(int(v) for v in table) for table in block_tables)
         parent_arrays = [np.asarray(p, dtype=np.int64).reshape(-1) for p in parents]
@@ -225,8 +256,30 @@ class PackedTreeMetadata:
             padded[row, :len(table)] = table
         host = np.concatenate((np.asarray(counts, dtype=np.int64), np.asarray(prefixes, dtype=np.int64),
                                padded.reshape(-1), flat_parents, np.asarray(pages, dtype=np.int64)))
-        device = torch.device(device)
-        staged = torch.from_numpy(host.astype(np.int32)).to(device)   # the one upload
+        offsets = np.concatenate(([0], np.cumsum(counts))).astype(np.int64)
+        bias_offsets = np.concatenate(([0], np.cumsum(np.asarray(counts, dtype=np.int64) ** 2)))
+        node = np.arange(total, dtype=np.int64)
+        slots = np.asarray(pages, dtype=np.int64)[node // block_size] * block_size + node % block_size
+        return StagedTopology(host=host.astype(np.int32), counts=tuple(counts),
+                              prefixes=prefixes, tables=tables, pages=pages, ids=ids,
+                              width=width, block_size=int(block_size),
+                              query_offsets=tuple(offsets.tolist()),
+                              bias_offsets=tuple(bias_offsets.tolist()),
+                              slot_ids=tuple(slots.tolist()))
+
+    @classmethod
+    def from_staged_topology(cls, staged: torch.Tensor, topo: "StagedTopology"
+                             ) -> "PackedTreeMetadata":
+        """Device half of from_parents_device: ``staged`` is ``topo.host`` on the GPU (int32,
+        contiguous); one jt_metadata_build_launch on the current stream builds the rest."""
+        from . import _launch, _lib
+
+        if (staged.dtype != torch.int32 or staged.ndim != 1 or not staged.is_cuda
+                or staged.numel() != topo.host.size or not staged.is_contiguous()):
+            raise ValueError("staged topology must be the int32 buffer of stage_topology on a GPU")
+        device = staged.device
+        counts, pages, block_size = topo.counts, topo.pages, topo.block_size
+        count, width, total = len(counts), topo.width, sum(counts)
         cursor = 0
 
         def take(n):
@@ -237,11 +290,7 @@ class PackedTreeMetadata:
 
         node_counts, prefix_lens_d = take(count), take(count)
         block_tables_d, parents_d, pages_d = take(count * width), take(total), take(len(pages))
-        bias_offsets = [0]
-        offsets = [0]
-        for c in counts:
-            offsets.append(offsets[-1] + c)
-            bias_offsets.append(bias_offsets[-1] + c * c)
+        bias_offsets = topo.bias_offsets
         out = dict(
             cu_seqlens_q=torch.empty(count + 1, dtype=torch.int32, device=device),
             query_to_request=torch.empty(total, dtype=torch.int32, device=device),
@@ -258,17 +307,14 @@ class PackedTreeMetadata:
         p.num_nodes, p.num_pages = total, len(pages)
         lib = _lib.load_library()
         _lib.check(lib.jt_metadata_build_launch(ctypes.byref(p), _launch.stream_handle(device)))
-        node = np.arange(total, dtype=np.int64)
-        slots = tuple((np.asarray(pages, dtype=np.int64)[node // block_size] * block_size +
-                       node % block_size).tolist())
         return cls(
             cu_seqlens_q=out["cu_seqlens_q"], query_to_request=out["query_to_request"],
             query_local_row=out["query_local_row"], prefix_lens=prefix_lens_d,
             block_tables=block_tables_d.view(count, width), tree_slots=out["tree_slots"],
             qq_bias=out["qq_bias"], qq_bias_offsets=out["qq_bias_offsets"],
-            node_counts=node_counts, block_size=int(block_size), prefix_lengths=prefixes,
-            query_offsets=tuple(offsets), node_counts_host=tuple(counts),
-            block_tables_host=tables, tree_slot_ids=slots, request_ids=ids)
+            node_counts=node_counts, block_size=int(block_size), prefix_lengths=topo.prefixes,
+            query_offsets=topo.query_offsets, node_counts_host=tuple(counts),
+            block_tables_host=topo.tables, tree_slot_ids=topo.slot_ids, request_ids=topo.ids)
 
     @classmethod
     def from_parents(cls, prefix_lens, block_tables, parents, tree_slots, block_size, *,

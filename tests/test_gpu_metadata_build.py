@@ -52,6 +52,29 @@ def test_ragged_batch_every_field():
     assert jb.read_device_errors() == 0
 
 
+def test_staged_topology_through_a_copy_stream():
+    """The two public halves of from_parents_device as a pipelined caller uses them: the
+    int32 topology in pinned memory, copied on a side stream, the device build on the
+    compute stream after it; every field equals the host builder's."""
+    batch = workloads.config3()
+    used = {p for t in batch.block_tables for p in t}
+    need = -(-batch.total_queries // 256)
+    arena = [p for p in range(batch.num_blocks) if p not in used][:need]
+    topo = PackedTreeMetadata.stage_topology(batch.prefix_lens, batch.block_tables,
+                                             batch.parents, arena, 256)
+    pinned = torch.from_numpy(topo.host).pin_memory()
+    staged = torch.empty(pinned.shape, dtype=torch.int32, device=DEV)
+    side = torch.cuda.Stream(DEV)
+    with torch.cuda.stream(side):
+        staged.copy_(pinned, non_blocking=True)
+    torch.cuda.current_stream(DEV).wait_stream(side)
+    dev = PackedTreeMetadata.from_staged_topology(staged, topo)
+    host, _ = _host_and_device(batch.prefix_lens, batch.block_tables, batch.parents, arena, 256)
+    _assert_equal(host, dev)
+    with pytest.raises(ValueError, match="staged topology"):
+        PackedTreeMetadata.from_staged_topology(staged[:-1], topo)
+
+
 def test_largest_tree_and_deep_chain():
     parents = [[-1] + list(range(1023)), [-1] + [0] * 99]  # a 1024-deep chain, a wide star
     host, dev = _host_and_device([300, 5], [[1, 2], [3]], parents, [50 + i for i in range(5)], 256)
