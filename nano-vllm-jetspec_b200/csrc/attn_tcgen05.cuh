@@ -984,11 +984,14 @@ __global__ void __launch_bounds__(kThreads, 1)
         tmem_wait_ld();
         const int col = 64 * c + 32 * chunk;
         if (split_item) {
-          float4* dst = reinterpret_cast<float4*>(w.part_o + (slot * kM + t128) * kD + col);
+          // Column-group-major partials, [slot][32 groups of 4 columns][128 rows]: the 32
+          // lanes of a warp store 512 contiguous bytes per instruction.
+          float4* dst = reinterpret_cast<float4*>(w.part_o) +
+                        (slot * (kD / 4) + col / 4) * kM + t128;
 #pragma unroll
           for (int k = 0; k < 8; ++k)
-            dst[k] = make_float4(__uint_as_float(o[4 * k]), __uint_as_float(o[4 * k + 1]),
-                                 __uint_as_float(o[4 * k + 2]), __uint_as_float(o[4 * k + 3]));
+            dst[k * kM] = make_float4(__uint_as_float(o[4 * k]), __uint_as_float(o[4 * k + 1]),
+                                      __uint_as_float(o[4 * k + 2]), __uint_as_float(o[4 * k + 3]));
         } else if (row_ok) {
           const int64_t off = static_cast<int64_t>(it.q_start + j) * p.out_stride0 +
                               static_cast<int64_t>(it.h * G + g) * p.out_stride1 + col;
@@ -1033,8 +1036,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         // Per-(row, half) merge: each half publishes its 64 columns and its own copy of the
         // row's max (log2 units) and sum, then bumps the (row, half) counter; the arrival
         // that completes it (this half of every split) merges those 64 columns.  Nothing
-        // waits: rows and halves finish independently.  The merge issues each split's
-        // loads together (one load round per split, not one per 4 columns).
+        // waits: rows and halves finish independently.
         w.part_ml[(slot * 2 + c) * kM + t128] = make_float2(m_run, l_fin);
         __threadfence();
         int* counter = w.counters +
@@ -1045,37 +1047,49 @@ __global__ void __launch_bounds__(kThreads, 1)
           *counter = 0;
           __threadfence();
           if (row_ok) {
+            // Online merge over the splits, two splits' loads in flight per round: the
+            // running max moves as new splits arrive and the accumulated columns are
+            // rescaled, so no separate pass over the maxima is needed.
             const int64_t slot0 =
                 it.slot_base + (static_cast<int64_t>(it.h) * it.mblocks + it.tp) * it.n_split;
-            float mmax = -INFINITY;
-            for (int s2 = 0; s2 < it.n_split; ++s2)
-              mmax = fmaxf(mmax, __ldcg(w.part_ml + ((slot0 + s2) * 2 + c) * kM + t128).x);
-            const float mref = mmax == -INFINITY ? 0.f : mmax;
+            const int ns = it.n_split;
             const int64_t off = static_cast<int64_t>(it.q_start + j) * p.out_stride0 +
                                 static_cast<int64_t>(it.h * G + g) * p.out_stride1 + 64 * c;
+            const float4* po = reinterpret_cast<const float4*>(w.part_o);
 #pragma unroll 1
             for (int part = 0; part < 2; ++part) {
+              const int cg0 = 16 * c + 8 * part;  // first 4-column group of this part
               float acc[32];
 #pragma unroll
               for (int k = 0; k < 32; ++k) acc[k] = 0.f;
-              float den = 0.f;
+              float den = 0.f, mrun = -INFINITY;
 #pragma unroll 1
-              for (int s2 = 0; s2 < it.n_split; ++s2) {
-                const float2 ml = __ldcg(w.part_ml + ((slot0 + s2) * 2 + c) * kM + t128);
-                const float4* src = reinterpret_cast<const float4*>(
-                    w.part_o + ((slot0 + s2) * kM + t128) * kD + 64 * c + 32 * part);
-                float4 v[8];
-#pragma unroll
-                for (int k = 0; k < 8; ++k) v[k] = __ldcg(src + k);
-                const float wv = jt::fast_exp2(ml.x - mref);
-                den += wv * ml.y;
+              for (int s2 = 0; s2 < ns; s2 += 2) {
+                const bool two = s2 + 1 < ns;
+                const float2 mla = __ldcg(w.part_ml + ((slot0 + s2) * 2 + c) * kM + t128);
+                const float2 mlb = two ? __ldcg(w.part_ml + ((slot0 + s2 + 1) * 2 + c) * kM + t128)
+                                       : make_float2(-INFINITY, 0.f);
+                float4 va[8], vb[8];
 #pragma unroll
                 for (int k = 0; k < 8; ++k) {
-                  acc[4 * k] += wv * v[k].x;
-                  acc[4 * k + 1] += wv * v[k].y;
-                  acc[4 * k + 2] += wv * v[k].z;
-                  acc[4 * k + 3] += wv * v[k].w;
+                  va[k] = __ldcg(po + ((slot0 + s2) * (kD / 4) + cg0 + k) * kM + t128);
+                  vb[k] = two ? __ldcg(po + ((slot0 + s2 + 1) * (kD / 4) + cg0 + k) * kM + t128)
+                              : make_float4(0.f, 0.f, 0.f, 0.f);
                 }
+                const float mnew = fmaxf(mrun, fmaxf(mla.x, mlb.x));
+                const float mref = mnew == -INFINITY ? 0.f : mnew;
+                const float sc = mrun == -INFINITY ? 0.f : jt::fast_exp2(mrun - mref);
+                const float wa = jt::fast_exp2(mla.x - mref);
+                const float wb = two ? jt::fast_exp2(mlb.x - mref) : 0.f;
+                den = den * sc + wa * mla.y + wb * mlb.y;
+#pragma unroll
+                for (int k = 0; k < 8; ++k) {
+                  acc[4 * k] = acc[4 * k] * sc + wa * va[k].x + wb * vb[k].x;
+                  acc[4 * k + 1] = acc[4 * k + 1] * sc + wa * va[k].y + wb * vb[k].y;
+                  acc[4 * k + 2] = acc[4 * k + 2] * sc + wa * va[k].z + wb * vb[k].z;
+                  acc[4 * k + 3] = acc[4 * k + 3] * sc + wa * va[k].w + wb * vb[k].w;
+                }
+                mrun = mnew;
               }
               const float dinv = 1.f / den;
               if (p.out_dtype == JT_F32) {
