@@ -177,7 +177,7 @@ __global__ void __launch_bounds__(kPlanThreads)
     return;
   }
 
-  __shared__ int cand_red[kPlanThreads / 32][3][kSplitCandidates];
+  __shared__ int cand_red[kPlanThreads / 32][4][kSplitCandidates];
   __shared__ int64_t cand_est[kSplitCandidates];
   __shared__ int cand_ok[kSplitCandidates];
   __shared__ int bucket_count[kBuckets];
@@ -202,7 +202,7 @@ __global__ void __launch_bounds__(kPlanThreads)
     const int len = kSplitBase << c;
     // Reduced in 32 bits: each thread's terms are clamped to 2^24, so a warp's sum stays
     // below 2^29 and a clamped slot count still exceeds any partial budget.
-    unsigned c_slots = 0, c_work = 0, c_long = 0;
+    unsigned c_slots = 0, c_work = 0, c_long = 0, c_full = 0;
     for (int r = tid; r < R; r += kPlanThreads) {
       const int nodes = r == r0 ? nodes0 : p.node_counts[r];
       const int prefix = r == r0 ? prefix0 : p.prefix_lens[r];
@@ -214,36 +214,46 @@ __global__ void __launch_bounds__(kPlanThreads)
       const int64_t work = static_cast<int64_t>(mb) * H * (tiles + ns * kItemCostTiles);
       c_work = static_cast<unsigned>(min(static_cast<int64_t>(c_work) + work, static_cast<int64_t>(1) << 24));
       c_long = max(c_long, static_cast<unsigned>(max(ns > 1 ? len / 128 : 0, (last_keys + 127) / 128)));
-      if (ns > 1)
+      if (ns > 1) {
         c_slots = static_cast<unsigned>(
             min(static_cast<int64_t>(c_slots) + static_cast<int64_t>(ns) * mb * H,
                 static_cast<int64_t>(1) << 24));
+        c_full = static_cast<unsigned>(
+            min(static_cast<int64_t>(c_full) + static_cast<int64_t>(ns - 1) * mb * H,
+                static_cast<int64_t>(1) << 24));
+      }
     }
     c_slots = __reduce_add_sync(0xffffffffu, min(c_slots, 1u << 24));
     c_work = min(c_work, 1u << 24);
     c_work = __reduce_add_sync(0xffffffffu, c_work);
     c_long = __reduce_max_sync(0xffffffffu, c_long);
+    c_full = __reduce_add_sync(0xffffffffu, min(c_full, 1u << 24));
     if (lane == 0) {
       cand_red[warp][0][c] = static_cast<int>(c_slots);
       cand_red[warp][1][c] = static_cast<int>(c_work);
       cand_red[warp][2][c] = static_cast<int>(c_long);
+      cand_red[warp][3][c] = static_cast<int>(c_full);
     }
   }
   if (tid < kBuckets) bucket_count[tid] = 0;
   __syncthreads();
   if (tid < kSplitCandidates) {
-    // Candidate `tid`: partial slots, and the estimated makespan in tile times (longest-
-    // first list scheduling finishes within max(average load, longest item)) plus the
-    // fixed cost of a split plan.
-    int64_t sl = 0, wk = 0, lg = 0;
+    // Candidate `tid`: partial slots, and the estimated makespan in tile times: longest-
+    // first list scheduling finishes within max(average load, longest item), and no
+    // sooner than the waves its full-length split items take on their own (items of one
+    // length fill the CTAs wave by wave); plus the fixed cost of a split plan.
+    int64_t sl = 0, wk = 0, lg = 0, fl = 0;
 #pragma unroll
     for (int k = 0; k < kPlanThreads / 32; ++k) {
       sl += cand_red[k][0][tid];
       wk += cand_red[k][1][tid];
       lg = max(lg, static_cast<int64_t>(cand_red[k][2][tid]));
+      fl += cand_red[k][3][tid];
     }
+    const int64_t full_len = (kSplitBase << tid) / 128 + kItemCostTiles;
     cand_ok[tid] = sl <= w.max_slots;
-    cand_est[tid] = max((wk + num_ctas - 1) / num_ctas, lg + kItemCostTiles) +
+    cand_est[tid] = max(max((wk + num_ctas - 1) / num_ctas, lg + kItemCostTiles),
+                        (fl + num_ctas - 1) / num_ctas * full_len) +
                     (sl > 0 ? kMergeCostTiles : 0);
   }
   __syncthreads();
