@@ -54,7 +54,8 @@ def parse():
     parser.add_argument("--steps", type=int, default=200)
     parser.add_argument("--warmup", type=int, default=10)
     parser.add_argument("--impl", choices=("ours", "reference", "reference-triton", "accept-walk",
-                                           "metadata-build", "row-linear", "verify-step"),
+                                           "metadata-build", "row-linear", "verify-step",
+                                           "split-sweep"),
                         default="ours",
                         help="reference-triton: the reference's own Triton kernels (installed "
                              "under baseline/_ref) beside ours on configs 1-4, one GPU; "
@@ -454,6 +455,57 @@ def run_accept_walk(args, rank: int):
         line["reference_accept_batch_ms"] = timed_wall(
             lambda: ref_accept(logits, trees, offsets, max_depth))
     print(json.dumps(line), flush=True)
+
+
+# ---- split-KV sweep ------------------------------------------------------------------------
+def run_split_sweep(args, rank: int):
+    """The attention launch (plan + kernel) with the plan's own split choice and with forced
+    split lengths, on configs 2-4 and on config 4's per-GPU shapes at 4 / 2 / 1 KV heads:
+    CUDA events around each launch, a 256 MB L2 flush before it, medians.  One GPU."""
+    if rank != 0:
+        return
+    from jetspec_b200.tree_gqa import launch_tree_attention
+    device = torch.device("cuda", 0)
+    torch.cuda.set_device(device)
+    steps = max(args.steps, 5)
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=device)
+    shapes = [("config2", workloads.config2()), ("config3", workloads.config3()),
+              ("config4", workloads.config4())]
+    shapes += [(f"config4 {h} KV heads", workloads.config4(num_kv_heads=h)) for h in (4, 2, 1)]
+    results = []
+    for name, batch in shapes:
+        meta = batch.metadata(device)
+        q, k, v = workloads.make_tensors(batch, device, poison=False, generator_device="cuda")
+        out = torch.empty_like(q)
+        splits = (0, 1024, 2048, 4096, 8192, 16384)
+
+        def call(split):
+            launch_tree_attention(out, q, k, v, meta, HEAD_DIM ** -0.5, GROUPS,
+                                  split_keys=split)
+        for split in splits:
+            for _ in range(3):
+                call(split)
+        # Round-robin over the split lengths, so clock or thermal drift during the sweep
+        # spreads over all of them.
+        times = {split: [] for split in splits}
+        for _ in range(steps):
+            for split in splits:
+                flush.zero_()
+                s0, s1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                s0.record()
+                call(split)
+                s1.record()
+                torch.cuda.synchronize(device)
+                times[split].append(s0.elapsed_time(s1))
+        row = {"workload": name}
+        for split in splits:
+            row["auto" if split == 0 else str(split)] = statistics.median(times[split])
+        results.append(row)
+        del q, k, v, out, meta
+        torch.cuda.empty_cache()
+    print(json.dumps({"impl": "split-sweep", "unit": "ms per launch (plan + attention)",
+                      "steps": steps, "l2": "256 MB flush before every launch",
+                      "results": results}), flush=True)
 
 
 # ---- metadata build for a verification round ---------------------------------------------
@@ -1136,6 +1188,8 @@ def main():
         return run_reference_triton(args, rank)
     if args.impl == "accept-walk":
         return run_accept_walk(args, rank)
+    if args.impl == "split-sweep":
+        return run_split_sweep(args, rank)
     if args.impl == "metadata-build":
         return run_metadata_build(args, rank)
     if args.impl == "row-linear":
