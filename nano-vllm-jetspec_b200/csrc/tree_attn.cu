@@ -37,7 +37,8 @@ constexpr int kTileKeys = 64;     // keys per KV tile
 constexpr int kStages = 3;        // cp.async ring depth
 constexpr int kMaxMaskWords = 32; // tree nodes per request <= 1024
 constexpr int kPlanThreads = 256;
-constexpr int kBuckets = 32;
+constexpr int kBuckets = 256;  // item-order buckets: 8 per octave of key counts
+static_assert(kBuckets == kPlanThreads, "one bucket per plan thread in the bucket scan");
 constexpr int kSplitCandidates = 16;  // split lengths 1024 << c
 constexpr int kSplitBase = 1024;
 // Planning costs in 128-key tile times, measured: the fixed cost of one work item (query
@@ -142,6 +143,15 @@ DevLayout device_layout(const Layout& L, void* ws) {
 // ---- plan kernel --------------------------------------------------------------------
 __device__ __forceinline__ int request_mblocks(int nodes, int groups, int bm) {
   return static_cast<int>((static_cast<int64_t>(nodes) * groups + bm - 1) / bm);
+}
+
+// Bucket of an item with `keys` keys in the longest-first order: the octave
+// floor(log2(keys)) and the next three bits below it (exact below 8 keys), so items within
+// 12.5 % of each other share a bucket.
+__device__ __forceinline__ int key_bucket(int keys) {
+  keys = max(keys, 1);
+  const int e = 31 - __clz(keys);
+  return e < 3 ? e * 8 : e * 8 + ((keys >> (e - 3)) & 7);
 }
 
 __device__ __forceinline__ int request_splits(int prefix, int split_keys) {
@@ -317,25 +327,39 @@ __global__ void __launch_bounds__(kPlanThreads)
   for (int64_t i = tid; i < static_cast<int64_t>(s_carry[1]) * w.counter_stride; i += kPlanThreads)
     w.counters[i] = 0;
 
-  // Longest-first item order: bucket units (request, split) by floor(log2(keys)).
+  // Longest-first item order: bucket units (request, split) by key_bucket(keys).
   for (int r = tid; r < R; r += kPlanThreads) {
     const int4 info = w.req[r];
     if (info.x == 0) continue;
     const int prefix = p.prefix_lens[r], nodes = p.node_counts[r];
     for (int s = 0; s < info.x; ++s) {
       const int keys = (s + 1 < info.x) ? split : prefix + nodes - s * split;
-      const int bkt = 31 - __clz(max(keys, 1));
-      atomicAdd(&bucket_count[bkt], info.w * H);
+      atomicAdd(&bucket_count[key_bucket(keys)], info.w * H);
     }
   }
   __syncthreads();
-  if (tid == 0) {
-    int run = 0;
-    for (int b = kBuckets - 1; b >= 0; --b) { bucket_start[b] = run; run += bucket_count[b]; }
-    w.header[1] = run <= w.max_items ? run : 0;
-    if (run > w.max_items) atomicOr(&g_attn_errors, JT_DEVERR_OUT_OF_RANGE);
-    w.header[0] = 0;
-    w.header[2] = split;
+  {
+    // Bucket starts in descending bucket order: an exclusive scan with thread t on
+    // bucket kBuckets-1-t (warp shuffles, then the warp totals).
+    const int b = kBuckets - 1 - tid;
+    const int cnt = bucket_count[b];
+    int x = cnt;
+    for (int o = 1; o < 32; o <<= 1) {
+      const int y = __shfl_up_sync(0xffffffffu, x, o);
+      if (lane >= o) x += y;
+    }
+    if (lane == 31) warp_tot[0][warp] = x;
+    __syncthreads();
+    int base = 0;
+    for (int k = 0; k < warp; ++k) base += warp_tot[0][k];
+    bucket_start[b] = base + x - cnt;
+    if (tid == kPlanThreads - 1) {
+      const int run = base + x;
+      w.header[1] = run <= w.max_items ? run : 0;
+      if (run > w.max_items) atomicOr(&g_attn_errors, JT_DEVERR_OUT_OF_RANGE);
+      w.header[0] = 0;
+      w.header[2] = split;
+    }
   }
   __syncthreads();
   for (int r = tid; r < R; r += kPlanThreads) {
@@ -344,8 +368,7 @@ __global__ void __launch_bounds__(kPlanThreads)
     const int prefix = p.prefix_lens[r], nodes = p.node_counts[r];
     for (int s = 0; s < info.x; ++s) {
       const int keys = (s + 1 < info.x) ? split : prefix + nodes - s * split;
-      const int bkt = 31 - __clz(max(keys, 1));
-      const int pos = atomicAdd(&bucket_start[bkt], info.w * H);
+      const int pos = atomicAdd(&bucket_start[key_bucket(keys)], info.w * H);
       if (pos + info.w * H > w.max_items) continue;
       for (int h = 0; h < H; ++h)
         for (int m = 0; m < info.w; ++m) w.items[pos + h * info.w + m] = make_int4(r, s, h, m);
