@@ -178,7 +178,10 @@ __global__ void __launch_bounds__(kPlanThreads)
       return;
     }
     const float* bias = p.qq_bias + p.qq_bias_offsets[r] + static_cast<int64_t>(j) * nodes;
-    for (int word = 0; word < w.mask_words; ++word) {
+    // Only the words that hold this tree's nodes: the attention kernels never read a word
+    // at or past ceil(nodes / 32) (a key past the request's last node is out of range).
+    const int words = (nodes + 31) / 32;
+    for (int word = 0; word < words; ++word) {
       const int n = word * 32 + lane;
       const bool visible = n < nodes && n <= j && bias[n] == 0.0f;
       const uint32_t bits = __ballot_sync(0xffffffffu, visible);
