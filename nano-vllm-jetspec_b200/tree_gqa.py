@@ -14,6 +14,8 @@ from . import _launch, _lib
 
 SUPPORTED_HEAD_DIMS = (64, 128)
 MAX_TREE_NODES = 1024
+# jt_tree_attn_workspace_size is a pure function of the launch shape.
+_WORKSPACE_SIZES: dict = {}
 
 
 def _validate(q, k, v, metadata, groups, output_dtype):
@@ -104,11 +106,15 @@ def launch_tree_attention_eager(out, q, k_pool, v_pool, metadata, scale, groups,
     kv_heads = int(k_pool.shape[2])
     head_dim = int(q.shape[-1])
     scratch = None
+    stream = _launch.raw_stream(device)
     if q.dtype != torch.float32:
-        size = ctypes.c_size_t(0)
-        _lib.check(lib.jt_tree_attn_workspace_size(num_requests, total, kv_heads, int(groups),
-                                                   head_dim, ctypes.byref(size)))
-        scratch = _launch.workspace(device, size.value)
+        shape = (num_requests, total, kv_heads, int(groups), head_dim)
+        nbytes = _WORKSPACE_SIZES.get(shape)
+        if nbytes is None:
+            size = ctypes.c_size_t(0)
+            _lib.check(lib.jt_tree_attn_workspace_size(*shape, ctypes.byref(size)))
+            nbytes = _WORKSPACE_SIZES.setdefault(shape, int(size.value))
+        scratch = _launch.workspace(device, nbytes, stream)
     p = _lib.JtTreeAttnParams()
     p.out, p.q, p.k_pool, p.v_pool = out.data_ptr(), q.data_ptr(), k_pool.data_ptr(), v_pool.data_ptr()
     p.cu_seqlens_q = metadata.cu_seqlens_q.data_ptr()
@@ -138,7 +144,7 @@ def launch_tree_attention_eager(out, q, k_pool, v_pool, metadata, scale, groups,
     p.split_keys = int(split_keys)
     p.workspace = None if scratch is None else scratch.data_ptr()
     p.workspace_bytes = 0 if scratch is None else scratch.numel()
-    _lib.check(lib.jt_tree_attn_launch(ctypes.byref(p), _launch.stream_handle(device)))
+    _lib.check(lib.jt_tree_attn_launch(ctypes.byref(p), ctypes.c_void_p(stream)))
     return out
 
 
