@@ -24,6 +24,7 @@
 #include <cudaTypedefs.h>
 
 #include <algorithm>
+#include <atomic>
 #include <mutex>
 #include <type_traits>
 
@@ -873,10 +874,16 @@ bool tcgen05_eligible(const JtTreeAttnParams& p) {
   if (p.groups > tc::kM || tc::kM % p.groups != 0) return false;
   if ((p.out_stride0 | p.out_stride1) % 8 != 0) return false;
   if ((p.q_stride0 | p.q_stride1) % 8 != 0 || !al16(p.q)) return false;
-  int dev = 0, major = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess) return false;
-  if (cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev) != cudaSuccess)
-    return false;
+  // Compute-capability major per device, queried once (0: not queried yet).
+  static std::atomic<int> cc_major[64];
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return false;
+  int major = cc_major[dev].load(std::memory_order_relaxed);
+  if (major == 0) {
+    if (cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev) != cudaSuccess)
+      return false;
+    cc_major[dev].store(major, std::memory_order_relaxed);
+  }
   return major == 10 && tensor_map_encoder() != nullptr;
 }
 
